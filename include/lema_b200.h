@@ -1,0 +1,206 @@
+/*
+ * lema_b200.h — C ABI of the B200 (sm_100a) W8A8 streamed-layer hot path.
+ *
+ * Every entry point takes plain pointers, sizes and leading dimensions (in
+ * elements), plus a CUDA stream handle passed as `void*` (a `cudaStream_t`;
+ * NULL means the legacy default stream). No torch types cross this boundary.
+ *
+ * Status convention: 0 = success; a nonzero `lema_status` otherwise, with a
+ * human-readable message in `lema_last_error()` (thread-local). Nothing
+ * aborts or traps. Device-side failures (a bounded wait that ran out) are
+ * recorded in a per-device error word read by `lema_device_error()`.
+ *
+ * Arithmetic contract (the W8A8 operator; the reference has no quantised
+ * linear, so this library defines it and the CPU oracle restates it):
+ *   quantise rows:  amax[r] = max_k |x[r,k]| (fp32, exact from bf16)
+ *                   s[r]    = amax[r] / 127 (IEEE fp32 division), 1 if amax == 0
+ *                   q[r,k]  = clamp(rint_half_even(x[r,k] / s[r]), -127, 127)
+ *   int8 GEMM:      acc[m,n] = sum_k xq[m,k] * wq[n,k]   (exact s32)
+ *   epilogue:       y[m,n] = bf16_rne((float(acc) * sx[m]) * sw[n] + bias[n])
+ *                   (fp32, in this order, no fused multiply-add)
+ *   dgrad (STE):    wdeq[n,k] = bf16_rne(float(wq[n,k]) * sw[n])
+ *                   dx[m,k]   = bf16_rne(sum_n dy[m,n] * wdeq[n,k])  (fp32 acc)
+ */
+#ifndef LEMA_B200_H
+#define LEMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LEMA_API __attribute__((visibility("default")))
+#else
+#define LEMA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum lema_status {
+  LEMA_OK = 0,
+  LEMA_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride */
+  LEMA_ERR_MISALIGNED = 2,       /* pointer or leading dimension breaks a TMA/vector rule */
+  LEMA_ERR_UNSUPPORTED = 3,      /* shape outside what the kernels implement */
+  LEMA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+  LEMA_ERR_NOT_REGISTERED = 5,   /* memory manager: unknown buffer / slot id */
+  LEMA_ERR_OVERFLOW = 6,         /* memory manager: pack larger than the buffer */
+  LEMA_ERR_TIMEOUT = 7,          /* a bounded wait ran out */
+  LEMA_ERR_DEVICE = 8            /* a kernel recorded a device-side failure */
+} lema_status;
+
+/* ---- errors / introspection ------------------------------------------- */
+
+/* Message of the last failing call on this thread ("" if none). */
+LEMA_API const char* lema_last_error(void);
+
+/* Library version string, e.g. "lema_b200 0.1.0 sm_100a". */
+LEMA_API const char* lema_version(void);
+
+/* Synchronises the current device, then reads and clears its device-side
+ * error word (0 = no kernel recorded a failure). */
+LEMA_API int lema_device_error(int32_t* code_out);
+
+/* Number of SMs the kernels size their persistent grids for (current device). */
+LEMA_API int lema_num_sms(int32_t* out);
+
+/* ---- K1: per-row dynamic symmetric int8 quantisation ------------------- */
+/* Replaces the activation side of the F.linear call inside the nn.Linear
+ * projections that adapters/_llama.py:245-250 runs (wrapped by
+ * _lora.py:23-26). rows x cols bf16 (row stride ldx) -> int8 (row stride ldq)
+ * plus one fp32 scale per row. Per-token for activations (rows = tokens),
+ * per-output-channel for weights (rows = out_features of an nn.Linear weight
+ * [N,K]). Requires 16-byte aligned rows when cols >= 8 (ldx % 8 == 0, ldq % 16 == 0
+ * and aligned base pointers); smaller or ragged rows take a scalar path. */
+LEMA_API int lema_quantize_rows(const void* x_bf16, int64_t rows, int64_t cols, int64_t ldx,
+                       int8_t* q, int64_t ldq, float* scale, void* stream);
+
+/* The same rule applied to fp32 rows (the true weights of a trainable
+ * projection, re-quantised after each optimizer step). */
+LEMA_API int lema_quantize_rows_f32(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                           int8_t* q, int64_t ldq, float* scale, void* stream);
+
+/* Per-token activation quantisation (alias of lema_quantize_rows). */
+LEMA_API int lema_quantize_per_token(const void* x_bf16, int64_t M, int64_t K, int64_t ldx,
+                            int8_t* xq, int64_t ldq, float* sx, void* stream);
+
+/* ---- K2+K3: int8 tcgen05 GEMM with fused dequant/bias/bf16 epilogue ----- */
+/* y[M,N] (bf16, row stride ldy) from xq[M,K] (ld ldx), wq[N,K] (ld ldw),
+ * sx[M], sw[N], bias[N] (bf16, may be NULL = zero). acc_dbg (may be NULL)
+ * receives the raw s32 accumulators [M,N] (row stride ldacc) for bit-exact
+ * checks; y may be NULL when only acc_dbg is wanted.
+ * Constraints: ldx % 16 == 0, ldw % 16 == 0, xq/wq 16-byte aligned,
+ * K >= 0 (K == 0 gives y = bias). */
+LEMA_API int lema_w8a8_gemm(const int8_t* xq, int64_t ldx, const float* sx,
+                   const int8_t* wq, int64_t ldw, const float* sw,
+                   const void* bias_bf16, void* y_bf16, int64_t ldy,
+                   int32_t* acc_dbg, int64_t ldacc,
+                   int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Forward of one W8A8 linear: K1 on x then K2+K3. xq_ws [M, ldq] int8 and
+ * sx_ws [M] fp32 are caller-provided workspaces (they hold the quantised
+ * activations afterwards). Replaces nn.Linear.forward at the A0 call sites. */
+LEMA_API int lema_w8a8_linear_fwd(const void* x_bf16, int64_t ldx,
+                         const int8_t* wq, int64_t ldw, const float* sw,
+                         const void* bias_bf16, void* y_bf16, int64_t ldy,
+                         int8_t* xq_ws, int64_t ldq, float* sx_ws,
+                         int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- K4: backward of the frozen base (straight-through estimator) ------- */
+/* wdT[K,N] (bf16, row stride ldt) = bf16_rne(float(wq[n,k]) * sw[n]),
+ * transposed so the dgrad GEMM reads it K-major. */
+LEMA_API int lema_dequant_transpose(const int8_t* wq, int64_t ldw, const float* sw,
+                           int64_t N, int64_t K, void* wdT_bf16, int64_t ldt,
+                           void* stream);
+
+/* y[M,N] = bf16_rne(a[M,K] . b[N,K]^T), bf16 operands, fp32 accumulation in
+ * TMEM (tcgen05 kind::f16). lda % 8 == 0, ldb % 8 == 0, 16-byte aligned. */
+LEMA_API int lema_bf16_gemm_tn(const void* a_bf16, int64_t lda, const void* b_bf16, int64_t ldb,
+                      void* y_bf16, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                      void* stream);
+
+/* dx[M,K] = dy[M,N] . wdeq[N,K]. wdT_ws is a caller-provided bf16 workspace
+ * of at least K * ldt elements, ldt = N rounded up to a multiple of 8.
+ * Replaces the autograd dgrad of F.linear reached from _trainer.py:161,166. */
+LEMA_API int lema_w8a8_dgrad(const void* dy_bf16, int64_t lddy,
+                    const int8_t* wq, int64_t ldw, const float* sw,
+                    void* dx_bf16, int64_t lddx, void* wdT_ws, int64_t ldt,
+                    int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- K6: grouped W8A8 GEMM (MoE experts) -------------------------------- */
+/* Tokens are pre-sorted by expert: rows [offsets[e], offsets[e+1]) of xq/sx/y
+ * belong to expert e, whose weights are wq + e*N*ldw, sw + e*N and
+ * bias + e*N (bias may be NULL). offsets is a HOST array of E+1 entries.
+ * Replaces the per-expert matmuls of the grouped_mm experts implementation
+ * selected at adapters/_mixtral.py:21-22 and run at :266-268. */
+LEMA_API int lema_grouped_w8a8_gemm(const int8_t* xq, int64_t ldx, const float* sx,
+                           const int8_t* wq, int64_t ldw, const float* sw,
+                           const void* bias_bf16, void* y_bf16, int64_t ldy,
+                           const int64_t* offsets_host, int32_t E,
+                           int64_t N, int64_t K, void* stream);
+
+/* ---- K5: boundary-activation checkpoint offload -------------------------- */
+/* Copies `bytes` from device memory `src` into pinned host memory `dst`
+ * (allocated with cudaHostAlloc / torch pin_memory) on `copy_stream`, after
+ * `after_event` (may be NULL) has completed; records `done_event` (may be
+ * NULL) on copy_stream when the copy is issued. mode 0 = copy engine
+ * (cudaMemcpyAsync), mode 1 = SM kernel storing through the mapped host
+ * pointer with 16-byte stores. Replaces the VRAM-resident
+ * boundary_activations list of _trainer.py:109-111. */
+LEMA_API int lema_ckpt_save(const void* src, void* pinned_dst, size_t bytes, int32_t mode,
+                   void* copy_stream, void* after_event, void* done_event);
+
+/* Host pinned -> device restore of a saved boundary activation
+ * (_trainer.py:146-148), same event protocol, copy engine only. */
+LEMA_API int lema_ckpt_restore(const void* pinned_src, void* dst, size_t bytes,
+                      void* copy_stream, void* after_event, void* done_event);
+
+/* ---- Native memory manager (drop-in for _csrc/memory_manager.{h,cpp}) ---- */
+/* Mirrors LemaMemoryManager (memory_manager.h:25-92, pybind names at
+ * memory_manager.cpp:204-217): RAM buffers and VRAM slots are registered by
+ * pointer + byte size (the caller keeps ownership), transfers run on one
+ * H2D copy stream with a ring of events, prefetch jobs run on 2 worker
+ * threads. Errors return a status instead of throwing. */
+typedef struct lema_mm lema_mm;
+typedef void (*lema_job_fn)(void* user);
+
+LEMA_API int lema_mm_create(int64_t num_layers_hint, int64_t max_layer_size, int32_t device,
+                   lema_mm** out);
+LEMA_API int lema_mm_destroy(lema_mm* mm);
+LEMA_API int lema_mm_register_ram_buffer(lema_mm* mm, int64_t layer_id, void* host_ptr, size_t bytes);
+LEMA_API int lema_mm_register_vram_slot(lema_mm* mm, int64_t slot, void* dev_ptr, size_t bytes);
+/* Packs n host tensors (pointer + bytes) back to back into RAM buffer layer_id. */
+LEMA_API int lema_mm_pack_layer_to_ram(lema_mm* mm, int64_t layer_id, const void* const* srcs,
+                              const size_t* sizes, int64_t n);
+/* Same, but each tensor starts on a multiple of `align` bytes (int8 segments). */
+LEMA_API int lema_mm_pack_layer_to_ram_aligned(lema_mm* mm, int64_t layer_id, const void* const* srcs,
+                                      const size_t* sizes, int64_t n, size_t align,
+                                      size_t* offsets_out);
+/* H2D of the whole registered RAM buffer (or its first `bytes`, 0 = all) into
+ * a VRAM slot; returns an event id. The copy stream first waits for the
+ * slot's "free" event so a slot is never overwritten while compute still
+ * reads it. */
+LEMA_API int lema_mm_async_transfer_to_vram(lema_mm* mm, int64_t layer_id, int64_t vram_slot,
+                                   size_t bytes, int64_t* event_id_out);
+/* Makes `stream` wait (on the device, no host block) for a transfer event. */
+LEMA_API int lema_mm_stream_wait_transfer(lema_mm* mm, int64_t event_id, void* stream);
+/* Records on `stream` that compute is done reading `vram_slot`. */
+LEMA_API int lema_mm_release_vram_slot(lema_mm* mm, int64_t vram_slot, void* stream);
+LEMA_API int lema_mm_wait_vram_transfer(lema_mm* mm, int64_t event_id);
+/* Bounded variant: LEMA_ERR_TIMEOUT after timeout_ms. */
+LEMA_API int lema_mm_wait_vram_transfer_timeout(lema_mm* mm, int64_t event_id, int64_t timeout_ms);
+LEMA_API int lema_mm_is_transfer_complete(lema_mm* mm, int64_t event_id, int32_t* done_out);
+LEMA_API int lema_mm_synchronize_all(lema_mm* mm);
+LEMA_API int lema_mm_submit_prefetch_job(lema_mm* mm, lema_job_fn fn, void* user, int64_t* job_id_out);
+LEMA_API int lema_mm_is_prefetch_complete(lema_mm* mm, int64_t job_id, int32_t* done_out);
+LEMA_API int lema_mm_wait_for_prefetch(lema_mm* mm, int64_t job_id);
+LEMA_API int lema_mm_wait_for_prefetch_timeout(lema_mm* mm, int64_t job_id, int64_t timeout_ms);
+LEMA_API int lema_mm_is_layer_in_ram(lema_mm* mm, int64_t layer_id, int32_t* out);
+/* The manager's H2D copy stream (a cudaStream_t). */
+LEMA_API int lema_mm_copy_stream(lema_mm* mm, void** stream_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEMA_B200_H */

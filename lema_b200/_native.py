@@ -1,0 +1,134 @@
+"""ctypes binding of ``liblema_b200.so`` (the C ABI declared in include/lema_b200.h).
+
+The library is built in-tree (``python -m lema_b200.build``). There is no
+fallback: if the library is missing or a call fails, a ``LemaError`` is
+raised with the library's own message.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "liblema_b200.so"
+
+_lib = None
+_lock = threading.Lock()
+
+i64 = C.c_int64
+i32 = C.c_int32
+vp = C.c_void_p
+sz = C.c_size_t
+
+JOB_FN = C.CFUNCTYPE(None, vp)
+
+# name -> argument types (all return int status unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "lema_last_error": [],
+    "lema_version": [],
+    "lema_device_error": [C.POINTER(i32)],
+    "lema_num_sms": [C.POINTER(i32)],
+    "lema_quantize_rows": [vp, i64, i64, i64, vp, i64, vp, vp],
+    "lema_quantize_rows_f32": [vp, i64, i64, i64, vp, i64, vp, vp],
+    "lema_quantize_per_token": [vp, i64, i64, i64, vp, i64, vp, vp],
+    "lema_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i64, i64, i64, i64, vp],
+    "lema_w8a8_linear_fwd": [vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, i64, i64, i64, vp],
+    "lema_dequant_transpose": [vp, i64, vp, i64, i64, vp, i64, vp],
+    "lema_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp],
+    "lema_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i64, i64, vp],
+    "lema_grouped_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i32, i64, i64, vp],
+    "lema_ckpt_save": [vp, vp, sz, i32, vp, vp, vp],
+    "lema_ckpt_restore": [vp, vp, sz, vp, vp, vp],
+    "lema_mm_create": [i64, i64, i32, C.POINTER(vp)],
+    "lema_mm_destroy": [vp],
+    "lema_mm_register_ram_buffer": [vp, i64, vp, sz],
+    "lema_mm_register_vram_slot": [vp, i64, vp, sz],
+    "lema_mm_pack_layer_to_ram": [vp, i64, C.POINTER(vp), C.POINTER(sz), i64],
+    "lema_mm_pack_layer_to_ram_aligned": [vp, i64, C.POINTER(vp), C.POINTER(sz), i64, sz,
+                                          C.POINTER(sz)],
+    "lema_mm_async_transfer_to_vram": [vp, i64, i64, sz, C.POINTER(i64)],
+    "lema_mm_stream_wait_transfer": [vp, i64, vp],
+    "lema_mm_release_vram_slot": [vp, i64, vp],
+    "lema_mm_wait_vram_transfer": [vp, i64],
+    "lema_mm_wait_vram_transfer_timeout": [vp, i64, i64],
+    "lema_mm_is_transfer_complete": [vp, i64, C.POINTER(i32)],
+    "lema_mm_synchronize_all": [vp],
+    "lema_mm_submit_prefetch_job": [vp, JOB_FN, vp, C.POINTER(i64)],
+    "lema_mm_is_prefetch_complete": [vp, i64, C.POINTER(i32)],
+    "lema_mm_wait_for_prefetch": [vp, i64],
+    "lema_mm_wait_for_prefetch_timeout": [vp, i64, i64],
+    "lema_mm_is_layer_in_ram": [vp, i64, C.POINTER(i32)],
+    "lema_mm_copy_stream": [vp, C.POINTER(vp)],
+}
+_RESTYPES = {"lema_last_error": C.c_char_p, "lema_version": C.c_char_p}
+
+# Status codes (enum lema_status).
+LEMA_OK = 0
+LEMA_ERR_INVALID_ARGUMENT = 1
+LEMA_ERR_MISALIGNED = 2
+LEMA_ERR_UNSUPPORTED = 3
+LEMA_ERR_CUDA = 4
+LEMA_ERR_NOT_REGISTERED = 5
+LEMA_ERR_OVERFLOW = 6
+LEMA_ERR_TIMEOUT = 7
+LEMA_ERR_DEVICE = 8
+
+
+class LemaError(RuntimeError):
+    """A C-ABI call returned a nonzero status."""
+
+    def __init__(self, code: int, message: str, call: str = ""):
+        self.code = code
+        super().__init__(f"{call}: [{code}] {message}" if call else f"[{code}] {message}")
+
+
+def lib() -> C.CDLL:
+    """Loads the native library once; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"lema_b200 native library not found at {LIB_PATH}; "
+                    "build it with `python -m lema_b200.build` (needs nvcc)")
+            handle = C.CDLL(str(LIB_PATH))
+            for name, args in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPES.get(name, C.c_int)
+            _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().lema_last_error().decode()
+
+
+def call(name: str, *args) -> None:
+    """Invokes a status-returning entry point and raises LemaError on failure."""
+    rc = getattr(lib(), name)(*args)
+    if rc != LEMA_OK:
+        raise LemaError(rc, last_error(), name)
+
+
+def version() -> str:
+    return lib().lema_version().decode()
+
+
+def device_error() -> int:
+    """Synchronises the current device and returns (and clears) its device error word."""
+    out = i32(0)
+    call("lema_device_error", C.byref(out))
+    return out.value
+
+
+def num_sms() -> int:
+    out = i32(0)
+    call("lema_num_sms", C.byref(out))
+    return out.value
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)

@@ -1,0 +1,588 @@
+// gemm_sm100.cu — K2/K3 (int8 tcgen05 GEMM + fused dequant/bias/bf16 epilogue),
+// the bf16 tcgen05 GEMM used by K4 (dgrad), and K6 (grouped int8 GEMM for MoE
+// experts). One persistent, warp-specialised kernel template serves all three:
+//
+//   warp 0      TMA producer: one thread streams 128-byte-wide K slices of the
+//               A tile (128 rows) and B tile (BN rows) into a STAGES-deep ring
+//               of 128B-swizzled shared-memory buffers (plain TMA, no multicast).
+//   warp 1      allocates TMEM (2 x BN columns: double-buffered accumulators);
+//               one thread issues tcgen05.mma (M=128, N=BN, K=32 bytes per
+//               instruction) and tcgen05.commit to free smem stages / publish
+//               finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, then
+//               y = bf16((float(acc) * sx[m]) * sw[n] + bias[n]) (int8 kind) or
+//               y = bf16(acc) (bf16 kind), stored straight to global memory,
+//               while the MMA warp already accumulates the next tile into the
+//               other TMEM buffer.
+//
+// Tiles are ordered m-fastest inside each group so concurrently running CTAs
+// share the B (weight) tile through L2. A "group" is a contiguous row range of
+// A that multiplies its own B matrix (MoE experts); the dense GEMM is one group.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace lema {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kRowBytes = 128;  // K bytes per stage row (one 128B swizzle atom row)
+constexpr int kMaxGroups = 64;
+constexpr int kThreads = 192;
+
+enum GemmKind : int { kKindI8 = 0, kKindBF16 = 1 };
+
+struct GemmParams {
+  int32_t num_kb;       // K slices of 128 bytes
+  int32_t n;            // columns of every group's output
+  int32_t num_n_tiles;  // ceil(n / BN)
+  int32_t num_groups;
+  int32_t total_tiles;
+  int32_t row_start[kMaxGroups + 1];   // group g owns A rows [row_start[g], row_start[g+1])
+  int32_t tile_start[kMaxGroups + 1];  // first linear tile index of group g
+  const float* sx;                     // [rows] per-row scale (int8 kind)
+  const float* sw;                     // [groups * n] per-column scale (int8 kind)
+  const __nv_bfloat16* bias;           // [groups * n] or null
+  __nv_bfloat16* y;                    // may be null
+  int64_t ldy;
+  int32_t* acc;                        // raw s32 accumulators or null (int8 kind)
+  int64_t ldacc;
+  int32_t* err;                        // device error word
+};
+
+__device__ int32_t g_gemm_err = 0;
+
+__device__ __forceinline__ void record_error(int32_t* err, int32_t code, int* abort_flag) {
+  atomicCAS(err, 0, code);
+  *reinterpret_cast<volatile int*>(abort_flag) = 1;
+}
+
+__device__ __forceinline__ bool aborted(const int* abort_flag) {
+  return *reinterpret_cast<const volatile int*>(abort_flag) != 0;
+}
+
+// Linear tile index -> (group, first A row, end row of the group, column tile).
+__device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, int& row0,
+                                            int& row_end, int& n_tile) {
+  g = 0;
+  while (g + 1 < p.num_groups && t >= p.tile_start[g + 1]) ++g;
+  const int local = t - p.tile_start[g];
+  const int rows = p.row_start[g + 1] - p.row_start[g];
+  const int m_tiles = (rows + kBM - 1) / kBM;
+  const int mt = local % m_tiles;
+  const int nt = local / m_tiles;
+  row0 = p.row_start[g] + mt * kBM;
+  row_end = p.row_start[g + 1];
+  n_tile = nt;
+}
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kABytes = kBM * kRowBytes;
+  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
+  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
+};
+
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tma_a,
+                      const __grid_constant__ CUtensorMap tma_b,
+                      const __grid_constant__ GemmParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  constexpr int kTmemCols = 2 * BN;  // 256 or 512: a power of two >= 32
+  constexpr int kElemsPerRow = (KIND == kKindI8) ? 128 : 64;
+  constexpr int kKStepBytes = 32;  // K=32 int8 or K=16 bf16 per MMA instruction
+  constexpr uint32_t kIdesc =
+      (KIND == kKindI8) ? ptx::idesc_i8_s32(kBM, BN) : ptx::idesc_bf16_f32(kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&tma_a);
+    ptx::prefetch_tmap(&tma_b);
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tmem_full[b], 1);
+      ptx::mbar_init(&tmem_empty[b], 128);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;  // loads issued so far; load i used stage i % STAGES
+      for (int t = blockIdx.x; t < p.total_tiles && !aborted(abort_flag); t += gridDim.x) {
+        int g, row0, row_end, nt;
+        decode_tile(p, t, g, row0, row_end, nt);
+        const int b_row0 = g * p.n + nt * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_error(p.err, kDevErrProducerTimeout, abort_flag);
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          ptx::tma_load_2d(smem_a + stage * L::kABytes, &tma_a, &full[stage],
+                           kb * kElemsPerRow, row0);
+          ptx::tma_load_2d(smem_b + stage * L::kBBytes, &tma_b, &full[stage],
+                           kb * kElemsPerRow, b_row0);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag)) {
+        // Drain: the last (up to STAGES) issued loads must land before this
+        // CTA's shared memory is released.
+        for (int64_t i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
+          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < p.total_tiles && !aborted(abort_flag); t += gridDim.x) {
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+          record_error(p.err, kDevErrMmaTimeout, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase)) {
+            record_error(p.err, kDevErrMmaTimeout, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(smem_a + stage * L::kABytes);
+          const uint32_t b_addr = ptx::smem_u32(smem_b + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kRowBytes / kKStepBytes; ++k) {
+            const uint64_t ad = ptx::desc_kmajor_sw128(a_addr + k * kKStepBytes);
+            const uint64_t bd = ptx::desc_kmajor_sw128(b_addr + k * kKStepBytes);
+            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            if (KIND == kKindI8)
+              ptx::mma_i8(d_tmem, ad, bd, kIdesc, accumulate);
+            else
+              ptx::mma_bf16(d_tmem, ad, bd, kIdesc, accumulate);
+          }
+          issued_any = true;
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&tmem_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (aborted(abort_flag) && issued_any) {
+        // Drain outstanding MMAs before TMEM is released: commit to a stage
+        // barrier whose next phase nobody else completes and wait for it.
+        ptx::mma_commit(&tmem_full[acc]);
+        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may read: [32q, 32q+32)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool y_vec = p.y != nullptr && (p.ldy % 8) == 0 &&
+                       (reinterpret_cast<uintptr_t>(p.y) & 15u) == 0;
+    const bool acc_vec = p.acc != nullptr && (p.ldacc % 4) == 0 &&
+                         (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      int g, row0, row_end, nt;
+      decode_tile(p, t, g, row0, row_end, nt);
+      const int n0 = nt * BN;
+      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
+        record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
+        break;
+      }
+      if (aborted(abort_flag)) break;
+      ptx::tc_fence_after();
+      const int r = row0 + quarter * 32 + lane;
+      const bool rvalid = r < row_end;
+      float sxr = 0.f;
+      if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
+      const float* swg = (KIND == kKindI8) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
+      const __nv_bfloat16* bg =
+          p.bias != nullptr ? p.bias + static_cast<int64_t>(g) * p.n : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN + c * 32);
+        ptx::tmem_ld_32x32b_x32(taddr, v);
+        ptx::tmem_ld_wait();
+        const int n = n0 + c * 32;
+        if (!rvalid || n >= p.n) continue;
+        const bool full_chunk = (n + 32) <= p.n;
+        if (KIND == kKindI8 && p.acc != nullptr) {
+          int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
+          if (full_chunk && acc_vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<uint4*>(arow + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && n + j < p.n; ++j) arow[j] = static_cast<int32_t>(v[j]);
+          }
+        }
+        if (p.y == nullptr) continue;
+        __align__(16) __nv_bfloat16 out[32];
+        if (KIND == kKindI8) {
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
+                                  __ldg(swg + n + j));
+              if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+              out[j] = __float2bfloat16_rn(f);
+            }
+          } else {
+            for (int j = 0; j < 32 && n + j < p.n; ++j) {
+              float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
+                                  swg[n + j]);
+              if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+              out[j] = __float2bfloat16_rn(f);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float f = __uint_as_float(v[j]);
+            if (bg != nullptr && n + j < p.n) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+            out[j] = __float2bfloat16_rn(f);
+          }
+        }
+        __nv_bfloat16* yrow = p.y + static_cast<int64_t>(r) * p.ldy + n;
+        if (full_chunk && y_vec) {
+          const uint4* src = reinterpret_cast<const uint4*>(out);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yrow)[j] = src[j];
+        } else {
+          for (int j = 0; j < 32 && n + j < p.n; ++j) yrow[j] = out[j];
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tmem_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D K-major operand map: `rows` rows of `k` elements, row stride `ld`
+// elements, box = 128 bytes of K x box_rows rows, 128-byte swizzle, zero fill.
+int make_operand_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                     int elem_bytes, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytes / elem_bytes),
+                       static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " +
+                                        std::to_string(static_cast<int>(r)) + ")");
+  return LEMA_OK;
+}
+
+template <int KIND, int BN, int STAGES>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
+           cudaStream_t stream) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = gemm_sm100_kernel<KIND, BN, STAGES>;
+  static bool attr_done[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(LEMA_ERR_CUDA, "bad device");
+  if (!attr_done[dev]) {
+    LEMA_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    attr_done[dev] = true;
+  }
+  const int grid = std::min(p.total_tiles, device_sm_count());
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+int32_t* gemm_err_ptr() {
+  int32_t* ptr = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_gemm_err) != cudaSuccess)
+    return nullptr;
+  return ptr;
+}
+
+struct Groups {
+  int num = 0;
+  int64_t row_start[kMaxGroups + 1];
+};
+
+// Shared front end of the dense, grouped and bf16 GEMMs.
+int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
+             const Groups& groups, int64_t n, int64_t k, const float* sx, const float* sw,
+             const void* bias, void* y, int64_t ldy, int32_t* acc, int64_t ldacc,
+             cudaStream_t stream) {
+  const int elem = (kind == kKindI8) ? 1 : 2;
+  const int64_t rows = groups.row_start[groups.num];
+  if (rows == 0 || n == 0) return LEMA_OK;
+  if (a == nullptr || b == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null operand");
+  if (y == nullptr && acc == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "no output (y and acc_dbg both null)");
+  if (kind == kKindI8 && (sx == nullptr || sw == nullptr))
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null scale pointer");
+  if (rows > INT32_MAX || n > INT32_MAX || k > INT32_MAX ||
+      n * static_cast<int64_t>(groups.num) > INT32_MAX)
+    return set_error(LEMA_ERR_UNSUPPORTED, "dimension exceeds int32");
+  if ((y != nullptr && ldy < n) || (acc != nullptr && ldacc < n))
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "output leading dimension < N");
+  if (k == 0) return set_error(LEMA_ERR_UNSUPPORTED, "K == 0 must be handled by the caller");
+  if (lda < k || ldb < k) return set_error(LEMA_ERR_INVALID_ARGUMENT, "operand ld < K");
+  if (!aligned16(a) || !aligned16(b) || (lda * elem) % 16 != 0 || (ldb * elem) % 16 != 0)
+    return set_error(LEMA_ERR_MISALIGNED,
+                     "TMA operands need 16-byte aligned base pointers and row strides");
+
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int num_kb = static_cast<int>((k * elem + kRowBytes - 1) / kRowBytes);
+  p.num_kb = num_kb;
+  p.n = static_cast<int32_t>(n);
+  p.num_groups = groups.num;
+  p.sx = sx;
+  p.sw = sw;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.acc = acc;
+  p.ldacc = ldacc;
+  p.err = gemm_err_ptr();
+  if (p.err == nullptr) return set_error(LEMA_ERR_CUDA, "cannot resolve device error word");
+
+  // Tile shape: 128 x 256 when that already fills the machine, else 128 x 128.
+  const int sms = device_sm_count();
+  int64_t m_tiles_total = 0;
+  for (int g = 0; g < groups.num; ++g)
+    m_tiles_total += (groups.row_start[g + 1] - groups.row_start[g] + kBM - 1) / kBM;
+  const int bn = (m_tiles_total * ((n + 255) / 256) >= sms && n > 128) ? 256 : 128;
+  p.num_n_tiles = static_cast<int32_t>((n + bn - 1) / bn);
+  int64_t tiles = 0;
+  for (int g = 0; g < groups.num; ++g) {
+    p.row_start[g] = static_cast<int32_t>(groups.row_start[g]);
+    p.tile_start[g] = static_cast<int32_t>(tiles);
+    const int64_t mt = (groups.row_start[g + 1] - groups.row_start[g] + kBM - 1) / kBM;
+    tiles += mt * p.num_n_tiles;
+  }
+  p.row_start[groups.num] = static_cast<int32_t>(rows);
+  p.tile_start[groups.num] = static_cast<int32_t>(tiles);
+  if (tiles > INT32_MAX) return set_error(LEMA_ERR_UNSUPPORTED, "too many tiles");
+  p.total_tiles = static_cast<int32_t>(tiles);
+  if (tiles == 0) return LEMA_OK;
+
+  const CUtensorMapDataType dt =
+      (kind == kKindI8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ma, mb;
+  int rc = make_operand_map(&ma, a, dt, elem, rows, k, lda, kBM);
+  if (rc) return rc;
+  rc = make_operand_map(&mb, b, dt, elem, n * groups.num, k, ldb, bn);
+  if (rc) return rc;
+
+  if (kind == kKindI8) {
+    return bn == 256 ? launch<kKindI8, 256, 4>(ma, mb, p, stream)
+                     : launch<kKindI8, 128, 6>(ma, mb, p, stream);
+  }
+  return bn == 256 ? launch<kKindBF16, 256, 4>(ma, mb, p, stream)
+                   : launch<kKindBF16, 128, 6>(ma, mb, p, stream);
+}
+
+// y = bias (or 0) broadcast over rows: the K == 0 case.
+__global__ void fill_bias_kernel(__nv_bfloat16* y, int64_t ldy, int64_t m, int64_t n,
+                                 const __nv_bfloat16* bias) {
+  const int64_t total = m * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n, c = i % n;
+    y[r * ldy + c] = bias ? bias[c] : __float2bfloat16_rn(0.f);
+  }
+}
+
+__global__ void fill_zero_i32_kernel(int32_t* a, int64_t lda, int64_t m, int64_t n) {
+  const int64_t total = m * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    a[(i / n) * lda + (i % n)] = 0;
+}
+
+int k_zero_outputs(void* y, int64_t ldy, const void* bias, int32_t* acc, int64_t ldacc,
+                   int64_t m, int64_t n, cudaStream_t s) {
+  if (m == 0 || n == 0) return LEMA_OK;
+  const int grid = static_cast<int>(std::min<int64_t>((m * n + 255) / 256, 4096));
+  if (y)
+    fill_bias_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(y), ldy, m, n,
+                                          static_cast<const __nv_bfloat16*>(bias));
+  if (acc) fill_zero_i32_kernel<<<grid, 256, 0, s>>>(acc, ldacc, m, n);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+}  // namespace
+
+int gemm_read_device_error(int32_t* out) {
+  int32_t v = 0, zero = 0;
+  LEMA_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(v)));
+  LEMA_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_err, &zero, sizeof(zero)));
+  *out = v;
+  return LEMA_OK;
+}
+
+}  // namespace lema
+
+using namespace lema;
+
+extern "C" int lema_w8a8_gemm(const int8_t* xq, int64_t ldx, const float* sx, const int8_t* wq,
+                              int64_t ldw, const float* sw, const void* bias_bf16, void* y_bf16,
+                              int64_t ldy, int32_t* acc_dbg, int64_t ldacc, int64_t M, int64_t N,
+                              int64_t K, void* stream) {
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  auto s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return k_zero_outputs(y_bf16, ldy, bias_bf16, acc_dbg, ldacc, M, N, s);
+  Groups g;
+  g.num = 1;
+  g.row_start[0] = 0;
+  g.row_start[1] = M;
+  return run_gemm(kKindI8, xq, ldx, wq, ldw, g, N, K, sx, sw, bias_bf16, y_bf16, ldy, acc_dbg,
+                  ldacc, s);
+}
+
+extern "C" int lema_bf16_gemm_tn(const void* a_bf16, int64_t lda, const void* b_bf16,
+                                 int64_t ldb, void* y_bf16, int64_t ldy, int64_t M, int64_t N,
+                                 int64_t K, void* stream) {
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  auto s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return k_zero_outputs(y_bf16, ldy, nullptr, nullptr, 0, M, N, s);
+  Groups g;
+  g.num = 1;
+  g.row_start[0] = 0;
+  g.row_start[1] = M;
+  return run_gemm(kKindBF16, a_bf16, lda, b_bf16, ldb, g, N, K, nullptr, nullptr, nullptr,
+                  y_bf16, ldy, nullptr, 0, s);
+}
+
+extern "C" int lema_grouped_w8a8_gemm(const int8_t* xq, int64_t ldx, const float* sx,
+                                      const int8_t* wq, int64_t ldw, const float* sw,
+                                      const void* bias_bf16, void* y_bf16, int64_t ldy,
+                                      const int64_t* offsets_host, int32_t E, int64_t N,
+                                      int64_t K, void* stream) {
+  clear_error();
+  if (offsets_host == nullptr || E <= 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "offsets must hold E+1 entries, E >= 1");
+  if (E > kMaxGroups)
+    return set_error(LEMA_ERR_UNSUPPORTED, "more than 64 experts per grouped launch");
+  if (N < 0 || K < 0 || offsets_host[0] != 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad sizes or offsets[0] != 0");
+  Groups g;
+  g.num = E;
+  for (int e = 0; e <= E; ++e) {
+    g.row_start[e] = offsets_host[e];
+    if (e > 0 && offsets_host[e] < offsets_host[e - 1])
+      return set_error(LEMA_ERR_INVALID_ARGUMENT, "offsets must be non-decreasing");
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    // Every row gets its expert's bias.
+    for (int e = 0; e < E; ++e) {
+      const int64_t r0 = offsets_host[e], r1 = offsets_host[e + 1];
+      if (r1 == r0) continue;
+      const void* b = bias_bf16 ? static_cast<const __nv_bfloat16*>(bias_bf16) + e * N : nullptr;
+      int rc = k_zero_outputs(static_cast<__nv_bfloat16*>(y_bf16) + r0 * ldy, ldy, b, nullptr, 0,
+                              r1 - r0, N, s);
+      if (rc) return rc;
+    }
+    return LEMA_OK;
+  }
+  return run_gemm(kKindI8, xq, ldx, wq, ldw, g, N, K, sx, sw, bias_bf16, y_bf16, ldy, nullptr, 0,
+                  s);
+}

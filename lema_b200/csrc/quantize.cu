@@ -1,0 +1,300 @@
+// quantize.cu — K1: per-row dynamic symmetric int8 quantisation (per token for
+// activations, per output channel for weights), the int8 -> bf16 dequant +
+// transpose that feeds the dgrad GEMM, and the C-ABI front ends that chain
+// K1 -> K2/K3 (forward) and dequant -> bf16 GEMM (dgrad).
+//
+// K1 is HBM-bound: one CTA of 128 threads owns one row, reads it once with
+// 128-bit loads into registers (up to 16 vectors per thread = 16384 bf16),
+// reduces |x| with warp shuffles + a 4-entry shared array, then quantises from
+// registers and writes int8 with 64-bit stores. Rows longer than the register
+// budget, unaligned rows and ragged column counts take a two-pass scalar path.
+// The arithmetic is the operator contract: IEEE fp32 division by the scale
+// (no reciprocal), round-half-even, clamp to [-127, 127].
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "internal.h"
+
+namespace lema {
+
+extern "C" int lema_w8a8_gemm(const int8_t*, int64_t, const float*, const int8_t*, int64_t,
+                              const float*, const void*, void*, int64_t, int32_t*, int64_t,
+                              int64_t, int64_t, int64_t, void*);
+extern "C" int lema_bf16_gemm_tn(const void*, int64_t, const void*, int64_t, void*, int64_t,
+                                 int64_t, int64_t, int64_t, void*);
+
+namespace {
+
+constexpr int kQThreads = 128;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Max over the CTA (128 threads = 4 warps); every thread gets the result.
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  return r;
+}
+
+__device__ __forceinline__ float row_scale(float amax) {
+  return amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
+}
+
+__device__ __forceinline__ int8_t quant1(float x, float s) {
+  int q = __float2int_rn(__fdiv_rn(x, s));
+  q = max(-127, min(127, q));
+  return static_cast<int8_t>(q);
+}
+
+template <typename T>
+struct Vec;
+template <>
+struct Vec<__nv_bfloat16> {
+  static constexpr int kElems = 8;  // 8 x bf16 per 16-byte vector
+  __device__ static float absmax(const uint4& v) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+    __nv_bfloat162 m = __hmax2(__habs2(h[0]), __habs2(h[1]));
+    m = __hmax2(m, __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
+  }
+  __device__ static void quant(const uint4& v, float s, int8_t* out) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = quant1(__bfloat162float(h[i]), s);
+  }
+  __device__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+};
+template <>
+struct Vec<float> {
+  static constexpr int kElems = 4;
+  __device__ static float absmax(const uint4& v) {
+    return fmaxf(fmaxf(fabsf(__uint_as_float(v.x)), fabsf(__uint_as_float(v.y))),
+                 fmaxf(fabsf(__uint_as_float(v.z)), fabsf(__uint_as_float(v.w))));
+  }
+  __device__ static void quant(const uint4& v, float s, int8_t* out) {
+    out[0] = quant1(__uint_as_float(v.x), s);
+    out[1] = quant1(__uint_as_float(v.y), s);
+    out[2] = quant1(__uint_as_float(v.z), s);
+    out[3] = quant1(__uint_as_float(v.w), s);
+  }
+  __device__ static float to_f(float x) { return x; }
+};
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Register-resident path: cols % kElems == 0, 16-byte aligned rows, and
+// cols <= VPT * 128 * kElems.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __restrict__ x,
+                                                                   int64_t ldx, int cols,
+                                                                   int8_t* __restrict__ q,
+                                                                   int64_t ldq,
+                                                                   float* __restrict__ scale) {
+  constexpr int E = Vec<T>::kElems;
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  const int nvec = cols / E;
+  uint4 v[VPT];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kQThreads;
+    if (idx < nvec) {
+      v[i] = ld_stream(xr + idx);
+      amax = fmaxf(amax, Vec<T>::absmax(v[i]));
+    }
+  }
+  amax = block_max(amax, red);
+  const float s = row_scale(amax);
+  int8_t* qr = q + row * ldq;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kQThreads;
+    if (idx < nvec) {
+      __align__(8) int8_t out[E];
+      Vec<T>::quant(v[i], s, out);
+      if (E == 8)
+        *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(idx) * E) =
+            *reinterpret_cast<const uint2*>(out);
+      else
+        *reinterpret_cast<uint32_t*>(qr + static_cast<int64_t>(idx) * E) =
+            *reinterpret_cast<const uint32_t*>(out);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+// General path: any alignment / length; reads the row twice.
+template <typename T>
+__global__ void __launch_bounds__(kQThreads) quant_rows_generic_kernel(const T* __restrict__ x,
+                                                                       int64_t ldx, int64_t cols,
+                                                                       int8_t* __restrict__ q,
+                                                                       int64_t ldq,
+                                                                       float* __restrict__ scale) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ldx;
+  float amax = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += kQThreads)
+    amax = fmaxf(amax, fabsf(Vec<T>::to_f(xr[c])));
+  amax = block_max(amax, red);
+  const float s = row_scale(amax);
+  int8_t* qr = q + row * ldq;
+  for (int64_t c = threadIdx.x; c < cols; c += kQThreads) qr[c] = quant1(Vec<T>::to_f(xr[c]), s);
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <typename T>
+int quantize_rows_impl(const T* x, int64_t rows, int64_t cols, int64_t ldx, int8_t* q,
+                       int64_t ldq, float* scale, cudaStream_t s) {
+  clear_error();
+  if (rows < 0 || cols < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0) return LEMA_OK;
+  if (x == nullptr || q == nullptr || scale == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldx < cols || ldq < cols) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld < cols");
+  if (rows > INT32_MAX) return set_error(LEMA_ERR_UNSUPPORTED, "rows exceed 2^31-1");
+  constexpr int E = Vec<T>::kElems;
+  const bool vec_ok = cols > 0 && cols % E == 0 && aligned16(x) && (ldx * sizeof(T)) % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(q) % E) == 0 && ldq % E == 0;
+  const int64_t per_thread = (cols / E + kQThreads - 1) / kQThreads;
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (vec_ok && per_thread <= 16) {
+    if (per_thread <= 1)
+      quant_rows_vec_kernel<T, 1><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+    else if (per_thread <= 2)
+      quant_rows_vec_kernel<T, 2><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+    else if (per_thread <= 4)
+      quant_rows_vec_kernel<T, 4><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+    else if (per_thread <= 8)
+      quant_rows_vec_kernel<T, 8><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+    else if (per_thread <= 12)
+      quant_rows_vec_kernel<T, 12><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+    else
+      quant_rows_vec_kernel<T, 16><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
+  } else {
+    quant_rows_generic_kernel<T><<<grid, kQThreads, 0, s>>>(x, ldx, cols, q, ldq, scale);
+  }
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+// wdT[k, n] = bf16(float(wq[n, k]) * sw[n]); 64 x 64 tiles through shared memory.
+constexpr int kTT = 64;
+__global__ void __launch_bounds__(256) dequant_transpose_kernel(const int8_t* __restrict__ wq,
+                                                                int64_t ldw,
+                                                                const float* __restrict__ sw,
+                                                                int64_t n_rows, int64_t k_cols,
+                                                                __nv_bfloat16* __restrict__ out,
+                                                                int64_t ldt) {
+  __shared__ __nv_bfloat16 tile[kTT][kTT + 2];  // [k][n], padded against bank conflicts
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTT;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kTT;
+  // Load: 64 rows (n) x 64 int8 (k); thread -> (row = t / 4, 16 bytes at (t % 4) * 16).
+  {
+    const int r = threadIdx.x / 4, c16 = (threadIdx.x % 4) * 16;
+    const int64_t n = n0 + r;
+    float s = 0.f;
+    if (n < n_rows) s = sw[n];
+    const int8_t* src = wq + n * ldw + k0 + c16;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t k = k0 + c16 + j;
+      float f = 0.f;
+      if (n < n_rows && k < k_cols) f = __fmul_rn(static_cast<float>(src[j]), s);
+      tile[c16 + j][r] = __float2bfloat16_rn(f);
+    }
+  }
+  __syncthreads();
+  // Store: 64 rows (k) x 64 bf16 (n); each thread writes 2 x 8 consecutive n.
+  for (int i = threadIdx.x; i < kTT * (kTT / 8); i += 256) {
+    const int r = i / (kTT / 8), c8 = (i % (kTT / 8)) * 8;
+    const int64_t k = k0 + r;
+    if (k >= k_cols) continue;
+    __nv_bfloat16* dst = out + k * ldt + n0 + c8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (n0 + c8 + j < n_rows) dst[j] = tile[r][c8 + j];
+  }
+}
+
+}  // namespace
+
+int quant_read_device_error(int32_t* out) {
+  *out = 0;
+  return LEMA_OK;
+}
+
+}  // namespace lema
+
+using namespace lema;
+
+extern "C" int lema_quantize_rows(const void* x_bf16, int64_t rows, int64_t cols, int64_t ldx,
+                                  int8_t* q, int64_t ldq, float* scale, void* stream) {
+  return quantize_rows_impl(static_cast<const __nv_bfloat16*>(x_bf16), rows, cols, ldx, q, ldq,
+                            scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lema_quantize_rows_f32(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                                      int8_t* q, int64_t ldq, float* scale, void* stream) {
+  return quantize_rows_impl(x, rows, cols, ldx, q, ldq, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lema_quantize_per_token(const void* x_bf16, int64_t M, int64_t K, int64_t ldx,
+                                       int8_t* xq, int64_t ldq, float* sx, void* stream) {
+  return lema_quantize_rows(x_bf16, M, K, ldx, xq, ldq, sx, stream);
+}
+
+extern "C" int lema_w8a8_linear_fwd(const void* x_bf16, int64_t ldx, const int8_t* wq,
+                                    int64_t ldw, const float* sw, const void* bias_bf16,
+                                    void* y_bf16, int64_t ldy, int8_t* xq_ws, int64_t ldq,
+                                    float* sx_ws, int64_t M, int64_t N, int64_t K, void* stream) {
+  int rc = lema_quantize_rows(x_bf16, M, K, ldx, xq_ws, ldq, sx_ws, stream);
+  if (rc) return rc;
+  return lema_w8a8_gemm(xq_ws, ldq, sx_ws, wq, ldw, sw, bias_bf16, y_bf16, ldy, nullptr, 0, M, N,
+                        K, stream);
+}
+
+extern "C" int lema_dequant_transpose(const int8_t* wq, int64_t ldw, const float* sw, int64_t N,
+                                      int64_t K, void* wdT_bf16, int64_t ldt, void* stream) {
+  clear_error();
+  if (N < 0 || K < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  if (N == 0 || K == 0) return LEMA_OK;
+  if (wq == nullptr || sw == nullptr || wdT_bf16 == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldw < K || ldt < N) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld too small");
+  if ((K + kTT - 1) / kTT > INT32_MAX || (N + kTT - 1) / kTT > 65535)
+    return set_error(LEMA_ERR_UNSUPPORTED, "matrix too large for the transpose grid");
+  dim3 grid(static_cast<unsigned>((K + kTT - 1) / kTT), static_cast<unsigned>((N + kTT - 1) / kTT));
+  dequant_transpose_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      wq, ldw, sw, N, K, static_cast<__nv_bfloat16*>(wdT_bf16), ldt);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_w8a8_dgrad(const void* dy_bf16, int64_t lddy, const int8_t* wq, int64_t ldw,
+                               const float* sw, void* dx_bf16, int64_t lddx, void* wdT_ws,
+                               int64_t ldt, int64_t M, int64_t N, int64_t K, void* stream) {
+  clear_error();
+  if (ldt < N || ldt % 8 != 0)
+    return set_error(LEMA_ERR_MISALIGNED, "workspace ld must be >= N and a multiple of 8");
+  int rc = lema_dequant_transpose(wq, ldw, sw, N, K, wdT_ws, ldt, stream);
+  if (rc) return rc;
+  // dx[M, K] = dy[M, N] . wdT[K, N]^T
+  return lema_bf16_gemm_tn(dy_bf16, lddy, wdT_ws, ldt, dx_bf16, lddx, M, K, N, stream);
+}

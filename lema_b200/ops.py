@@ -1,0 +1,287 @@
+"""Torch-facing W8A8 operators over the C ABI.
+
+These are the host-side mirror of the op the reference runs at every
+projection of a streamed decoder layer: ``nn.Linear`` inside HF
+``LlamaDecoderLayer`` (created at adapters/_llama.py:80, called at
+adapters/_llama.py:245-250), wrapped by ``LoRAWrapper.forward``
+(_lora.py:23-26). The quantised operator is defined in include/lema_b200.h:
+
+* ``quantize_rows``      per-row symmetric int8 (per token / per output channel)
+* ``w8a8_gemm``          int8 x int8 -> s32 (tcgen05) + dequant/bias/bf16 epilogue
+* ``w8a8_linear``        differentiable y = x W^T (+ b) with straight-through
+                         backward dx = dy . (wq * sw) through ``w8a8_dgrad``
+* ``grouped_w8a8_gemm``  the same per expert over pre-sorted token ranges
+
+All tensors must live on a CUDA device; there is no CPU fallback. Calls run
+on the current torch stream of the tensors' device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _native as N
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "lema_b200 ops run only on CUDA tensors (no CPU fallback); got a tensor on "
+                f"{t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    if dev is None:
+        raise RuntimeError("no tensor given")
+    return dev
+
+
+def _rows_view(t: torch.Tensor) -> torch.Tensor:
+    """2-D view with unit stride along the last dim (copies only if needed)."""
+    if t.dim() != 2:
+        raise ValueError(f"expected a 2-D tensor, got shape {tuple(t.shape)}")
+    if t.stride(1) != 1 or t.stride(0) < t.shape[1]:
+        t = t.contiguous()
+    return t
+
+
+def _ld(t: torch.Tensor) -> int:
+    return t.stride(0) if t.shape[0] > 1 else max(t.shape[1], t.stride(0))
+
+
+def pad_to(n: int, m: int) -> int:
+    return (n + m - 1) // m * m
+
+
+# ---------------------------------------------------------------------------
+# K1: quantisation
+# ---------------------------------------------------------------------------
+
+def quantize_rows(x: torch.Tensor, out: torch.Tensor | None = None,
+                  scale: torch.Tensor | None = None, ldq: int | None = None
+                  ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row int8 quantisation of a bf16 or fp32 [R, C] tensor.
+
+    Returns (q int8 [R, C] (a view of an [R, ldq] buffer), scale fp32 [R]).
+    ``ldq`` defaults to C rounded up to 16 so the result can feed the GEMM.
+    """
+    dev = _require_cuda(x)
+    x = _rows_view(x)
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"quantize_rows takes bf16 or fp32, got {x.dtype}")
+    rows, cols = x.shape
+    if ldq is None:
+        ldq = pad_to(max(cols, 1), 16)
+    if out is None:
+        buf = torch.empty(rows, ldq, dtype=torch.int8, device=dev)
+        if ldq > cols:
+            buf[:, cols:].zero_()
+    else:
+        buf = out
+        if buf.dtype != torch.int8 or buf.shape[0] != rows or buf.stride(1) != 1:
+            raise ValueError("out must be int8 [rows, >=cols] with unit column stride")
+        ldq = buf.stride(0) if rows > 1 else ldq
+    if scale is None:
+        scale = torch.empty(rows, dtype=torch.float32, device=dev)
+    fn = "lema_quantize_rows" if x.dtype == torch.bfloat16 else "lema_quantize_rows_f32"
+    N.call(fn, _ptr(x), rows, cols, _ld(x), _ptr(buf), ldq, _ptr(scale), _stream(dev))
+    return buf[:, :cols], scale
+
+
+def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel int8 quantisation of an nn.Linear weight [N, K].
+
+    Returns (wq int8 [N, K] with row stride padded to 16, sw fp32 [N]).
+    """
+    if w.dtype not in (torch.bfloat16, torch.float32):
+        w = w.to(torch.bfloat16)
+    return quantize_rows(w)
+
+
+# ---------------------------------------------------------------------------
+# K2+K3: int8 GEMM with fused epilogue
+# ---------------------------------------------------------------------------
+
+def w8a8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+              bias: torch.Tensor | None = None, want_y: bool = True, want_acc: bool = False,
+              out: torch.Tensor | None = None):
+    """y[M,N] = bf16((acc * sx[m]) * sw[n] + bias[n]), acc = xq . wq^T (exact s32).
+
+    Returns y, or (y, acc) when ``want_acc`` (y is None if not ``want_y``).
+    """
+    dev = _require_cuda(xq, sx, wq, sw, bias)
+    if xq.dtype != torch.int8 or wq.dtype != torch.int8:
+        raise TypeError("xq and wq must be int8")
+    M, K = xq.shape
+    Nn, K2 = wq.shape
+    if K2 != K:
+        raise ValueError(f"K mismatch: {K} vs {K2}")
+    if xq.stride(1) != 1 or wq.stride(1) != 1:
+        raise ValueError("xq and wq need unit column stride")
+    sx = sx.contiguous().float()
+    sw = sw.contiguous().float()
+    if bias is not None:
+        bias = bias.contiguous().to(torch.bfloat16)
+    y = None
+    if want_y:
+        y = out if out is not None else torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
+    acc = torch.empty(M, Nn, dtype=torch.int32, device=dev) if want_acc else None
+    N.call("lema_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw),
+           _ptr(bias), _ptr(y), Nn if y is None else _ld(y), _ptr(acc), Nn, M, Nn, K,
+           _stream(dev))
+    if want_acc:
+        return y, acc
+    return y
+
+
+def w8a8_linear_forward(x2d: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                        bias: torch.Tensor | None = None) -> torch.Tensor:
+    """K1 + K2/K3 on a bf16 [M, K] input: the forward of one W8A8 projection."""
+    dev = _require_cuda(x2d, wq, sw, bias)
+    x2d = _rows_view(x2d)
+    if x2d.dtype != torch.bfloat16:
+        raise TypeError("w8a8 forward takes bf16 activations")
+    M, K = x2d.shape
+    Nn = wq.shape[0]
+    if wq.shape[1] != K:
+        raise ValueError(f"weight in_features {wq.shape[1]} != input features {K}")
+    ldq = pad_to(max(K, 1), 16)
+    xq = torch.empty(M, ldq, dtype=torch.int8, device=dev)
+    sx = torch.empty(M, dtype=torch.float32, device=dev)
+    y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
+    if bias is not None:
+        bias = bias.contiguous().to(torch.bfloat16)
+    N.call("lema_w8a8_linear_fwd", _ptr(x2d), _ld(x2d), _ptr(wq), _ld(wq), _ptr(sw),
+           _ptr(bias), _ptr(y), Nn, _ptr(xq), ldq, _ptr(sx), M, Nn, K, _stream(dev))
+    return y
+
+
+# ---------------------------------------------------------------------------
+# K4: backward of the frozen base
+# ---------------------------------------------------------------------------
+
+def dequant_transpose(wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """wdT[K, ldt] bf16 with wdT[k, n] = bf16(float(wq[n, k]) * sw[n]); returns [K, N] view."""
+    dev = _require_cuda(wq, sw)
+    Nn, K = wq.shape
+    ldt = pad_to(max(Nn, 1), 8)
+    wdT = torch.empty(K, ldt, dtype=torch.bfloat16, device=dev)
+    N.call("lema_dequant_transpose", _ptr(wq), _ld(wq), _ptr(sw.contiguous().float()), Nn, K,
+           _ptr(wdT), ldt, _stream(dev))
+    return wdT[:, :Nn]
+
+
+def bf16_gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """y = bf16(a . b^T) with fp32 accumulation (tcgen05 kind::f16)."""
+    dev = _require_cuda(a, b)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("bf16 operands required")
+    a = _rows_view(a)
+    b = _rows_view(b)
+    M, K = a.shape
+    Nn = b.shape[0]
+    y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
+    N.call("lema_bf16_gemm_tn", _ptr(a), _ld(a), _ptr(b), _ld(b), _ptr(y), Nn, M, Nn, K,
+           _stream(dev))
+    return y
+
+
+def w8a8_dgrad(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """dx[M, K] = bf16(dy[M, N] . wdeq[N, K]), wdeq = bf16(wq * sw) (straight-through)."""
+    dev = _require_cuda(dy, wq, sw)
+    dy = _rows_view(dy)
+    if dy.dtype != torch.bfloat16:
+        dy = dy.to(torch.bfloat16)
+    if (dy.stride(0) * 2) % 16 != 0 or dy.data_ptr() % 16 != 0:
+        # TMA needs 16-byte row pitch: re-lay dy out with a padded pitch.
+        M0, N0 = dy.shape
+        buf = torch.zeros(M0, pad_to(N0, 8), dtype=torch.bfloat16, device=dev)
+        buf[:, :N0] = dy
+        dy = buf[:, :N0]
+    M, Nn = dy.shape
+    K = wq.shape[1]
+    ldt = pad_to(max(Nn, 1), 8)
+    ws = torch.empty(K, ldt, dtype=torch.bfloat16, device=dev)
+    dx = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    N.call("lema_w8a8_dgrad", _ptr(dy), _ld(dy), _ptr(wq), _ld(wq), _ptr(sw.contiguous().float()),
+           _ptr(dx), K, _ptr(ws), ldt, M, Nn, K, _stream(dev))
+    return dx
+
+
+# ---------------------------------------------------------------------------
+# K6: grouped W8A8 GEMM (MoE experts)
+# ---------------------------------------------------------------------------
+
+def grouped_w8a8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                      offsets: list[int], bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert W8A8 GEMM. xq [T, K] rows sorted by expert, wq [E, N, K], sw [E, N],
+    offsets: E+1 host ints (rows of expert e are offsets[e]:offsets[e+1])."""
+    dev = _require_cuda(xq, sx, wq, sw, bias)
+    E, Nn, K = wq.shape
+    if len(offsets) != E + 1:
+        raise ValueError("offsets must have E+1 entries")
+    if wq.stride(2) != 1 or wq.stride(0) != Nn * wq.stride(1):
+        raise ValueError("expert weights must be stacked contiguously: [E, N, ldw]")
+    T = xq.shape[0]
+    y = torch.empty(T, Nn, dtype=torch.bfloat16, device=dev)
+    offs = (C.c_int64 * (E + 1))(*[int(o) for o in offsets])
+    if bias is not None:
+        bias = bias.contiguous().to(torch.bfloat16)
+    N.call("lema_grouped_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx.contiguous().float()),
+           _ptr(wq), wq.stride(1), _ptr(sw.contiguous().float()), _ptr(bias), _ptr(y), Nn,
+           offs, E, Nn, K, _stream(dev))
+    return y
+
+
+# ---------------------------------------------------------------------------
+# Differentiable linear
+# ---------------------------------------------------------------------------
+
+class _W8A8LinearFn(torch.autograd.Function):
+    """y = W8A8(x); dx = dy . (wq * sw) (STE through both quantisers); no dW (frozen base)."""
+
+    @staticmethod
+    def forward(ctx, x2d, wq, sw, bias):
+        y = w8a8_linear_forward(x2d, wq, sw, bias)
+        ctx.save_for_backward(wq, sw)
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        wq, sw = ctx.saved_tensors
+        dx = w8a8_dgrad(dy, wq, sw) if ctx.needs_input_grad[0] else None
+        dbias = None
+        if ctx.has_bias and ctx.needs_input_grad[3]:
+            dbias = dy.float().sum(0).to(torch.bfloat16)
+        return dx, None, None, dbias
+
+
+def w8a8_linear(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Functional W8A8 linear over [..., K] -> [..., N] (bf16 compute, input dtype out)."""
+    K = x.shape[-1]
+    lead = x.shape[:-1]
+    in_dtype = x.dtype
+    x2d = x.reshape(-1, K)
+    if x2d.dtype != torch.bfloat16:
+        x2d = x2d.to(torch.bfloat16)
+    y = _W8A8LinearFn.apply(x2d, wq, sw, bias)
+    y = y.reshape(*lead, wq.shape[0])
+    if in_dtype != torch.bfloat16 and in_dtype.is_floating_point:
+        y = y.to(in_dtype)
+    return y
