@@ -167,7 +167,8 @@ def test_dequant_transpose_and_dgrad(cuda_device, oracle, M, N, K):
     np.testing.assert_array_equal(bits(wdT.contiguous()), ref_wdT)
     dy = rand_bf16((M, N), seed=M + 3, outliers=False)
     dx = ops.w8a8_dgrad(dy.to(dev), wq, sw)
-    _, ref = oracle.c_bf16_gemm_tn(bits(dy), np.ascontiguousarray(ref_wdT.T))
+    # dx[m, k] = sum_n dy[m, n] * wdT[k, n]: wdT is the [K, N] right operand
+    _, ref = oracle.c_bf16_gemm_tn(bits(dy), ref_wdT)
     _dgrad_tol_check(bits(dx), ref)
 
 
