@@ -106,6 +106,23 @@ LEMA_API int lema_w8a8_linear_fwd(const void* x_bf16, int64_t ldx,
                          int8_t* xq_ws, int64_t ldq, float* sx_ws,
                          int64_t M, int64_t N, int64_t K, void* stream);
 
+/* Allocation-free variant of lema_w8a8_linear_fwd. It has no counterpart in
+ * the reference. For callers that cannot allocate device memory (a host that
+ * binds this ABI from a runtime without a CUDA allocator, or a process whose
+ * device memory is owned by a framework's caching allocator under a fixed
+ * VRAM budget): the quantised-activation workspace lives in fixed device
+ * arrays inside this library (16 MiB of int8 + 65536 fp32 row scales, held
+ * by every GPU that loads the library until exit). Requires
+ * M * round_up(K, 16) <= 16 MiB and M <= 65536, else LEMA_ERR_UNSUPPORTED.
+ * The first call on a device looks up the arrays' device addresses; make it
+ * before any stream capture. All calls on a device share the arrays, so calls
+ * that overlap on the GPU race and must be serialised by the caller. Calls no
+ * cudaMalloc/cudaFree. */
+LEMA_API int lema_w8a8_linear_fwd_noalloc(const void* x_bf16, int64_t ldx,
+                                          const int8_t* wq, int64_t ldw, const float* sw,
+                                          const void* bias_bf16, void* y_bf16, int64_t ldy,
+                                          int64_t M, int64_t N, int64_t K, void* stream);
+
 /* ---- K4: backward of the frozen base (straight-through estimator) ------- */
 /* wdT[K,N] (bf16, row stride ldt) = bf16_rne(float(wq[n,k]) * sw[n]),
  * transposed so the dgrad GEMM reads it K-major. */

@@ -33,6 +33,7 @@ _SIGNATURES: dict[str, list] = {
     "lema_quantize_per_token": [vp, i64, i64, i64, vp, i64, vp, vp],
     "lema_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i64, i64, i64, i64, vp],
     "lema_w8a8_linear_fwd": [vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, i64, i64, i64, vp],
+    "lema_w8a8_linear_fwd_noalloc": [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, i64, vp],
     "lema_dequant_transpose": [vp, i64, vp, i64, i64, vp, i64, vp],
     "lema_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp],
     "lema_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i64, i64, vp],
