@@ -19,6 +19,7 @@
 // share the B (weight) tile through L2. A "group" is a contiguous row range of
 // A that multiplies its own B matrix (MoE experts); the dense GEMM is one group.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -67,17 +68,19 @@ __device__ __forceinline__ bool aborted(const int* abort_flag) {
   return *reinterpret_cast<const volatile int*>(abort_flag) != 0;
 }
 
-// Linear tile index -> (group, first A row, end row of the group, column tile).
+// Linear tile index -> (group, first A row, end row of the group, column tile)
+// for tiles TM rows high.
+template <int TM>
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, int& row0,
                                             int& row_end, int& n_tile) {
   g = 0;
   while (g + 1 < p.num_groups && t >= p.tile_start[g + 1]) ++g;
   const int local = t - p.tile_start[g];
   const int rows = p.row_start[g + 1] - p.row_start[g];
-  const int m_tiles = (rows + kBM - 1) / kBM;
+  const int m_tiles = (rows + TM - 1) / TM;
   const int mt = local % m_tiles;
   const int nt = local / m_tiles;
-  row0 = p.row_start[g] + mt * kBM;
+  row0 = p.row_start[g] + mt * TM;
   row_end = p.row_start[g + 1];
   n_tile = nt;
 }
@@ -92,6 +95,76 @@ struct SmemLayout {
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
 };
+
+// Epilogue of one 128-row x (NCHUNK*32)-column accumulator block held in TMEM
+// columns [col0, col0 + NCHUNK*32) of this warp's lane quarter. Row r of the
+// output is this thread's row; columns start at n0.
+template <int KIND, int NCHUNK>
+__device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem_row_base,
+                                              uint32_t col0, int r, bool rvalid, int g, int n0,
+                                              bool y_vec, bool acc_vec) {
+  float sxr = 0.f;
+  if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
+  const float* swg = (KIND == kKindI8) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
+  const __nv_bfloat16* bg = p.bias != nullptr ? p.bias + static_cast<int64_t>(g) * p.n : nullptr;
+#pragma unroll 1
+  for (int c = 0; c < NCHUNK; ++c) {
+    uint32_t v[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+    ptx::tmem_ld_32x32b_x32(tmem_row_base + col0 + static_cast<uint32_t>(c * 32), v);
+    ptx::tmem_ld_wait();
+    const int n = n0 + c * 32;
+    if (!rvalid || n >= p.n) continue;
+    const bool full_chunk = (n + 32) <= p.n;
+    if (KIND == kKindI8 && p.acc != nullptr) {
+      int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
+      if (full_chunk && acc_vec) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<uint4*>(arow + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else {
+        for (int j = 0; j < 32 && n + j < p.n; ++j) arow[j] = static_cast<int32_t>(v[j]);
+      }
+    }
+    if (p.y == nullptr) continue;
+    __align__(16) __nv_bfloat16 out[32];
+    if (KIND == kKindI8) {
+      if (full_chunk) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
+                              __ldg(swg + n + j));
+          if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+          out[j] = __float2bfloat16_rn(f);
+        }
+      } else {
+        for (int j = 0; j < 32 && n + j < p.n; ++j) {
+          float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
+                              swg[n + j]);
+          if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+          out[j] = __float2bfloat16_rn(f);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float f = __uint_as_float(v[j]);
+        if (bg != nullptr && n + j < p.n) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
+        out[j] = __float2bfloat16_rn(f);
+      }
+    }
+    __nv_bfloat16* yrow = p.y + static_cast<int64_t>(r) * p.ldy + n;
+    if (full_chunk && y_vec) {
+      const uint4* src = reinterpret_cast<const uint4*>(out);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yrow)[j] = src[j];
+    } else {
+      for (int j = 0; j < 32 && n + j < p.n; ++j) yrow[j] = out[j];
+    }
+  }
+}
+
+// ------------------------------ 1-SM kernel --------------------------------
 
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -152,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t issued = 0;  // loads issued so far; load i used stage i % STAGES
       for (int t = blockIdx.x; t < p.total_tiles && !aborted(abort_flag); t += gridDim.x) {
         int g, row0, row_end, nt;
-        decode_tile(p, t, g, row0, row_end, nt);
+        decode_tile<kBM>(p, t, g, row0, row_end, nt);
         const int b_row0 = g * p.n + nt * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
@@ -226,8 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (acc == 0) acc_phase ^= 1;
       }
       if (aborted(abort_flag) && issued_any) {
-        // Drain outstanding MMAs before TMEM is released: commit to a stage
-        // barrier whose next phase nobody else completes and wait for it.
+        // Drain outstanding MMAs before TMEM is released.
         ptx::mma_commit(&tmem_full[acc]);
         (void)ptx::mbar_wait(&tmem_full[acc], acc_phase);
       }
@@ -243,8 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       int g, row0, row_end, nt;
-      decode_tile(p, t, g, row0, row_end, nt);
-      const int n0 = nt * BN;
+      decode_tile<kBM>(p, t, g, row0, row_end, nt);
       if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
@@ -252,69 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (aborted(abort_flag)) break;
       ptx::tc_fence_after();
       const int r = row0 + quarter * 32 + lane;
-      const bool rvalid = r < row_end;
-      float sxr = 0.f;
-      if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
-      const float* swg = (KIND == kKindI8) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
-      const __nv_bfloat16* bg =
-          p.bias != nullptr ? p.bias + static_cast<int64_t>(g) * p.n : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                               static_cast<uint32_t>(acc * BN + c * 32);
-        ptx::tmem_ld_32x32b_x32(taddr, v);
-        ptx::tmem_ld_wait();
-        const int n = n0 + c * 32;
-        if (!rvalid || n >= p.n) continue;
-        const bool full_chunk = (n + 32) <= p.n;
-        if (KIND == kKindI8 && p.acc != nullptr) {
-          int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
-          if (full_chunk && acc_vec) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<uint4*>(arow + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && n + j < p.n; ++j) arow[j] = static_cast<int32_t>(v[j]);
-          }
-        }
-        if (p.y == nullptr) continue;
-        __align__(16) __nv_bfloat16 out[32];
-        if (KIND == kKindI8) {
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
-                                  __ldg(swg + n + j));
-              if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
-              out[j] = __float2bfloat16_rn(f);
-            }
-          } else {
-            for (int j = 0; j < 32 && n + j < p.n; ++j) {
-              float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
-                                  swg[n + j]);
-              if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
-              out[j] = __float2bfloat16_rn(f);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float f = __uint_as_float(v[j]);
-            if (bg != nullptr && n + j < p.n) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
-            out[j] = __float2bfloat16_rn(f);
-          }
-        }
-        __nv_bfloat16* yrow = p.y + static_cast<int64_t>(r) * p.ldy + n;
-        if (full_chunk && y_vec) {
-          const uint4* src = reinterpret_cast<const uint4*>(out);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yrow)[j] = src[j];
-        } else {
-          for (int j = 0; j < 32 && n + j < p.n; ++j) yrow[j] = out[j];
-        }
-      }
+      epilogue_rows<KIND, BN / 32>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
+                                   static_cast<uint32_t>(acc * BN), r, r < row_end, g, nt * BN,
+                                   y_vec, acc_vec);
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tmem_empty[acc]);
       acc ^= 1;
@@ -327,6 +338,204 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------ 2-SM kernel --------------------------------
+// A CTA pair (cluster of 2) computes a 256 x 256 tile with cta_group::2 MMAs
+// (M=256, N=256, K=32 bytes): CTA r loads A rows [256i + 128r, +128) and B rows
+// [256j + 128r, +128) into its own shared memory; the even (leader) CTA's
+// single MMA thread reads both CTAs' buffers, and each CTA's TMEM receives the
+// accumulators of its own 128 A rows x all 256 columns. Per SM this halves
+// the B bytes moved through L2 and shared memory compared with 128 x 256 tiles.
+//
+// Barriers: the leader's full[s] counts both CTAs' TMA bytes (the follower's
+// loads name the leader's barrier); empty[s] and tmem_full[b] exist in both
+// CTAs and receive the leader's multicast commits; the leader's tmem_empty[b]
+// collects one arrival per epilogue warp of both CTAs (8).
+
+template <int KIND, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                           const __grid_constant__ CUtensorMap tma_b,
+                           const __grid_constant__ GemmParams p) {
+  constexpr int kTM = 256, kTN = 256;
+  using L = SmemLayout<128, STAGES>;  // per CTA: 128 A rows + 128 B rows per stage
+  constexpr int kTmemCols = 2 * kTN;  // double-buffered 128 x 256 accumulators
+  constexpr int kElemsPerRow = (KIND == kKindI8) ? 128 : 64;
+  constexpr int kKStepBytes = 32;
+  constexpr uint32_t kIdesc =
+      (KIND == kKindI8) ? ptx::idesc_i8_s32(kTM, kTN) : ptx::idesc_bf16_f32(kTM, kTN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = (rank & 1u) == 0;
+  const int pair = blockIdx.x / 2;
+  const int npairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&tma_a);
+    ptx::prefetch_tmap(&tma_b);
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tmem_full[b], 1);
+      ptx::mbar_init(&tmem_empty[b], 8);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  __syncwarp();
+  ptx::cluster_sync();  // barriers of both CTAs initialised before any remote use
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      for (int t = pair; t < p.total_tiles && !aborted(abort_flag); t += npairs) {
+        int g, row0, row_end, nt;
+        decode_tile<kTM>(p, t, g, row0, row_end, nt);
+        const int a_row = row0 + static_cast<int>(rank) * 128;
+        const int b_row = g * p.n + nt * kTN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_error(p.err, kDevErrProducerTimeout, abort_flag);
+            break;
+          }
+          if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t lbar = ptx::smem_u32(&full[stage]) & ptx::kPeerBitMask;
+          ptx::tma_load_2d_pair(smem_a + stage * L::kABytes, &tma_a, lbar, kb * kElemsPerRow,
+                                a_row);
+          ptx::tma_load_2d_pair(smem_b + stage * L::kBBytes, &tma_b, lbar, kb * kElemsPerRow,
+                                b_row);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag) && leader) {
+        // The leader's full barriers count both CTAs' bytes: drain them before
+        // either CTA can pass the final cluster barrier.
+        for (int64_t i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
+          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA only) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued_any = false;
+      for (int t = pair; t < p.total_tiles && !aborted(abort_flag); t += npairs) {
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+          record_error(p.err, kDevErrMmaTimeout, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase)) {
+            record_error(p.err, kDevErrMmaTimeout, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(smem_a + stage * L::kABytes);
+          const uint32_t b_addr = ptx::smem_u32(smem_b + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kRowBytes / kKStepBytes; ++k) {
+            const uint64_t ad = ptx::desc_kmajor_sw128(a_addr + k * kKStepBytes);
+            const uint64_t bd = ptx::desc_kmajor_sw128(b_addr + k * kKStepBytes);
+            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            if (KIND == kKindI8)
+              ptx::mma_i8_pair(d_tmem, ad, bd, kIdesc, accumulate);
+            else
+              ptx::mma_bf16_pair(d_tmem, ad, bd, kIdesc, accumulate);
+          }
+          issued_any = true;
+          ptx::mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit_pair(&tmem_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (aborted(abort_flag) && issued_any) {
+        ptx::mma_commit_pair(&tmem_full[acc], 0x1);
+        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool y_vec = p.y != nullptr && (p.ldy % 8) == 0 &&
+                       (reinterpret_cast<uintptr_t>(p.y) & 15u) == 0;
+    const bool acc_vec = p.acc != nullptr && (p.ldacc % 4) == 0 &&
+                         (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
+    const uint32_t leader_tmem_empty0 = ptx::mapa_shared(ptx::smem_u32(&tmem_empty[0]), rank & ~1u);
+    for (int t = pair; t < p.total_tiles; t += npairs) {
+      int g, row0, row_end, nt;
+      decode_tile<kTM>(p, t, g, row0, row_end, nt);
+      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
+        record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
+        break;
+      }
+      if (aborted(abort_flag)) break;
+      ptx::tc_fence_after();
+      const int r = row0 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      epilogue_rows<KIND, kTN / 32>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
+                                    static_cast<uint32_t>(acc * kTN), r, r < row_end, g,
+                                    nt * kTN, y_vec, acc_vec);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(leader_tmem_empty0 + static_cast<uint32_t>(acc * 8));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncwarp();
+  ptx::cluster_sync();  // both CTAs done with TMEM, remote arrivals and loads
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -388,6 +597,64 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
   return LEMA_OK;
 }
 
+constexpr int kPairStages = 6;
+
+// Pairs (clusters of 2 CTAs, 1 CTA per SM) the device can keep resident.
+template <int KIND>
+int pair_slots() {
+  using L = SmemLayout<128, kPairStages>;
+  auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
+  static int cache[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return 0;
+  if (cache[dev] == 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (device_sm_count() / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = device_sm_count() / 2;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+template <int KIND>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
+                cudaStream_t stream) {
+  using L = SmemLayout<128, kPairStages>;
+  auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
+  const int slots = pair_slots<KIND>();
+  if (slots <= 0) return set_error(LEMA_ERR_CUDA, "cannot size the CTA-pair grid");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * std::min(p.total_tiles, slots));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, p));
+  return LEMA_OK;
+}
+
 int32_t* gemm_err_ptr() {
   int32_t* ptr = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_gemm_err) != cudaSuccess)
@@ -399,6 +666,31 @@ struct Groups {
   int num = 0;
   int64_t row_start[kMaxGroups + 1];
 };
+
+enum TilePath { kPath1Sm128 = 0, kPath1Sm256 = 1, kPathPair = 2 };
+
+// Tile path: LEMA_GEMM_TILE=1sm128|1sm256|pair forces one (tests, tuning);
+// otherwise the pair kernel (256 x 256 per CTA pair) when its tiles fill the
+// resident pairs, else 128 x 256 when those fill the SMs, else 128 x 128.
+int choose_path(int kind, const Groups& groups, int64_t n) {
+  const char* env = std::getenv("LEMA_GEMM_TILE");
+  if (env != nullptr) {
+    if (std::strcmp(env, "1sm128") == 0) return kPath1Sm128;
+    if (std::strcmp(env, "1sm256") == 0) return kPath1Sm256;
+    if (std::strcmp(env, "pair") == 0) return kPathPair;
+  }
+  auto m_tiles = [&](int tm) {
+    int64_t t = 0;
+    for (int g = 0; g < groups.num; ++g)
+      t += (groups.row_start[g + 1] - groups.row_start[g] + tm - 1) / tm;
+    return t;
+  };
+  const int sms = device_sm_count();
+  const int slots = kind == kKindI8 ? pair_slots<kKindI8>() : pair_slots<kKindBF16>();
+  if (slots > 0 && n > 128 && m_tiles(256) * ((n + 255) / 256) >= slots) return kPathPair;
+  if (n > 128 && m_tiles(128) * ((n + 255) / 256) >= sms) return kPath1Sm256;
+  return kPath1Sm128;
+}
 
 // Shared front end of the dense, grouped and bf16 GEMMs.
 int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
@@ -426,8 +718,7 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
 
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
-  const int num_kb = static_cast<int>((k * elem + kRowBytes - 1) / kRowBytes);
-  p.num_kb = num_kb;
+  p.num_kb = static_cast<int>((k * elem + kRowBytes - 1) / kRowBytes);
   p.n = static_cast<int32_t>(n);
   p.num_groups = groups.num;
   p.sx = sx;
@@ -440,18 +731,15 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   p.err = gemm_err_ptr();
   if (p.err == nullptr) return set_error(LEMA_ERR_CUDA, "cannot resolve device error word");
 
-  // Tile shape: 128 x 256 when that already fills the machine, else 128 x 128.
-  const int sms = device_sm_count();
-  int64_t m_tiles_total = 0;
-  for (int g = 0; g < groups.num; ++g)
-    m_tiles_total += (groups.row_start[g + 1] - groups.row_start[g] + kBM - 1) / kBM;
-  const int bn = (m_tiles_total * ((n + 255) / 256) >= sms && n > 128) ? 256 : 128;
-  p.num_n_tiles = static_cast<int32_t>((n + bn - 1) / bn);
+  const int path = choose_path(kind, groups, n);
+  const int tm = path == kPathPair ? 256 : 128;
+  const int tn = path == kPath1Sm128 ? 128 : 256;
+  p.num_n_tiles = static_cast<int32_t>((n + tn - 1) / tn);
   int64_t tiles = 0;
   for (int g = 0; g < groups.num; ++g) {
     p.row_start[g] = static_cast<int32_t>(groups.row_start[g]);
     p.tile_start[g] = static_cast<int32_t>(tiles);
-    const int64_t mt = (groups.row_start[g + 1] - groups.row_start[g] + kBM - 1) / kBM;
+    const int64_t mt = (groups.row_start[g + 1] - groups.row_start[g] + tm - 1) / tm;
     tiles += mt * p.num_n_tiles;
   }
   p.row_start[groups.num] = static_cast<int32_t>(rows);
@@ -462,18 +750,21 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
 
   const CUtensorMapDataType dt =
       (kind == kKindI8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int b_box = path == kPath1Sm256 ? 256 : 128;
   CUtensorMap ma, mb;
   int rc = make_operand_map(&ma, a, dt, elem, rows, k, lda, kBM);
   if (rc) return rc;
-  rc = make_operand_map(&mb, b, dt, elem, n * groups.num, k, ldb, bn);
+  rc = make_operand_map(&mb, b, dt, elem, n * groups.num, k, ldb, b_box);
   if (rc) return rc;
 
   if (kind == kKindI8) {
-    return bn == 256 ? launch<kKindI8, 256, 4>(ma, mb, p, stream)
-                     : launch<kKindI8, 128, 6>(ma, mb, p, stream);
+    if (path == kPathPair) return launch_pair<kKindI8>(ma, mb, p, stream);
+    return path == kPath1Sm256 ? launch<kKindI8, 256, 4>(ma, mb, p, stream)
+                               : launch<kKindI8, 128, 6>(ma, mb, p, stream);
   }
-  return bn == 256 ? launch<kKindBF16, 256, 4>(ma, mb, p, stream)
-                   : launch<kKindBF16, 128, 6>(ma, mb, p, stream);
+  if (path == kPathPair) return launch_pair<kKindBF16>(ma, mb, p, stream);
+  return path == kPath1Sm256 ? launch<kKindBF16, 256, 4>(ma, mb, p, stream)
+                             : launch<kKindBF16, 128, 6>(ma, mb, p, stream);
 }
 
 // y = bias (or 0) broadcast over rows: the K == 0 case.

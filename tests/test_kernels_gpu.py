@@ -239,3 +239,72 @@ def test_ckpt_kernel_mode_rejects_pageable_memory(cuda_device):
     host = torch.zeros(64)  # pageable
     with pytest.raises(N.LemaError):
         N.call("lema_ckpt_save", src.data_ptr(), host.data_ptr(), 256, 1, None, None, None)
+
+
+# --------------------------------------------------------------------------- tile paths
+# Every GEMM tile path (1-SM 128x128, 1-SM 128x256, CTA-pair 256x256) against
+# the oracle, forced with LEMA_GEMM_TILE.
+
+PATH_SHAPES = [(300, 520, 4112), (1000, 768, 640), (4096, 4096, 4096), (64, 256, 128)]
+
+
+@pytest.mark.parametrize("path", ["1sm128", "1sm256", "pair"])
+@pytest.mark.parametrize("M,N,K", PATH_SHAPES)
+def test_gemm_tile_paths_bitexact(cuda_device, oracle, monkeypatch, path, M, N, K):
+    monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+    sx = torch.rand(M, device=dev, generator=g) * 0.01 + 1e-4
+    sw = torch.rand(N, device=dev, generator=g) * 1e-3 + 1e-5
+    bias = (torch.randn(N, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    y, acc = ops.w8a8_gemm(a, sx, b, sw, bias=bias, want_acc=True)
+    an, bn = a.cpu().numpy(), b.cpu().numpy()
+    if M * N * K <= 2 ** 31:
+        ref = oracle.c_int8_gemm(an, bn)
+        np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+    else:
+        rs, cs = oracle.c_int8_gemm_checksums(an, bn)
+        np.testing.assert_array_equal(acc.long().sum(1).cpu().numpy(), rs)
+        np.testing.assert_array_equal(acc.long().sum(0).cpu().numpy(), cs)
+        ref = acc.cpu().numpy()
+        blk = oracle.c_int8_gemm(an[3900:4096], bn[3800:4096])
+        np.testing.assert_array_equal(ref[3900:4096, 3800:4096], blk)
+    yref = oracle.c_epilogue(acc.cpu().numpy(), sx.cpu().numpy(), sw.cpu().numpy(), bits(bias))
+    np.testing.assert_array_equal(bits(y), yref)
+
+
+@pytest.mark.parametrize("path", ["1sm128", "1sm256", "pair"])
+def test_bf16_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
+    monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    dev = cuda_device
+    a = rand_bf16((600, 1040), seed=31, outliers=False)
+    b = rand_bf16((520, 1040), seed=32, outliers=False)
+    y = ops.bf16_gemm_tn(a.to(dev), b.to(dev))
+    _, ref = oracle.c_bf16_gemm_tn(bits(a), bits(b))
+    _dgrad_tol_check(bits(y), ref)
+
+
+@pytest.mark.parametrize("path", ["1sm128", "pair"])
+def test_grouped_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
+    monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    dev = cuda_device
+    E, N, K = 4, 512, 384
+    counts = [300, 0, 513, 77]
+    offsets = np.concatenate([[0], np.cumsum(counts)]).tolist()
+    T = offsets[-1]
+    g = torch.Generator(device=dev).manual_seed(41)
+    xq = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=dev, generator=g)
+    sx = torch.rand(T, device=dev, generator=g) * 0.01 + 1e-4
+    wq = torch.randint(-127, 128, (E, N, K), dtype=torch.int8, device=dev, generator=g)
+    sw = torch.rand(E, N, device=dev, generator=g) * 1e-3 + 1e-5
+    y = ops.grouped_w8a8_gemm(xq, sx, wq, sw, offsets)
+    xqn, sxn, wqn, swn = (t.cpu().numpy() for t in (xq, sx, wq, sw))
+    for e in range(E):
+        r0, r1 = offsets[e], offsets[e + 1]
+        if r1 == r0:
+            continue
+        acc = oracle.c_int8_gemm(xqn[r0:r1], wqn[e])
+        ref = oracle.c_epilogue(acc, sxn[r0:r1], swn[e], None)
+        np.testing.assert_array_equal(bits(y[r0:r1].contiguous()), ref, err_msg=f"expert {e}")
