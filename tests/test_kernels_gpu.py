@@ -74,6 +74,33 @@ def test_quantize_rows_strided_and_f32(cuda_device, oracle):
     np.testing.assert_array_equal(s.cpu().numpy(), sr)
 
 
+def test_quantize_adversarial_rows(cuda_device, oracle):
+    """Rows whose quotients x / s sit on or near half-integers, and rows with
+    subnormal scales: the device quotient must round exactly like the oracle's
+    IEEE division."""
+    allbits = np.arange(65536, dtype=np.uint32)
+    f = (allbits << 16).view(np.float32)
+    f = f[np.isfinite(f)]
+    rng = np.random.default_rng(7)
+    pos = np.unique(np.abs(f[f != 0]))
+    amaxes = np.concatenate([pos[:24], pos[-8:], rng.choice(pos, 80, replace=False),
+                             np.float32([1.0, 127.0, 254.0, 2.0, 0.5, 63.5])])
+    rows = []
+    for amax in amaxes.astype(np.float32):
+        cand = f[np.abs(f) <= amax]
+        row = rng.choice(cand, 4095, replace=True).astype(np.float32)
+        rows.append(np.concatenate([[amax], row]))
+    # exact ties: s = 1 (amax 127) and s = 2 (amax 254) with k + 0.5 values
+    ties = np.float32([127.0] + [k + 0.5 for k in range(-127, 127)] + [0.0] * 3841)
+    rows.append(ties)
+    rows.append(ties * 2)
+    x = torch.from_numpy(np.stack(rows)).to(torch.bfloat16)
+    q, s = ops.quantize_rows(x.to(cuda_device))
+    qr, sr = oracle.c_quantize_rows(bits(x))
+    np.testing.assert_array_equal(s.cpu().numpy(), sr)
+    np.testing.assert_array_equal(q.cpu().numpy(), qr)
+
+
 def test_quantize_empty(cuda_device):
     x = torch.empty(0, 64, dtype=torch.bfloat16, device=cuda_device)
     q, s = ops.quantize_rows(x)
