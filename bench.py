@@ -1,6 +1,14 @@
 """Benchmark of the W8A8 hot path on B200 (one JSON line on stdout).
 
 Workloads (``--workload``):
+  llama7b_streamed_lora (default)
+                    one LoRA training step of the 32-layer Llama-2-7B-shaped
+                    model (random init, vocab 32000, all seven projections
+                    W8A8, LoRA r16 alpha 32 on q/v) on bs=8 x seq=512 tokens
+                    per GPU: int8 weight segments streamed from pinned host
+                    RAM per layer, boundary activations offloaded to pinned
+                    host and restored for the recompute, data-parallel LoRA
+                    gradient all-reduce (NCCL) for N > 1. Metric: tokens/s.
   w8a8_linear_4096  one W8A8 linear forward step (K1 quantise + K2/K3 GEMM with
                     fused epilogue) at M=N=K=4096, the per-layer shape of the
                     7B streamed model at bs=8 x seq=512. Metric: int8 TOPS.
@@ -9,8 +17,9 @@ Contract: ``python bench.py --gpus N --steps K --warmup W`` (N>1 under torchrun,
 one rank per GPU, replicas: each rank runs the same step on its own data, no
 collective on the data path). W warm-up steps, then K timed steps bracketed by
 barrier + synchronize; the device time is the max over ranks. ``--impl
-reference`` times the CPU restatement of the path (there is no reference
-implementation of a W8A8 linear to run) on the host cores instead.
+reference`` times the CPU restatement of the path (the reference has no W8A8
+implementation to run, and its Python package is not installed on the GPU
+host) on the host cores instead.
 """
 from __future__ import annotations
 
@@ -300,6 +309,181 @@ def run_linear(args, world, rank, local) -> dict | None:
     return res
 
 
+# ---------------------------------------------------------------------------
+# GPU workload: one streamed LoRA training step of the 7B-shaped model
+# ---------------------------------------------------------------------------
+
+def measure_h2d_gbs(dev, nbytes=1 << 30) -> float:
+    """Pinned host -> device copy bandwidth of this GPU (one 1 GiB copy, best of 3)."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = float("inf")
+    for _ in range(3):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(src, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return nbytes / (best / 1e3) / 1e9
+
+
+def cpu_train_sample(seq: int, threads: int) -> dict:
+    """CPU restatement of one streamed layer's work (no-grad forward, recompute
+    with grad, backward) on one Llama-2-7B-shaped block with the oracle's W8A8
+    linears, LoRA r16 on q/v, for `seq` tokens; scaled to the 32-layer model
+    (the embedding/head are not included)."""
+    from lema_b200.llama import LlamaBlock, LlamaShape, apply_lora, rope_cos_sin
+    from oracle import oracle as O
+    from oracle.torch_ref import swap_linears
+    torch.set_num_threads(threads)
+    O.set_threads(threads)
+    shape = LlamaShape()
+    g = torch.Generator().manual_seed(0)
+    blk = LlamaBlock(shape, quantized=False, device="cpu")
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if "layernorm" not in name:
+                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+    apply_lora(blk, 16, 32.0)
+    swap_linears(blk)
+    blk.self_attn.attn_impl = "eager"
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+        blk.base_projection(name).wdeq_f32()  # frozen weights: dequantised once, outside timing
+    x = torch.randn(1, seq, shape.hidden, generator=g).to(torch.bfloat16)
+    dy = torch.randn(1, seq, shape.hidden, generator=g).to(torch.bfloat16)
+    cos, sin = rope_cos_sin(shape, seq, "cpu", torch.bfloat16)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        blk(x, cos, sin)
+    xr = x.clone().requires_grad_(True)
+    blk(xr, cos, sin).backward(dy)
+    t_layer = time.perf_counter() - t0
+    return {"tokens_per_s": seq / (shape.layers * t_layer), "seconds_per_layer": t_layer,
+            "sample": f"1 Llama-2-7B-shaped layer, {seq} tokens, no-grad forward + recompute + "
+                      f"backward through the oracle W8A8 linears ({t_layer:.2f} s), scaled x32 "
+                      "layers (embedding / lm_head excluded)"}
+
+
+def run_train(args, world, rank, local) -> dict | None:
+    from lema_b200 import _native, ops
+    from lema_b200.llama import LlamaShape
+    from lema_b200.trainer import StreamedLoraTrainer
+
+    dev = torch.device("cuda", local)
+    shape = LlamaShape()
+    batch, seq = 8, 512
+    tokens_per_step = batch * seq
+    tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16, lora_alpha=32.0,
+                             seed=0, resident_layers=args.resident_layers)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    n_batches = 4
+    ids_dev = [torch.randint(0, shape.vocab, (batch, seq), device=dev, generator=gen)
+               for _ in range(n_batches)]
+    for i in range(args.warmup):
+        tr.train_step(ids_dev[i % n_batches])
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ops.GemmTimer.enable(True)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    losses = []
+    for i in range(args.steps):
+        losses.append(tr.train_step(ids_dev[i % n_batches]))
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    gemm_ops, gemm_ms, gemm_launches = ops.GemmTimer.summary()
+    ops.GemmTimer.enable(False)
+    ms = t0.elapsed_time(t1)
+    ms_max = max_over_ranks(ms, world)
+    dev_err = _native.device_error()
+    if dev_err:
+        raise RuntimeError(f"kernel device error word {dev_err:#x}")
+    # end to end: token ids from pinned host memory every step, loss read back
+    ids_host = [t.cpu().pin_memory() for t in ids_dev]
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        loss = tr.train_step(ids_host[i % n_batches])
+        loss_val = float(loss.item())
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    h2d_gbs = measure_h2d_gbs(dev)
+    seg_bytes = tr.ws.seg_bytes
+    streamed = shape.layers - args.resident_layers
+    h2d_per_step = (2 * streamed - min(2, streamed)) * seg_bytes + \
+        tr.ckpt.nbytes * shape.layers
+    d2h_per_step = tr.ckpt.nbytes * shape.layers
+    tr.close()
+    if rank != 0:
+        return None
+    value = tokens_per_step * world * args.steps / (ms_max / 1e3)
+    e2e_value = tokens_per_step * world * args.steps / (e2e_ms / 1e3)
+    int8_peak = args.int8_peak_tops or measure_int8_peak(dev)
+    achieved = gemm_ops / (gemm_ms / 1e3) / 1e12
+    step_s = ms_max / 1e3 / args.steps
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s (whole job)",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 W8A8 projections (bf16 activations; bf16 attention, LoRA, lm_head)",
+        "data": "synthetic (random-init Llama-2-7B-shaped weights, token ids uniform in "
+                "[0, 32000), labels = inputs)",
+        "config": {"workload": "llama7b_streamed_lora: 32 x [hidden 4096, 32x128 heads, MLP "
+                               "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections "
+                               "streamed from pinned RAM, activation checkpoints offloaded",
+                   "global_batch": batch * world, "seq_len": seq,
+                   "parallelism": f"dp{world}",
+                   "resident_layers": args.resident_layers,
+                   "l2": "per-step weight stream 12.9 GB and activations >> L2"},
+        "gpu_launches": 42 * shape.layers * args.steps,
+        "loss_last": round(float(losses[-1]), 4),
+        "roofline": {"bound": "tensor", "kernel": "gemm_sm100 int8 (all W8A8 projection GEMMs "
+                                                  "of the timed steps)",
+                     "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
+                     "frac": round(achieved / int8_peak, 4),
+                     "peak_source": "measured cuBLASLt int8 GEMM (torch._int_mm 8192^3, burst)",
+                     "frac_of_spec_4500": round(achieved / INT8_SPEC_TOPS, 4),
+                     "traffic": None, "gemm_launches": gemm_launches,
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "algorithmic_ops_per_step": gemm_ops / args.steps},
+        "pcie": {"h2d_gbs_measured": round(h2d_gbs, 1),
+                 "h2d_bytes_per_step": h2d_per_step, "d2h_bytes_per_step": d2h_per_step,
+                 "h2d_bound_ms": round(h2d_per_step / (h2d_gbs * 1e9) * 1e3, 2),
+                 "h2d_frac_of_step": round(h2d_per_step / (h2d_gbs * 1e9) / step_s, 3)},
+        "clocks": clk,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s (whole job)",
+                "h2d_bytes_per_step": batch * seq * 8, "d2h_bytes_per_step": 4,
+                "path": "StreamedLoraTrainer.train_step(ids in pinned host memory) + loss.item()"},
+    }
+    if not args.skip_cpu:
+        threads = os.cpu_count() or 1
+        c = cpu_train_sample(args.cpu_seq, threads)
+        res["cpu_baseline"] = {"value": round(c["tokens_per_s"], 3), "unit": "tokens/s",
+                               "cores": threads, "kind": "port", "sample": c["sample"]}
+    return res
+
+
 def measure_int8_peak(dev) -> float:
     """Burst throughput of cuBLASLt's int8 GEMM (torch._int_mm) at 8192^3."""
     n = 8192
@@ -322,29 +506,45 @@ def measure_int8_peak(dev) -> float:
 
 
 def run_reference(args) -> dict | None:
-    """CPU arm: the oracle restatement of the W8A8 forward on all host threads."""
+    """CPU arm: the oracle restatement of the path on all host threads."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.workload == "llama7b_streamed_lora":
+        vals = [cpu_train_sample(args.cpu_seq, threads) for _ in range(args.steps)]
+        tps = statistics.median(v["tokens_per_s"] for v in vals)
+        return {
+            "metric": METRIC, "impl": "reference", "value": round(tps, 3),
+            "unit": "tokens/s (whole job)", "n_gpus": world, "steps": args.steps,
+            "warmup": 0, "ms_per_step": round(8 * 512 / tps * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 W8A8 projections (bf16 activations)", "data": "synthetic",
+            "config": {"workload": "llama7b_streamed_lora (per-layer CPU sample, scaled)",
+                       "global_batch": 8, "seq_len": 512, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads,
+                             "kind": "port", "sample": vals[0]["sample"]},
+            "e2e": {"value": round(tps, 3), "unit": "tokens/s (whole job)",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference has no W8A8 path; the CPU restatement in oracle/ is timed",
+        }
     M = N = K = 4096
-    vals = []
     for _ in range(max(1, args.warmup)):
         cpu_linear_sample(M, N, K, rows=args.cpu_rows, reps=1, threads=threads)
-    for _ in range(args.steps):
-        vals.append(cpu_linear_sample(M, N, K, rows=args.cpu_rows, reps=1, threads=threads))
+    vals = [cpu_linear_sample(M, N, K, rows=args.cpu_rows, reps=1, threads=threads)
+            for _ in range(args.steps)]
     tops = statistics.median(v["tops"] for v in vals)
-    sample = vals[0]["sample"]
     return {
         "metric": METRIC, "impl": "reference", "value": round(tops, 4),
-        "unit": "TOPS (int8, whole job)", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-        "steps": args.steps, "warmup": args.warmup,
+        "unit": "TOPS (int8, whole job)", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup,
         "ms_per_step": round(statistics.median(v["seconds"] for v in vals) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 x int8 -> s32 -> bf16", "data": "synthetic",
         "config": {"workload": "w8a8_linear_4096 (row sample on CPU)", "M": M, "N": N, "K": K},
         "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": vals[0]["sample"]},
         "e2e": {"value": round(tops, 4), "unit": "TOPS (int8, whole job)",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no W8A8 linear; the CPU restatement in oracle/ is timed",
@@ -354,15 +554,24 @@ def run_reference(args) -> dict | None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="w8a8_linear_4096")
+    ap.add_argument("--workload", default="llama7b_streamed_lora",
+                    choices=["llama7b_streamed_lora", "w8a8_linear_4096"])
+    ap.add_argument("--resident-layers", type=int, default=0,
+                    help="keep this many blocks' int8 segments resident in HBM")
+    ap.add_argument("--cpu-seq", type=int, default=128)
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--int8-peak-tops", type=float, default=0.0)
     args = ap.parse_args()
-    if args.warmup < 3:
+    train = args.workload == "llama7b_streamed_lora"
+    if args.steps is None:
+        args.steps = (3 if args.impl == "reference" else 10) if train else 50
+    if args.warmup is None:
+        args.warmup = 3 if train else 5
+    if args.warmup < 3 and args.impl != "reference":
         args.warmup = 3
     if args.impl == "reference":
         res = run_reference(args)
@@ -374,7 +583,7 @@ def main():
         if args.workload == "w8a8_linear_4096":
             res = run_linear(args, world, rank, local)
         else:
-            raise SystemExit(f"unknown workload {args.workload}")
+            res = run_train(args, world, rank, local)
         if res is not None:
             print(json.dumps(res), flush=True)
     finally:

@@ -24,6 +24,29 @@ import torch
 from . import _native as N
 
 
+class GemmTimer:
+    """Optional CUDA-event bracketing of every int8 GEMM launch (for the bench):
+    records (start, end, ops) on the launching stream. Off unless ``enable()``."""
+
+    enabled = False
+    records: list = []
+
+    @classmethod
+    def enable(cls, on: bool = True) -> None:
+        cls.enabled = on
+        cls.records = []
+
+    @classmethod
+    def summary(cls) -> tuple[float, float, int]:
+        """(total ops, total ms, launches) over the recorded GEMMs (synchronises)."""
+        ops_, ms = 0.0, 0.0
+        for e0, e1, n in cls.records:
+            e1.synchronize()
+            ms += e0.elapsed_time(e1)
+            ops_ += n
+        return ops_, ms, len(cls.records)
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -165,8 +188,20 @@ def w8a8_linear_forward(x2d: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
     y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
     if bias is not None:
         bias = bias.contiguous().to(torch.bfloat16)
-    N.call("lema_w8a8_linear_fwd", _ptr(x2d), _ld(x2d), _ptr(wq), _ld(wq), _ptr(sw),
-           _ptr(bias), _ptr(y), Nn, _ptr(xq), ldq, _ptr(sx), M, Nn, K, _stream(dev))
+    stream = _stream(dev)
+    if not GemmTimer.enabled:
+        N.call("lema_w8a8_linear_fwd", _ptr(x2d), _ld(x2d), _ptr(wq), _ld(wq), _ptr(sw),
+               _ptr(bias), _ptr(y), Nn, _ptr(xq), ldq, _ptr(sx), M, Nn, K, stream)
+        return y
+    N.call("lema_quantize_rows", _ptr(x2d), M, K, _ld(x2d), _ptr(xq), ldq, _ptr(sx), stream)
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    N.call("lema_w8a8_gemm", _ptr(xq), ldq, _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), _ptr(bias),
+           _ptr(y), Nn, None, Nn, M, Nn, K, stream)
+    e1.record(s)
+    GemmTimer.records.append((e0, e1, 2.0 * M * Nn * K))
     return y
 
 

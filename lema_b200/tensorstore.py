@@ -1,0 +1,190 @@
+"""Pinned-host streams of the streamed trainer: boundary-activation checkpoints
+(A5) and int8 weight segments (A7).
+
+``ActivationCheckpointStore`` replaces the VRAM-resident
+``boundary_activations`` list of ``LemaTrainer.train_step``
+(src/lema/_trainer.py:109-111 save, :146-148 restore): each layer's input is
+copied into a pinned host slot on a D2H copy stream right after it is produced
+(``lema_ckpt_save``, copy engine or SM store kernel), overlapping the next
+layer's compute and weight upload; in backward it is copied back on the H2D
+stream ahead of the layer's re-forward (``lema_ckpt_restore``). Ordering is by
+CUDA events only — the host never blocks.
+
+``WeightSegments`` holds every block's int8 weights, fp32 scales and bf16
+norm weights as one 128-byte-aligned segment per block in pinned host memory
+(the RAM side of the reference's ``_TransferEngine``, src/lema/_tensorstore.py:
+213-302) and streams segments into two VRAM slots through the native memory
+manager (``lema_mm_*``), binding W8A8Linear weights as views of the slot
+instead of copying them into parameters (src/lema/adapters/_llama.py:95-100).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+from .llama import PROJECTIONS, LlamaBlock, LlamaShape
+
+
+def _ev_ptr(ev: torch.cuda.Event | None):
+    return None if ev is None else C.c_void_p(ev.cuda_event)
+
+
+class ActivationCheckpointStore:
+    """``num`` pinned host slots of ``shape`` (bf16 by default)."""
+
+    def __init__(self, num: int, shape: tuple[int, ...], device: torch.device,
+                 dtype: torch.dtype = torch.bfloat16, mode: int = 0,
+                 h2d_stream: torch.cuda.Stream | None = None):
+        self.device = torch.device(device)
+        self.shape = tuple(shape)
+        self.dtype = dtype
+        self.mode = mode
+        self.host = torch.empty((num, *shape), dtype=dtype).pin_memory()
+        self.nbytes = self.host[0].numel() * self.host.element_size()
+        self.d2h = torch.cuda.Stream(device=self.device)
+        self.h2d = h2d_stream if h2d_stream is not None else torch.cuda.Stream(device=self.device)
+        self.saved = [torch.cuda.Event() for _ in range(num)]
+        self.restored = [torch.cuda.Event() for _ in range(num)]
+        self._dev_buf: dict[int, torch.Tensor] = {}
+
+    def save(self, i: int, t: torch.Tensor) -> None:
+        """Copies device tensor ``t`` into slot i once the current stream has produced it."""
+        if tuple(t.shape) != self.shape or t.dtype != self.dtype:
+            raise ValueError(f"checkpoint slot holds {self.shape} {self.dtype}, got "
+                             f"{tuple(t.shape)} {t.dtype}")
+        t = t.detach()
+        if not t.is_contiguous():
+            t = t.contiguous()
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        N.call("lema_ckpt_save", t.data_ptr(), self.host[i].data_ptr(), self.nbytes, self.mode,
+               self.d2h.cuda_stream, _ev_ptr(ready), _ev_ptr(self.saved[i]))
+        t.record_stream(self.d2h)  # the caching allocator keeps t alive until the copy ends
+
+    def restore_async(self, i: int) -> torch.Tensor:
+        """Starts the H2D copy of slot i into a device buffer and returns the buffer;
+        call ``wait(i)`` on the consuming stream before reading it."""
+        buf = torch.empty(self.shape, dtype=self.dtype, device=self.device)
+        # buf's memory may still be read by earlier work on the allocating stream:
+        # the copy stream starts only after that point.
+        self.h2d.wait_stream(torch.cuda.current_stream(self.device))
+        N.call("lema_ckpt_restore", self.host[i].data_ptr(), buf.data_ptr(), self.nbytes,
+               self.h2d.cuda_stream, _ev_ptr(self.saved[i]), _ev_ptr(self.restored[i]))
+        buf.record_stream(self.h2d)
+        self._dev_buf[i] = buf
+        return buf
+
+    def wait(self, i: int, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        s = stream or torch.cuda.current_stream(self.device)
+        s.wait_event(self.restored[i])
+        return self._dev_buf.pop(i)
+
+    def restore(self, i: int) -> torch.Tensor:
+        self.restore_async(i)
+        return self.wait(i)
+
+
+@dataclass
+class _Seg:
+    offset: int
+    nbytes: int
+    shape: tuple[int, ...]
+    dtype: torch.dtype
+
+
+class WeightSegments:
+    """All blocks' int8 segments in pinned RAM + two VRAM slots fed by the native
+    manager's H2D copy stream."""
+
+    ALIGN = 128
+
+    def __init__(self, shape: LlamaShape, num_blocks: int, device: torch.device):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.num_blocks = num_blocks
+        self.layout: dict[str, _Seg] = {}
+        off = 0
+
+        def add(name, shp, dtype):
+            nonlocal off
+            nb = int(torch.Size(shp).numel()) * torch.empty((), dtype=dtype).element_size()
+            self.layout[name] = _Seg(off, nb, tuple(shp), dtype)
+            off = (off + nb + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+
+        for name, (o, i) in shape.proj_shapes().items():
+            add(name + ".wq", (o, i), torch.int8)
+            add(name + ".sw", (o,), torch.float32)
+        add("input_layernorm", (shape.hidden,), torch.bfloat16)
+        add("post_attention_layernorm", (shape.hidden,), torch.bfloat16)
+        self.seg_bytes = off
+        self.ram = torch.empty(num_blocks, self.seg_bytes, dtype=torch.uint8).pin_memory()
+        self.vram = [torch.empty(self.seg_bytes, dtype=torch.uint8, device=self.device)
+                     for _ in range(2)]
+        self.mm = C.c_void_p()
+        dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        N.call("lema_mm_create", num_blocks + 2, self.seg_bytes, dev_index, C.byref(self.mm))
+        for b in range(num_blocks):
+            N.call("lema_mm_register_ram_buffer", self.mm, b, self.ram[b].data_ptr(),
+                   self.seg_bytes)
+        for s in range(2):
+            N.call("lema_mm_register_vram_slot", self.mm, s, self.vram[s].data_ptr(),
+                   self.seg_bytes)
+        sp = C.c_void_p()
+        N.call("lema_mm_copy_stream", self.mm, C.byref(sp))
+        self.h2d_stream = torch.cuda.ExternalStream(sp.value, device=self.device)
+        self._pending: dict[int, int] = {}
+
+    def close(self) -> None:
+        if self.mm:
+            N.call("lema_mm_destroy", self.mm)
+            self.mm = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- filling RAM (pack time) -------------------------------------------
+    def _view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        seg = self.layout[name]
+        raw = buf[seg.offset: seg.offset + seg.nbytes]
+        return raw.view(seg.dtype).view(seg.shape)
+
+    def pack_block(self, b: int, tensors: dict[str, torch.Tensor]) -> None:
+        """Writes one block's quantised tensors (device or host) into RAM segment b."""
+        ram = self.ram[b]
+        for name, t in tensors.items():
+            self._view(ram, name).copy_(t.detach().reshape(self.layout[name].shape))
+
+    # ---- streaming -----------------------------------------------------------
+    def upload(self, b: int, slot: int) -> None:
+        """Starts the H2D of block b's segment into VRAM slot ``slot`` (the copy
+        stream first waits until compute released that slot)."""
+        ev = C.c_int64(-1)
+        N.call("lema_mm_async_transfer_to_vram", self.mm, b, slot, 0, C.byref(ev))
+        self._pending[slot] = ev.value
+
+    def acquire(self, slot: int, stream: torch.cuda.Stream | None = None) -> None:
+        """Makes the compute stream wait (on the device) for slot's upload."""
+        s = stream or torch.cuda.current_stream(self.device)
+        ev = self._pending.pop(slot, -1)
+        if ev >= 0:
+            N.call("lema_mm_stream_wait_transfer", self.mm, ev, s.cuda_stream)
+
+    def release(self, slot: int, stream: torch.cuda.Stream | None = None) -> None:
+        """Records that compute on ``stream`` is done reading ``slot``."""
+        s = stream or torch.cuda.current_stream(self.device)
+        N.call("lema_mm_release_vram_slot", self.mm, slot, s.cuda_stream)
+
+    def bind(self, block: LlamaBlock, slot: int) -> None:
+        """Binds a block's W8A8 projections and norms to views of VRAM slot ``slot``."""
+        buf = self.vram[slot]
+        for name in PROJECTIONS:
+            block.base_projection(name).bind(self._view(buf, name + ".wq"),
+                                             self._view(buf, name + ".sw"))
+        block.input_layernorm.weight.data = self._view(buf, "input_layernorm")
+        block.post_attention_layernorm.weight.data = self._view(buf, "post_attention_layernorm")

@@ -1,0 +1,219 @@
+"""Layer-streamed LoRA training over W8A8 decoder blocks.
+
+``StreamedLoraTrainer.train_step`` follows ``LemaTrainer.train_step``
+(src/lema/_trainer.py:75-194) step for step, on the B200 data path:
+
+* forward, no grad (reference :93-116): block i's int8 segment is uploaded
+  from pinned RAM into one of two VRAM slots by the native manager's copy
+  stream while block i-1 computes; the block's W8A8 projections are bound to
+  views of the slot (no parameter copy, unlike src/lema/adapters/_llama.py:
+  95-100); the block's input is saved to a pinned host slot on a D2H stream
+  (reference keeps it in VRAM, :109-111);
+* head + loss (reference :151-162): final RMSNorm, bf16 lm_head, shifted
+  cross entropy, backward to the last hidden state;
+* backward in reverse (reference :125-173): the saved input is restored on the
+  H2D stream, the block is re-run with grad and back-propagated; the two
+  blocks still resident at the turnaround are reused without re-upload; each
+  finished layer's LoRA gradients start their data-parallel all-reduce
+  (NCCL) while the next layer computes;
+* optimizer (reference :183-187): clip_grad_norm_(1.0) and AdamW over the LoRA
+  parameters.
+
+Every cross-stream dependency is a CUDA event; the host never blocks on a
+transfer. The embedding and the head stay resident in HBM (they are frozen and
+small next to 180 GB); the 32 blocks stream.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .llama import PROJECTIONS, LlamaBlock, LlamaHead, LlamaShape, apply_lora, rope_cos_sin
+from .modules import LoRALinear
+from .tensorstore import ActivationCheckpointStore, WeightSegments
+
+
+class LoraGradReducer:
+    """Averages LoRA gradients over a process group, one flat fp32 bucket per
+    layer, launched asynchronously as each layer's backward finishes."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self._pending: list[tuple[object, torch.Tensor, list[torch.Tensor]]] = []
+
+    def launch(self, grads: list[torch.Tensor]) -> None:
+        if self.world == 1 or not grads:
+            return
+        flat = torch.cat([g.reshape(-1).float() for g in grads])
+        work = self.dist.all_reduce(flat, op=self.dist.ReduceOp.SUM, group=self.group,
+                                    async_op=True)
+        self._pending.append((work, flat, grads))
+
+    def finish(self) -> None:
+        for work, flat, grads in self._pending:
+            work.wait()
+            flat.div_(self.world)
+            off = 0
+            for g in grads:
+                n = g.numel()
+                g.copy_(flat[off:off + n].view_as(g))
+                off += n
+        self._pending.clear()
+
+
+class StreamedLoraTrainer:
+    def __init__(self, shape: LlamaShape, device, batch: int, seq: int, lora_rank: int = 16,
+                 lora_alpha: float = 32.0, targets: tuple[str, ...] = ("q_proj", "v_proj"),
+                 lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0, ckpt_mode: int = 0,
+                 resident_layers: int = 0, group=None):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.batch, self.seq = batch, seq
+        self.L = shape.layers
+        self.targets = targets
+        dev = self.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        # resident frozen embedding + head (HF init: normal(0, 0.02), norm weights 1)
+        self.embed = nn.Embedding(shape.vocab, shape.hidden, device=dev, dtype=torch.bfloat16)
+        self.embed.weight.requires_grad_(False)
+        with torch.no_grad():
+            self.embed.weight.normal_(0.0, 0.02, generator=g)
+        self.head = LlamaHead(shape, device=dev)
+        with torch.no_grad():
+            self.head.lm_head.weight.normal_(0.0, 0.02, generator=g)
+        for p in self.head.parameters():
+            p.requires_grad_(False)
+        # int8 segments of every block in pinned RAM (quantised once, on the device)
+        self.ws = WeightSegments(shape, self.L, dev)
+        for b in range(self.L):
+            tensors = {}
+            for name, (o, i) in shape.proj_shapes().items():
+                w = torch.empty(o, i, device=dev, dtype=torch.bfloat16).normal_(0.0, 0.02,
+                                                                                 generator=g)
+                wq, sw = ops.quantize_weight(w)
+                tensors[name + ".wq"] = wq
+                tensors[name + ".sw"] = sw
+            ones = torch.ones(shape.hidden, device=dev, dtype=torch.bfloat16)
+            tensors["input_layernorm"] = ones
+            tensors["post_attention_layernorm"] = ones
+            self.ws.pack_block(b, tensors)
+        torch.cuda.synchronize(dev)
+        # optional HBM-resident copies of the first `resident_layers` segments
+        self.resident = [self.ws.ram[b].to(dev) for b in range(min(resident_layers, self.L))]
+        # two block modules, bound per layer (the reference's module pool)
+        self.blocks = [LlamaBlock(shape, quantized=True, device=dev) for _ in range(2)]
+        for blk in self.blocks:
+            apply_lora(blk, lora_rank, lora_alpha, targets)
+        # LoRA parameters per layer, reference init (A kaiming-uniform, B zeros)
+        self.lora: list[dict[str, tuple[nn.Parameter, nn.Parameter]]] = []
+        for _ in range(self.L):
+            layer = {}
+            for name in targets:
+                o, i = shape.proj_shapes()[name]
+                a = torch.zeros(lora_rank, i, device=dev, dtype=torch.bfloat16)
+                nn.init.kaiming_uniform_(a, a=math.sqrt(5), generator=g)
+                layer[name] = (nn.Parameter(a),
+                               nn.Parameter(torch.zeros(o, lora_rank, device=dev,
+                                                        dtype=torch.bfloat16)))
+            self.lora.append(layer)
+        self.params = [p for layer in self.lora for ab in layer.values() for p in ab]
+        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=True)
+        self.ckpt = ActivationCheckpointStore(self.L, (batch, seq, shape.hidden), dev,
+                                              mode=ckpt_mode, h2d_stream=self.ws.h2d_stream)
+        self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
+        self.reducer = LoraGradReducer(group)
+        self.slot_layer = [-1, -1]
+        self.global_step = 0
+
+    # ---- weights -----------------------------------------------------------
+    def _ensure(self, layer: int) -> None:
+        """Starts the upload of ``layer`` into its slot unless it is already there."""
+        slot = layer % 2
+        if layer < len(self.resident) or self.slot_layer[slot] == layer:
+            return
+        self.ws.upload(layer, slot)
+        self.slot_layer[slot] = layer
+
+    def _bind(self, layer: int) -> LlamaBlock:
+        slot = layer % 2
+        blk = self.blocks[slot]
+        if layer < len(self.resident):
+            self._bind_resident(blk, layer)
+        else:
+            self.ws.acquire(slot)
+            self.ws.bind(blk, slot)
+        for name, (a, b) in self.lora[layer].items():
+            m = blk.projection(name)
+            m.lora_A = a
+            m.lora_B = b
+        return blk
+
+    def _bind_resident(self, blk: LlamaBlock, layer: int) -> None:
+        buf = self.resident[layer]
+        for name in PROJECTIONS:
+            blk.base_projection(name).bind(self.ws._view(buf, name + ".wq"),
+                                           self.ws._view(buf, name + ".sw"))
+        blk.input_layernorm.weight.data = self.ws._view(buf, "input_layernorm")
+        blk.post_attention_layernorm.weight.data = self.ws._view(buf, "post_attention_layernorm")
+
+    def _release(self, layer: int) -> None:
+        if layer >= len(self.resident):
+            self.ws.release(layer % 2)
+
+    # ---- one step ------------------------------------------------------------
+    def train_step(self, ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
+        """One optimizer step on a [batch, seq] micro-batch of token ids (device or
+        pinned host). Returns the loss as a 0-d device tensor."""
+        dev = self.device
+        ids = ids.to(dev, non_blocking=True)
+        labels = ids if labels is None else labels.to(dev, non_blocking=True)
+        L = self.L
+        # forward (no grad), saving each block's input to pinned host
+        with torch.no_grad():
+            h = self.embed(ids)
+            self._ensure(0)
+            for i in range(L):
+                if i + 1 < L:
+                    self._ensure(i + 1)
+                blk = self._bind(i)
+                self.ckpt.save(i, h)
+                h = blk(h, self.cos, self.sin)
+                self._release(i)
+        # head + loss
+        h = h.detach().requires_grad_(True)
+        logits = self.head(h)
+        loss = F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]),
+                               labels[:, 1:].reshape(-1))
+        loss.backward()
+        grad = h.grad
+        del logits, h
+        # backward in reverse: restore, re-forward with grad, backward
+        self.ckpt.restore_async(L - 1)
+        for i in range(L - 1, -1, -1):
+            if i - 1 >= 0:
+                self._ensure(i - 1)
+                self.ckpt.restore_async(i - 1)
+            blk = self._bind(i)
+            x = self.ckpt.wait(i).requires_grad_(True)
+            out = blk(x, self.cos, self.sin)
+            out.backward(grad)
+            grad = x.grad
+            del out, x
+            self._release(i)
+            self.reducer.launch([p.grad for ab in self.lora[i].values() for p in ab])
+        self.reducer.finish()
+        torch.nn.utils.clip_grad_norm_(self.params, 1.0)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=False)
+        self.global_step += 1
+        return loss.detach()
+
+    def close(self) -> None:
+        self.ws.close()

@@ -1,0 +1,87 @@
+"""CPU torch modules built on the W8A8 oracle — TEST INFRASTRUCTURE ONLY.
+
+``OracleW8A8Linear`` is an ``nn.Linear`` whose forward is the oracle's W8A8
+contract (quantise the bf16 input per token and the weight per output
+channel, exact int8 GEMM, fp32 dequant epilogue, bf16 out) and whose backward
+is the straight-through dgrad ``dx = dy . bf16(wq * sw)`` with fp32
+accumulation. It is swapped into the reference's own HF layers (via the
+reference adapter, src/lema/adapters/_llama.py:59-107, and LoRAWrapper,
+src/lema/_lora.py:13-26) to produce golden fixtures, and into
+lema_b200.llama.LlamaBlock on the CPU to form the layer-level oracle.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import oracle as O
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return O.torch_bf16_to_bits(t.detach().to(torch.bfloat16))
+
+
+class _OracleFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2d, mod, bias):
+        xq, sx = O.c_quantize_rows(_bits(x2d))
+        acc = O.c_int8_gemm(xq, mod.wq)
+        b = None if bias is None else _bits(bias)
+        y = O.bits_to_torch_bf16(O.c_epilogue(acc, sx, mod.sw, b))
+        ctx.mod = mod
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dyb = dy.to(torch.bfloat16).float()
+        dx = (dyb @ ctx.mod.wdeq_f32()).to(torch.bfloat16)
+        db = dy.float().sum(0).to(torch.bfloat16) if ctx.has_bias else None
+        return dx, None, db
+
+
+class OracleW8A8Linear(nn.Linear):
+    """CPU W8A8 linear (oracle arithmetic), frozen base, STE backward."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None):
+        out_f, in_f = weight.shape
+        nn.Module.__init__(self)
+        self.in_features = in_f
+        self.out_features = out_f
+        self.weight = nn.Parameter(weight.detach().to(torch.bfloat16).clone(), requires_grad=False)
+        self.bias = None if bias is None else nn.Parameter(bias.detach().to(torch.bfloat16).clone(),
+                                                           requires_grad=False)
+        self.wq, self.sw = O.c_quantize_rows(_bits(self.weight))
+        self._wdeq = None
+
+    def wdeq_f32(self) -> torch.Tensor:
+        """fp32 copy of bf16(wq * sw) [out, in] (the frozen weight: built once)."""
+        if self._wdeq is None:
+            wdT = O.c_dequant_transpose(self.wq, self.sw)
+            self._wdeq = O.bits_to_torch_bf16(np.ascontiguousarray(wdT.T)).float()
+        return self._wdeq
+
+    @classmethod
+    def from_linear(cls, lin: nn.Linear) -> "OracleW8A8Linear":
+        return cls(lin.weight, lin.bias)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        K = x.shape[-1]
+        y = _OracleFn.apply(x.reshape(-1, K), self, self.bias)
+        return y.reshape(*x.shape[:-1], self.out_features).to(x.dtype)
+
+
+def swap_linears(module: nn.Module, names=("q_proj", "k_proj", "v_proj", "o_proj",
+                                           "gate_proj", "up_proj", "down_proj")) -> None:
+    """Replaces every nn.Linear named in ``names`` (or the ``base_layer`` of a LoRA
+    wrapper with that name) by an OracleW8A8Linear holding the same weight."""
+    for parent in list(module.modules()):
+        for name, child in list(parent.named_children()):
+            if name not in names:
+                continue
+            if hasattr(child, "base_layer") and isinstance(child.base_layer, nn.Linear):
+                if not isinstance(child.base_layer, OracleW8A8Linear):
+                    child.base_layer = OracleW8A8Linear.from_linear(child.base_layer)
+            elif isinstance(child, nn.Linear) and not isinstance(child, OracleW8A8Linear):
+                setattr(parent, name, OracleW8A8Linear.from_linear(child))

@@ -1,0 +1,61 @@
+"""CPU tests of the layer-level oracle.
+
+1. lema_b200's LlamaBlock with bf16 nn.Linear projections computes the same
+   thing as HF LlamaDecoderLayer driven the way the reference adapter drives it
+   (src/lema/adapters/_llama.py:183-252).
+2. LlamaBlock with the oracle's W8A8 linears swapped in (eager attention, CPU)
+   reproduces the golden fixture generated from the reference's own Python
+   path (tests/golden/make_golden_layer.py) bit for bit: outputs, input
+   gradient and LoRA gradients.
+"""
+import torch
+from transformers.models.llama.modeling_llama import LlamaConfig, LlamaDecoderLayer
+
+from lema_b200.llama import LlamaBlock, LlamaShape, rope_cos_sin
+from oracle.oracle import torch_bf16_to_bits
+from oracle.torch_ref import swap_linears
+
+from layer_fixture import bf16, block_from_fixture, load
+
+
+def test_block_matches_hf_decoder_layer_fp32():
+    shape = LlamaShape(hidden=64, heads=4, kv_heads=2, intermediate=160, vocab=100, layers=1)
+    cfg = LlamaConfig(hidden_size=64, num_attention_heads=4, num_key_value_heads=2,
+                      intermediate_size=160, rms_norm_eps=1e-5, rope_theta=10000.0,
+                      max_position_embeddings=64)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    hf = LlamaDecoderLayer(cfg, layer_idx=0).float()
+    for p in hf.parameters():
+        torch.nn.init.normal_(p, std=0.05)
+    mine = LlamaBlock(shape, quantized=False, dtype=torch.float32)
+    mine.self_attn.attn_impl = "eager"
+    mine.load_state_dict(hf.state_dict())
+    x = torch.randn(2, 24, 64)
+    pos = torch.arange(24)[None].expand(2, -1)
+    cos, sin = rope_cos_sin(shape, 24, "cpu", torch.float32)
+    mask = torch.full((24, 24), float("-inf")).triu(1)[None, None].expand(2, 1, 24, 24)
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    hf_cos, hf_sin = LlamaRotaryEmbedding(cfg)(x, pos)
+    assert torch.allclose(hf_cos[0], cos[0]) and torch.allclose(hf_sin[0], sin[0])
+    ref = hf(x, attention_mask=mask, position_ids=pos, position_embeddings=(hf_cos, hf_sin))
+    ref = ref[0] if isinstance(ref, tuple) else ref
+    out = mine(x, cos, sin)
+    assert torch.allclose(out, ref, atol=1e-6, rtol=1e-5), (out - ref).abs().max()
+
+
+def test_oracle_block_reproduces_reference_fixture():
+    d, shape, rank, alpha = load()
+    blk = block_from_fixture(d, shape, rank, alpha, "cpu", quantized=False)
+    blk.self_attn.attn_impl = "eager"
+    swap_linears(blk)
+    x = bf16(d["x"]).clone().requires_grad_(True)
+    cos, sin = rope_cos_sin(shape, x.shape[1], "cpu", torch.bfloat16)
+    y = blk(x, cos, sin)
+    y.backward(bf16(d["dy"]))
+    assert (torch_bf16_to_bits(y) == d["y"]).all()
+    assert (torch_bf16_to_bits(x.grad) == d["dx"]).all()
+    for proj in ("q_proj", "v_proj"):
+        m = blk.projection(proj)
+        assert (torch_bf16_to_bits(m.lora_A.grad) == d[f"grad/self_attn.{proj}.lora_A"]).all()
+        assert (torch_bf16_to_bits(m.lora_B.grad) == d[f"grad/self_attn.{proj}.lora_B"]).all()
