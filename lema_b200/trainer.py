@@ -16,8 +16,10 @@
   blocks still resident at the turnaround are reused without re-upload; each
   finished layer's LoRA gradients start their data-parallel all-reduce
   (NCCL) while the next layer computes;
-* optimizer (reference :183-187): clip_grad_norm_(1.0) and AdamW over the LoRA
-  parameters.
+* optimizer (reference :183-187): every ``grad_accum`` micro-steps (the loss
+  is divided by ``grad_accum`` as at reference :156), clip_grad_norm_(1.0) and
+  AdamW over the LoRA parameters; with data parallelism the LoRA gradients
+  are averaged over ranks on that micro-step.
 
 Every cross-stream dependency is a CUDA event; the host never blocks on a
 transfer. The embedding and the head stay resident in HBM (they are frozen and
@@ -72,7 +74,7 @@ class StreamedLoraTrainer:
     def __init__(self, shape: LlamaShape, device, batch: int, seq: int, lora_rank: int = 16,
                  lora_alpha: float = 32.0, targets: tuple[str, ...] = ("q_proj", "v_proj"),
                  lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0, ckpt_mode: int = 0,
-                 resident_layers: int = 0, group=None):
+                 resident_layers: int = 0, grad_accum: int = 1, group=None):
         self.shape = shape
         self.device = torch.device(device)
         self.batch, self.seq = batch, seq
@@ -130,6 +132,8 @@ class StreamedLoraTrainer:
         self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
         self.reducer = LoraGradReducer(group)
         self.slot_layer = [-1, -1]
+        self.grad_accum = max(1, int(grad_accum))
+        self.micro_step = 0
         self.global_step = 0
 
     # ---- weights -----------------------------------------------------------
@@ -191,7 +195,10 @@ class StreamedLoraTrainer:
         logits = self.head(h)
         loss = F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]),
                                labels[:, 1:].reshape(-1))
-        loss.backward()
+        # the reference divides by the accumulation count (src/lema/_trainer.py:156)
+        (loss / self.grad_accum).backward()
+        self.micro_step += 1
+        stepping = self.micro_step % self.grad_accum == 0
         grad = h.grad
         del logits, h
         # backward in reverse: restore, re-forward with grad, backward
@@ -207,12 +214,14 @@ class StreamedLoraTrainer:
             grad = x.grad
             del out, x
             self._release(i)
-            self.reducer.launch([p.grad for ab in self.lora[i].values() for p in ab])
-        self.reducer.finish()
-        torch.nn.utils.clip_grad_norm_(self.params, 1.0)
-        self.opt.step()
-        self.opt.zero_grad(set_to_none=False)
-        self.global_step += 1
+            if stepping:
+                self.reducer.launch([p.grad for ab in self.lora[i].values() for p in ab])
+        if stepping:
+            self.reducer.finish()
+            torch.nn.utils.clip_grad_norm_(self.params, 1.0)
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=False)
+            self.global_step += 1
         return loss.detach()
 
     def close(self) -> None:

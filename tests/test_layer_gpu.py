@@ -8,7 +8,10 @@ Tolerance (bf16, stated per tensor): the GPU and CPU paths differ in
 reduction order (RMSNorm, attention, LoRA and dgrad GEMMs), and a one-ulp
 difference at a quantiser input can move one int8 value by one step. The bar:
 relative RMS error <= 2e-2 and max-abs error <= 0.25 * RMS(ref) for outputs
-and input gradients; relative RMS error <= 5e-2 for LoRA gradients.
+and input gradients; relative RMS error <= 5e-2 for LoRA gradients. When the
+device runs flash SDPA against the reference's eager attention (which rounds
+the 512 x 512 score matrix to bf16 before the softmax), the output bar is
+relative RMS error <= 5e-2.
 """
 import numpy as np
 import pytest
@@ -64,9 +67,11 @@ def _cfg2_block(device, quantized, seed=0):
     return shape, blk, g
 
 
-def test_cfg2_layer_fwd_ckpt_recompute_bwd(cuda_device):
+@pytest.mark.parametrize("attn", ["eager", "sdpa"])
+def test_cfg2_layer_fwd_ckpt_recompute_bwd(cuda_device, attn):
     """One 7B-shaped layer: forward, boundary checkpoint to pinned host and back,
-    re-forward with grad, backward — against the CPU oracle block."""
+    re-forward with grad, backward — against the CPU oracle block (eager attention,
+    as the reference adapter runs it)."""
     from oracle.torch_ref import swap_linears
     dev = cuda_device
     shape, cpu_blk, g = _cfg2_block(dev, quantized=False)
@@ -85,6 +90,7 @@ def test_cfg2_layer_fwd_ckpt_recompute_bwd(cuda_device):
     apply_lora(gpu_blk, 16, 32, params={k: (torch.nn.Parameter(a.detach().to(dev).clone()),
                                             torch.nn.Parameter(b.detach().to(dev).clone()))
                                         for k, (a, b) in lora.items()})
+    gpu_blk.self_attn.attn_impl = attn
     x = torch.randn(1, 512, shape.hidden, generator=g).to(torch.bfloat16)
     dy = torch.randn(1, 512, shape.hidden, generator=g).to(torch.bfloat16)
 
@@ -110,8 +116,9 @@ def test_cfg2_layer_fwd_ckpt_recompute_bwd(cuda_device):
     ccos, csin = rope_cos_sin(shape, 512, "cpu", torch.bfloat16)
     yc = cpu_blk(xc, ccos, csin)
     yc.backward(dy)
-    close(y, yc, what="y")
-    close(x_re.grad, xc.grad, what="dx")
+    out_rel = 2e-2 if attn == "eager" else 5e-2
+    close(y, yc, out_rel, 0.5, what="y")
+    close(x_re.grad, xc.grad, out_rel, 0.5, what="dx")
     for proj in ("q_proj", "v_proj"):
         gm, cm = gpu_blk.projection(proj), cpu_blk.projection(proj)
         close(gm.lora_A.grad, cm.lora_A.grad, 5e-2, 1.0, proj + ".dA")
