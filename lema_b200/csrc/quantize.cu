@@ -212,42 +212,52 @@ int quantize_rows_impl(const T* x, int64_t rows, int64_t cols, int64_t ldx, int8
   return LEMA_OK;
 }
 
-// wdT[k, n] = bf16(float(wq[n, k]) * sw[n]); 64 x 64 tiles through shared memory.
-constexpr int kTT = 64;
+// wdT[k, n] = bf16(float(wq[n, k]) * sw[n]). One CTA transposes a 64 (n) x
+// 128 (k) tile through shared memory: 16-byte loads of 16 int8 per thread
+// (consecutive threads take consecutive rows, so the shared-memory writes of a
+// warp hit consecutive bf16), then 16-byte stores of 8 bf16 along n.
+constexpr int kDTN = 64;
+constexpr int kDTK = 128;
 __global__ void __launch_bounds__(256) dequant_transpose_kernel(const int8_t* __restrict__ wq,
                                                                 int64_t ldw,
                                                                 const float* __restrict__ sw,
                                                                 int64_t n_rows, int64_t k_cols,
                                                                 __nv_bfloat16* __restrict__ out,
-                                                                int64_t ldt) {
-  __shared__ __nv_bfloat16 tile[kTT][kTT + 2];  // [k][n], padded against bank conflicts
-  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTT;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kTT;
-  // Load: 64 rows (n) x 64 int8 (k); thread -> (row = t / 4, 16 bytes at (t % 4) * 16).
-  {
-    const int r = threadIdx.x / 4, c16 = (threadIdx.x % 4) * 16;
+                                                                int64_t ldt, bool vec_in,
+                                                                bool vec_out) {
+  __shared__ __align__(16) __nv_bfloat16 tile[kDTK][kDTN + 8];  // [k][n], 144-byte rows
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kDTN;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kDTK;
+  for (int c = threadIdx.x; c < kDTN * (kDTK / 16); c += 256) {
+    const int r = c % kDTN, q = c / kDTN;  // row of the tile, 16-byte chunk along k
     const int64_t n = n0 + r;
-    float s = 0.f;
-    if (n < n_rows) s = sw[n];
-    const int8_t* src = wq + n * ldw + k0 + c16;
+    const int64_t kb = k0 + q * 16;
+    __align__(16) int8_t v[16];
+    if (vec_in && n < n_rows && kb + 16 <= k_cols) {
+      *reinterpret_cast<uint4*>(v) =
+          __ldg(reinterpret_cast<const uint4*>(wq + n * ldw + kb));
+    } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int64_t k = k0 + c16 + j;
-      float f = 0.f;
-      if (n < n_rows && k < k_cols) f = __fmul_rn(static_cast<float>(src[j]), s);
-      tile[c16 + j][r] = __float2bfloat16_rn(f);
+      for (int j = 0; j < 16; ++j)
+        v[j] = (n < n_rows && kb + j < k_cols) ? wq[n * ldw + kb + j] : static_cast<int8_t>(0);
     }
+    const float s = n < n_rows ? sw[n] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      tile[q * 16 + j][r] = __float2bfloat16_rn(__fmul_rn(static_cast<float>(v[j]), s));
   }
   __syncthreads();
-  // Store: 64 rows (k) x 64 bf16 (n); each thread writes 2 x 8 consecutive n.
-  for (int i = threadIdx.x; i < kTT * (kTT / 8); i += 256) {
-    const int r = i / (kTT / 8), c8 = (i % (kTT / 8)) * 8;
+  for (int c = threadIdx.x; c < kDTK * (kDTN / 8); c += 256) {
+    const int r = c / (kDTN / 8), q = c % (kDTN / 8);
     const int64_t k = k0 + r;
-    if (k >= k_cols) continue;
-    __nv_bfloat16* dst = out + k * ldt + n0 + c8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (n0 + c8 + j < n_rows) dst[j] = tile[r][c8 + j];
+    const int64_t n = n0 + q * 8;
+    if (k >= k_cols || n >= n_rows) continue;
+    __nv_bfloat16* dst = out + k * ldt + n;
+    if (vec_out && n + 8 <= n_rows) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[r][q * 8]);
+    } else {
+      for (int j = 0; j < 8 && n + j < n_rows; ++j) dst[j] = tile[r][q * 8 + j];
+    }
   }
 }
 
@@ -296,11 +306,14 @@ extern "C" int lema_dequant_transpose(const int8_t* wq, int64_t ldw, const float
   if (wq == nullptr || sw == nullptr || wdT_bf16 == nullptr)
     return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
   if (ldw < K || ldt < N) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld too small");
-  if ((K + kTT - 1) / kTT > INT32_MAX || (N + kTT - 1) / kTT > 65535)
+  if ((K + kDTK - 1) / kDTK > INT32_MAX || (N + kDTN - 1) / kDTN > 65535)
     return set_error(LEMA_ERR_UNSUPPORTED, "matrix too large for the transpose grid");
-  dim3 grid(static_cast<unsigned>((K + kTT - 1) / kTT), static_cast<unsigned>((N + kTT - 1) / kTT));
+  dim3 grid(static_cast<unsigned>((K + kDTK - 1) / kDTK),
+            static_cast<unsigned>((N + kDTN - 1) / kDTN));
+  const bool vec_in = aligned16(wq) && ldw % 16 == 0;
+  const bool vec_out = aligned16(wdT_bf16) && ldt % 8 == 0;
   dequant_transpose_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      wq, ldw, sw, N, K, static_cast<__nv_bfloat16*>(wdT_bf16), ldt);
+      wq, ldw, sw, N, K, static_cast<__nv_bfloat16*>(wdT_bf16), ldt, vec_in, vec_out);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }
