@@ -372,7 +372,7 @@ def run_train(args, world, rank, local) -> dict | None:
     from lema_b200.trainer import StreamedLoraTrainer
 
     dev = torch.device("cuda", local)
-    shape = LlamaShape()
+    shape = LlamaShape(layers=args.layers)
     batch, seq = 8, 512
     tokens_per_step = batch * seq
     tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16, lora_alpha=32.0,
@@ -449,9 +449,10 @@ def run_train(args, world, rank, local) -> dict | None:
         "dtype": "int8 W8A8 projections (bf16 activations; bf16 attention, LoRA, lm_head)",
         "data": "synthetic (random-init Llama-2-7B-shaped weights, token ids uniform in "
                 "[0, 32000), labels = inputs)",
-        "config": {"workload": "llama7b_streamed_lora: 32 x [hidden 4096, 32x128 heads, MLP "
-                               "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections "
-                               "streamed from pinned RAM, activation checkpoints offloaded",
+        "config": {"workload": f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 "
+                               "heads, MLP 11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 "
+                               "projections streamed from pinned RAM, activation checkpoints "
+                               "offloaded",
                    "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}",
                    "resident_layers": args.resident_layers,
@@ -562,6 +563,9 @@ def main():
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="decoder layers of the streamed model (32 = Llama-2-7B; fewer only "
+                         "for short profiling runs, never for a reported number)")
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--int8-peak-tops", type=float, default=0.0)
