@@ -136,6 +136,14 @@ LEMA_API int lema_bf16_gemm_tn(const void* a_bf16, int64_t lda, const void* b_bf
                       void* y_bf16, int64_t ldy, int64_t M, int64_t N, int64_t K,
                       void* stream);
 
+/* The same bf16 GEMM with the fp32 accumulators as output (y_f32[M,N], row
+ * stride ldy): the weight gradient dW = dy^T . x of a trainable projection
+ * (selective full fine-tuning), fed transposed operands. Replaces the
+ * autograd weight gradient whose fp32 accumulation _full_ft.py:186-192 keeps. */
+LEMA_API int lema_bf16_gemm_tn_f32(const void* a_bf16, int64_t lda, const void* b_bf16,
+                                   int64_t ldb, float* y_f32, int64_t ldy, int64_t M, int64_t N,
+                                   int64_t K, void* stream);
+
 /* dx[M,K] = dy[M,N] . wdeq[N,K]. wdT_ws is a caller-provided bf16 workspace
  * of at least K * ldt elements, ldt = N rounded up to a multiple of 8.
  * Replaces the autograd dgrad of F.linear reached from _trainer.py:161,166. */
@@ -155,6 +163,25 @@ LEMA_API int lema_grouped_w8a8_gemm(const int8_t* xq, int64_t ldx, const float* 
                            const void* bias_bf16, void* y_bf16, int64_t ldy,
                            const int64_t* offsets_host, int32_t E,
                            int64_t N, int64_t K, void* stream);
+
+/* Grouped bf16 GEMM: rows [offsets[e], offsets[e+1]) of a times b_e^T, with
+ * b_e = b + e*N*ldb ([N, K] per group), fp32 accumulation, bf16 out. offsets
+ * is a HOST array of E+1 entries. */
+LEMA_API int lema_grouped_bf16_gemm_tn(const void* a_bf16, int64_t lda, const void* b_bf16,
+                                       int64_t ldb, void* y_bf16, int64_t ldy,
+                                       const int64_t* offsets_host, int32_t E, int64_t N,
+                                       int64_t K, void* stream);
+
+/* Grouped straight-through dgrad of the MoE experts: rows of expert e get
+ * dx = dy . bf16(wq_e * sw_e) (wq_e = wq + e*N*ldw, [N, K]). wdT_ws holds at
+ * least E * K * ldt bf16 (ldt >= N, multiple of 8). Replaces the autograd
+ * dgrad of the per-expert F.linear calls of the grouped_mm experts
+ * implementation (adapters/_mixtral.py:21-22, 266-268). */
+LEMA_API int lema_grouped_w8a8_dgrad(const void* dy_bf16, int64_t lddy, const int8_t* wq,
+                                     int64_t ldw, const float* sw, void* dx_bf16,
+                                     int64_t lddx, void* wdT_ws, int64_t ldt,
+                                     const int64_t* offsets_host, int32_t E, int64_t N,
+                                     int64_t K, void* stream);
 
 /* ---- K5: boundary-activation checkpoint offload -------------------------- */
 /* Copies `bytes` from device memory `src` into pinned host memory `dst`

@@ -116,7 +116,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
     const int n = n0 + c * 32;
     if (!rvalid || n >= p.n) continue;
     const bool full_chunk = (n + 32) <= p.n;
-    if (KIND == kKindI8 && p.acc != nullptr) {
+    if (p.acc != nullptr) {  // raw accumulators: s32 (int8 kind) or fp32 bits (bf16 kind)
       int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
       if (full_chunk && acc_vec) {
 #pragma unroll
@@ -876,4 +876,46 @@ extern "C" int lema_grouped_w8a8_gemm(const int8_t* xq, int64_t ldx, const float
   }
   return run_gemm(kKindI8, xq, ldx, wq, ldw, g, N, K, sx, sw, bias_bf16, y_bf16, ldy, nullptr, 0,
                   s);
+}
+
+extern "C" int lema_grouped_bf16_gemm_tn(const void* a_bf16, int64_t lda, const void* b_bf16,
+                                         int64_t ldb, void* y_bf16, int64_t ldy,
+                                         const int64_t* offsets_host, int32_t E, int64_t N,
+                                         int64_t K, void* stream) {
+  clear_error();
+  if (offsets_host == nullptr || E <= 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "offsets must hold E+1 entries, E >= 1");
+  if (E > kMaxGroups)
+    return set_error(LEMA_ERR_UNSUPPORTED, "more than 64 groups per grouped launch");
+  if (N < 0 || K < 0 || offsets_host[0] != 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad sizes or offsets[0] != 0");
+  Groups g;
+  g.num = E;
+  for (int e = 0; e <= E; ++e) {
+    g.row_start[e] = offsets_host[e];
+    if (e > 0 && offsets_host[e] < offsets_host[e - 1])
+      return set_error(LEMA_ERR_INVALID_ARGUMENT, "offsets must be non-decreasing");
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  if (K == 0)
+    return k_zero_outputs(y_bf16, ldy, nullptr, nullptr, 0, offsets_host[E], N, s);
+  return run_gemm(kKindBF16, a_bf16, lda, b_bf16, ldb, g, N, K, nullptr, nullptr, nullptr,
+                  y_bf16, ldy, nullptr, 0, s);
+}
+
+extern "C" int lema_bf16_gemm_tn_f32(const void* a_bf16, int64_t lda, const void* b_bf16,
+                                     int64_t ldb, float* y_f32, int64_t ldy, int64_t M, int64_t N,
+                                     int64_t K, void* stream) {
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  if (y_f32 == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null output");
+  auto s = static_cast<cudaStream_t>(stream);
+  if (K == 0)
+    return k_zero_outputs(nullptr, 0, nullptr, reinterpret_cast<int32_t*>(y_f32), ldy, M, N, s);
+  Groups g;
+  g.num = 1;
+  g.row_start[0] = 0;
+  g.row_start[1] = M;
+  return run_gemm(kKindBF16, a_bf16, lda, b_bf16, ldb, g, N, K, nullptr, nullptr, nullptr,
+                  nullptr, 0, reinterpret_cast<int32_t*>(y_f32), ldy, s);
 }

@@ -24,6 +24,9 @@ extern "C" int lema_w8a8_gemm(const int8_t*, int64_t, const float*, const int8_t
                               int64_t, int64_t, int64_t, void*);
 extern "C" int lema_bf16_gemm_tn(const void*, int64_t, const void*, int64_t, void*, int64_t,
                                  int64_t, int64_t, int64_t, void*);
+extern "C" int lema_grouped_bf16_gemm_tn(const void*, int64_t, const void*, int64_t, void*,
+                                         int64_t, const int64_t*, int32_t, int64_t, int64_t,
+                                         void*);
 
 namespace {
 
@@ -328,4 +331,26 @@ extern "C" int lema_w8a8_dgrad(const void* dy_bf16, int64_t lddy, const int8_t* 
   if (rc) return rc;
   // dx[M, K] = dy[M, N] . wdT[K, N]^T
   return lema_bf16_gemm_tn(dy_bf16, lddy, wdT_ws, ldt, dx_bf16, lddx, M, K, N, stream);
+}
+
+extern "C" int lema_grouped_w8a8_dgrad(const void* dy_bf16, int64_t lddy, const int8_t* wq,
+                                       int64_t ldw, const float* sw, void* dx_bf16,
+                                       int64_t lddx, void* wdT_ws, int64_t ldt,
+                                       const int64_t* offsets_host, int32_t E, int64_t N,
+                                       int64_t K, void* stream) {
+  clear_error();
+  if (ldt < N || ldt % 8 != 0)
+    return set_error(LEMA_ERR_MISALIGNED, "workspace ld must be >= N and a multiple of 8");
+  if (offsets_host == nullptr || E <= 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "offsets must hold E+1 entries, E >= 1");
+  auto* ws = static_cast<__nv_bfloat16*>(wdT_ws);
+  for (int e = 0; e < E; ++e) {
+    if (offsets_host[e + 1] == offsets_host[e]) continue;  // expert without tokens
+    int rc = lema_dequant_transpose(wq + static_cast<int64_t>(e) * N * ldw, ldw, sw + e * N, N, K,
+                                    ws + static_cast<int64_t>(e) * K * ldt, ldt, stream);
+    if (rc) return rc;
+  }
+  // rows of expert e: dx = dy . wdT_e^T, wdT_e = ws[e] ([K, ldt])
+  return lema_grouped_bf16_gemm_tn(dy_bf16, lddy, wdT_ws, ldt, dx_bf16, lddx, offsets_host, E,
+                                   K, N, stream);
 }

@@ -1,0 +1,101 @@
+"""Selective full fine-tuning of W8A8 projections (row A9).
+
+Mirrors the reference's ``FullFTManager`` (src/lema/_full_ft.py): chosen
+projections of chosen layers are trainable; their true weights (model dtype,
+bf16) and fp32 AdamW moments live in host RAM (pinned here), their gradients
+accumulate in fp32 (``accumulate_grads``, :186-192 — on the device here), and
+at each accumulation boundary every selected layer is clipped to norm 1 over
+its accumulators (:194-202) and stepped with the same AdamW arithmetic
+(:204-229: decoupled weight decay, bias-corrected moments, eps 1e-8, the
+update computed in fp32 and the weight stored back in bf16).
+
+What W8A8 adds: the forward of a trainable projection uses the int8 copy of
+its *current* true weight, so after each step the new bf16 weight is
+re-quantised per output channel on the device (K1) and the int8 rows and
+scales are written back into the layer's pinned-RAM segment, from which the
+next forward streams them. The backward is straight-through: dx as for frozen
+projections, dW = dy^T . x with fp32 accumulation (``lema_bf16_gemm_tn_f32``).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+
+
+class SelectiveFullFT:
+    def __init__(self, ws, layers, modules, true_weights: dict, device, lr: float,
+                 weight_decay: float):
+        self.ws = ws
+        self.layers = tuple(layers)
+        self.modules = tuple(modules)
+        self.device = torch.device(device)
+        self.lr = lr
+        self.wd = weight_decay
+        self.true: dict[tuple[int, str], torch.Tensor] = {}
+        self.m: dict[tuple[int, str], torch.Tensor] = {}
+        self.v: dict[tuple[int, str], torch.Tensor] = {}
+        self.acc: dict[tuple[int, str], torch.Tensor] = {}
+        for key, w in true_weights.items():
+            self.true[key] = w.detach().to("cpu", torch.bfloat16).contiguous().pin_memory()
+            self.m[key] = torch.zeros(w.shape, dtype=torch.float32).pin_memory()
+            self.v[key] = torch.zeros(w.shape, dtype=torch.float32).pin_memory()
+            self.acc[key] = torch.zeros(w.shape, dtype=torch.float32, device=self.device)
+        self.layer_steps: dict[int, int] = {}
+
+    def attach(self, layer: int, block) -> None:
+        """Makes the selected projections of ``block`` (bound to ``layer``) trainable."""
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+            base = block.base_projection(name)
+            base.wgrad_acc = self.acc.get((layer, name))
+
+    def layer_grads(self, layer: int) -> list[torch.Tensor]:
+        return [self.acc[(layer, n)] for n in self.modules if (layer, n) in self.acc]
+
+    def clip_layer_(self, layer: int, max_norm: float = 1.0) -> float:
+        accs = self.layer_grads(layer)
+        total = sum(float(a.pow(2).sum()) for a in accs)
+        norm = math.sqrt(total)
+        if norm > max_norm and norm > 0:
+            for a in accs:
+                a.mul_(max_norm / norm)
+        return norm
+
+    @torch.no_grad()
+    def step_layer(self, layer: int) -> None:
+        beta1, beta2, eps = 0.9, 0.999, 1e-8
+        step = self.layer_steps.get(layer, 0) + 1
+        self.layer_steps[layer] = step
+        b1 = 1 - beta1 ** step
+        b2 = 1 - beta2 ** step
+        for name in self.modules:
+            key = (layer, name)
+            if key not in self.true:
+                continue
+            w = self.true[key].to(self.device, non_blocking=True).float()
+            g = self.acc[key]
+            m = self.m[key].to(self.device, non_blocking=True)
+            v = self.v[key].to(self.device, non_blocking=True)
+            if self.wd:
+                w.mul_(1 - self.lr * self.wd)
+            m.mul_(beta1).add_(g, alpha=1 - beta1)
+            v.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+            denom = v.sqrt().div_(math.sqrt(b2)).add_(eps)
+            w.addcdiv_(m, denom, value=-(self.lr / b1))
+            wb = w.to(torch.bfloat16)
+            # re-quantise the new weight into the layer's streamed int8 segment
+            wq, sw = ops.quantize_weight(wb)
+            ram = self.ws.ram[layer]
+            self.ws._view(ram, name + ".wq").copy_(wq)
+            self.ws._view(ram, name + ".sw").copy_(sw)
+            self.true[key].copy_(wb)
+            self.m[key].copy_(m)
+            self.v[key].copy_(v)
+            g.zero_()
+
+    def step(self) -> None:
+        for layer in self.layers:
+            self.clip_layer_(layer, 1.0)
+            self.step_layer(layer)

@@ -116,11 +116,28 @@ def _eager_causal_attention(q, k, v, scale):
     return torch.matmul(w, v)
 
 
+def _chunked_causal_attention(q, k, v, scale, chunk, gqa):
+    """Exact causal attention computed one query chunk at a time against all keys
+    up to the chunk's end, as the reference's chunked attention does (full score
+    rows per query chunk, src/lema/_tensorstore.py:565-608), with a lower-right
+    aligned causal mask inside each chunk."""
+    from torch.nn.attention.bias import causal_lower_right
+    S = q.shape[2]
+    outs = []
+    for c0 in range(0, S, chunk):
+        c1 = min(S, c0 + chunk)
+        mask = causal_lower_right(c1 - c0, c1)
+        outs.append(F.scaled_dot_product_attention(q[:, :, c0:c1], k[:, :, :c1], v[:, :, :c1],
+                                                   attn_mask=mask, scale=scale, enable_gqa=gqa))
+    return torch.cat(outs, dim=2)
+
+
 class LlamaAttention(nn.Module):
     def __init__(self, shape: LlamaShape, quantized: bool, device=None, dtype=torch.bfloat16):
         super().__init__()
         self.shape = shape
         self.attn_impl = "sdpa"  # "eager" reproduces HF eager attention op for op
+        self.attn_chunk = 0      # > 0: exact attention in query chunks of this many tokens
         ps = shape.proj_shapes()
         for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
             setattr(self, n, _linear(*ps[n], quantized, device, dtype))
@@ -134,6 +151,9 @@ class LlamaAttention(nn.Module):
         q, k = apply_rope(q, k, cos, sin)
         if self.attn_impl == "eager":
             o = _eager_causal_attention(q, k, v, d ** -0.5)
+        elif self.attn_chunk and S > self.attn_chunk:
+            o = _chunked_causal_attention(q, k, v, d ** -0.5, self.attn_chunk,
+                                          self.shape.heads != self.shape.kv_heads)
         else:
             gqa = self.shape.heads != self.shape.kv_heads
             o = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=d ** -0.5,
@@ -173,10 +193,18 @@ class LlamaBlock(nn.Module):
         m = self.projection(name)
         return m.base_layer if isinstance(m, LoRALinear) else m
 
+    gradient_checkpointing = False
+
     def forward(self, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         residual = h
         h = self.input_layernorm(h)
-        h = self.self_attn(h, cos, sin)
+        if self.gradient_checkpointing and torch.is_grad_enabled():
+            # attention is re-run in backward instead of keeping its activations,
+            # as the reference adapter does (src/lema/adapters/_llama.py:239-243)
+            from torch.utils.checkpoint import checkpoint
+            h = checkpoint(self.self_attn, h, cos, sin, use_reentrant=False)
+        else:
+            h = self.self_attn(h, cos, sin)
         h = residual + h
         residual = h
         h = self.post_attention_layernorm(h)

@@ -79,7 +79,13 @@ class W8A8Linear(nn.Linear):
         if bias is not None:
             self.bias.data = bias
 
+    # Selective full fine-tuning: when ``wgrad_acc`` (fp32 [out, in]) is set, the
+    # backward also adds the weight gradient dy^T . x into it.
+    wgrad_acc: torch.Tensor | None = None
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.wgrad_acc is not None and torch.is_grad_enabled() and self.bias is None:
+            return ops.w8a8_linear_trainable(x, self.weight, self.weight_scale, self)
         return ops.w8a8_linear(x, self.weight, self.weight_scale, self.bias)
 
     def extra_repr(self) -> str:

@@ -306,6 +306,35 @@ class _W8A8LinearFn(torch.autograd.Function):
         return dx, None, None, dbias
 
 
+class _W8A8TrainableFn(torch.autograd.Function):
+    """W8A8 forward of a trainable projection (the int8 copy of its current true
+    weight); backward: straight-through dx and the fp32 weight gradient
+    dW = dy^T . x, added into ``sink.wgrad_acc``."""
+
+    @staticmethod
+    def forward(ctx, x2d, wq, sw, sink):
+        y = w8a8_linear_forward(x2d, wq, sw, None)
+        ctx.save_for_backward(x2d, wq, sw)
+        ctx.sink = sink
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, wq, sw = ctx.saved_tensors
+        dx = w8a8_dgrad(dy, wq, sw) if ctx.needs_input_grad[0] else None
+        ctx.sink.wgrad_acc.add_(w8a8_wgrad(dy, x2d))
+        return dx, None, None, None
+
+
+def w8a8_linear_trainable(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor, sink) -> torch.Tensor:
+    K = x.shape[-1]
+    lead = x.shape[:-1]
+    x2d = x.reshape(-1, K)
+    if x2d.dtype != torch.bfloat16:
+        x2d = x2d.to(torch.bfloat16)
+    return _W8A8TrainableFn.apply(x2d, wq, sw, sink).reshape(*lead, wq.shape[0])
+
+
 def w8a8_linear(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
                 bias: torch.Tensor | None = None) -> torch.Tensor:
     """Functional W8A8 linear over [..., K] -> [..., N] (bf16 compute, input dtype out)."""
@@ -320,3 +349,70 @@ def w8a8_linear(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
     if in_dtype != torch.bfloat16 and in_dtype.is_floating_point:
         y = y.to(in_dtype)
     return y
+
+
+def _offsets_array(offsets) -> tuple[C.Array, int]:
+    offs = [int(o) for o in offsets]
+    return (C.c_int64 * len(offs))(*offs), len(offs) - 1
+
+
+def grouped_w8a8_dgrad(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                       offsets: list[int]) -> torch.Tensor:
+    """Per-expert straight-through dgrad: rows of expert e get dy . bf16(wq[e] * sw[e]).
+    dy [T, N] bf16 sorted by expert, wq [E, N, K] int8, sw [E, N]."""
+    dev = _require_cuda(dy, wq, sw)
+    dy = _rows_view(dy.to(torch.bfloat16))
+    E, Nn, K = wq.shape
+    if wq.stride(2) != 1 or wq.stride(0) != Nn * wq.stride(1):
+        raise ValueError("expert weights must be stacked contiguously: [E, N, ldw]")
+    offs, E2 = _offsets_array(offsets)
+    if E2 != E:
+        raise ValueError("offsets must have E+1 entries")
+    ldt = pad_to(max(Nn, 1), 8)
+    ws = torch.empty(E, K, ldt, dtype=torch.bfloat16, device=dev)
+    T = dy.shape[0]
+    dx = torch.empty(T, K, dtype=torch.bfloat16, device=dev)
+    N.call("lema_grouped_w8a8_dgrad", _ptr(dy), _ld(dy), _ptr(wq), wq.stride(1),
+           _ptr(sw.contiguous().float()), _ptr(dx), K, _ptr(ws), ldt, offs, E, Nn, K,
+           _stream(dev))
+    return dx
+
+
+def grouped_bf16_gemm_tn(a: torch.Tensor, b: torch.Tensor, offsets: list[int]) -> torch.Tensor:
+    """Rows [offsets[e], offsets[e+1]) of a times b[e]^T; a [T, K], b [E, N, K] bf16."""
+    dev = _require_cuda(a, b)
+    a = _rows_view(a)
+    E, Nn, K = b.shape
+    offs, E2 = _offsets_array(offsets)
+    if E2 != E:
+        raise ValueError("offsets must have E+1 entries")
+    y = torch.empty(a.shape[0], Nn, dtype=torch.bfloat16, device=dev)
+    N.call("lema_grouped_bf16_gemm_tn", _ptr(a), _ld(a), _ptr(b), b.stride(1), _ptr(y), Nn,
+           offs, E, Nn, K, _stream(dev))
+    return y
+
+
+def bf16_gemm_tn_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """fp32 y = a . b^T (bf16 operands, fp32 accumulators returned as is)."""
+    dev = _require_cuda(a, b)
+    a = _rows_view(a.to(torch.bfloat16))
+    b = _rows_view(b.to(torch.bfloat16))
+    M, K = a.shape
+    Nn = b.shape[0]
+    y = torch.empty(M, Nn, dtype=torch.float32, device=dev)
+    N.call("lema_bf16_gemm_tn_f32", _ptr(a), _ld(a), _ptr(b), _ld(b), _ptr(y), Nn, M, Nn, K,
+           _stream(dev))
+    return y
+
+
+def w8a8_wgrad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """Straight-through weight gradient of a W8A8 projection: dW[N, K] = dy^T . x
+    (bf16 inputs, fp32 accumulation) for dy [M, N], x [M, K]."""
+    dyt = dy.to(torch.bfloat16).t().contiguous()
+    xt = x.to(torch.bfloat16).t().contiguous()
+    K = xt.shape[0]
+    if (dyt.shape[1] * 2) % 16 != 0:  # TMA row pitch: pad the token dimension
+        M8 = pad_to(dyt.shape[1], 8)
+        dyt = torch.nn.functional.pad(dyt, (0, M8 - dyt.shape[1]))
+        xt = torch.nn.functional.pad(xt, (0, M8 - xt.shape[1]))
+    return bf16_gemm_tn_f32(dyt, xt) if K else torch.zeros(dyt.shape[0], 0, device=dy.device)

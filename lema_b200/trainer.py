@@ -16,6 +16,8 @@
   blocks still resident at the turnaround are reused without re-upload; each
   finished layer's LoRA gradients start their data-parallel all-reduce
   (NCCL) while the next layer computes;
+* selective full fine-tuning (reference :169-181, src/lema/_full_ft.py) of
+  chosen projections of chosen layers, see ``full_ft.SelectiveFullFT``;
 * optimizer (reference :183-187): every ``grad_accum`` micro-steps (the loss
   is divided by ``grad_accum`` as at reference :156), clip_grad_norm_(1.0) and
   AdamW over the LoRA parameters; with data parallelism the LoRA gradients
@@ -74,7 +76,11 @@ class StreamedLoraTrainer:
     def __init__(self, shape: LlamaShape, device, batch: int, seq: int, lora_rank: int = 16,
                  lora_alpha: float = 32.0, targets: tuple[str, ...] = ("q_proj", "v_proj"),
                  lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0, ckpt_mode: int = 0,
-                 resident_layers: int = 0, grad_accum: int = 1, group=None):
+                 resident_layers: int = 0, grad_accum: int = 1,
+                 gradient_checkpointing: bool = False, attn_chunk: int = 0,
+                 full_ft_layers: tuple[int, ...] = (),
+                 full_ft_modules: tuple[str, ...] = ("q_proj", "k_proj", "v_proj", "o_proj"),
+                 group=None):
         self.shape = shape
         self.device = torch.device(device)
         self.batch, self.seq = batch, seq
@@ -94,11 +100,14 @@ class StreamedLoraTrainer:
             p.requires_grad_(False)
         # int8 segments of every block in pinned RAM (quantised once, on the device)
         self.ws = WeightSegments(shape, self.L, dev)
+        true_weights = {}
         for b in range(self.L):
             tensors = {}
             for name, (o, i) in shape.proj_shapes().items():
                 w = torch.empty(o, i, device=dev, dtype=torch.bfloat16).normal_(0.0, 0.02,
                                                                                  generator=g)
+                if b in full_ft_layers and name in full_ft_modules:
+                    true_weights[(b, name)] = w
                 wq, sw = ops.quantize_weight(w)
                 tensors[name + ".wq"] = wq
                 tensors[name + ".sw"] = sw
@@ -112,7 +121,10 @@ class StreamedLoraTrainer:
         # two block modules, bound per layer (the reference's module pool)
         self.blocks = [LlamaBlock(shape, quantized=True, device=dev) for _ in range(2)]
         for blk in self.blocks:
-            apply_lora(blk, lora_rank, lora_alpha, targets)
+            if targets:
+                apply_lora(blk, lora_rank, lora_alpha, targets)
+            blk.gradient_checkpointing = gradient_checkpointing
+            blk.self_attn.attn_chunk = attn_chunk
         # LoRA parameters per layer, reference init (A kaiming-uniform, B zeros)
         self.lora: list[dict[str, tuple[nn.Parameter, nn.Parameter]]] = []
         for _ in range(self.L):
@@ -126,7 +138,14 @@ class StreamedLoraTrainer:
                                                         dtype=torch.bfloat16)))
             self.lora.append(layer)
         self.params = [p for layer in self.lora for ab in layer.values() for p in ab]
-        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=True)
+        self.opt = (torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=True)
+                    if self.params else None)
+        self.full_ft = None
+        if true_weights:
+            from .full_ft import SelectiveFullFT
+            self.full_ft = SelectiveFullFT(self.ws, sorted({b for b, _ in true_weights}),
+                                           full_ft_modules, true_weights, dev, lr, weight_decay)
+            del true_weights
         self.ckpt = ActivationCheckpointStore(self.L, (batch, seq, shape.hidden), dev,
                                               mode=ckpt_mode, h2d_stream=self.ws.h2d_stream)
         self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
@@ -157,6 +176,8 @@ class StreamedLoraTrainer:
             m = blk.projection(name)
             m.lora_A = a
             m.lora_B = b
+        if self.full_ft is not None:
+            self.full_ft.attach(layer, blk)
         return blk
 
     def _bind_resident(self, blk: LlamaBlock, layer: int) -> None:
@@ -215,12 +236,25 @@ class StreamedLoraTrainer:
             del out, x
             self._release(i)
             if stepping:
-                self.reducer.launch([p.grad for ab in self.lora[i].values() for p in ab])
+                grads = [p.grad for ab in self.lora[i].values() for p in ab]
+                if self.full_ft is not None:
+                    grads += self.full_ft.layer_grads(i)
+                self.reducer.launch(grads)
         if stepping:
             self.reducer.finish()
-            torch.nn.utils.clip_grad_norm_(self.params, 1.0)
-            self.opt.step()
-            self.opt.zero_grad(set_to_none=False)
+            if self.opt is not None:
+                torch.nn.utils.clip_grad_norm_(self.params, 1.0)
+                self.opt.step()
+                self.opt.zero_grad(set_to_none=False)
+            if self.full_ft is not None:
+                self.full_ft.step()
+                # the selected layers' int8 segments changed: drop stale copies
+                for s in (0, 1):
+                    if self.slot_layer[s] in self.full_ft.layers:
+                        self.slot_layer[s] = -1
+                for b in self.full_ft.layers:
+                    if b < len(self.resident):
+                        self.resident[b].copy_(self.ws.ram[b])
             self.global_step += 1
         return loss.detach()
 

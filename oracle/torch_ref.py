@@ -85,3 +85,49 @@ def swap_linears(module: nn.Module, names=("q_proj", "k_proj", "v_proj", "o_proj
                     child.base_layer = OracleW8A8Linear.from_linear(child.base_layer)
             elif isinstance(child, nn.Linear) and not isinstance(child, OracleW8A8Linear):
                 setattr(parent, name, OracleW8A8Linear.from_linear(child))
+
+
+class OracleExperts(nn.Module):
+    """CPU MoE experts on the oracle's W8A8 arithmetic, looping over experts the
+    way HF MixtralExperts does: per expert, OracleW8A8Linear(gate_up[e]) on the
+    routed token rows, silu(gate) * up, OracleW8A8Linear(down[e]), times the
+    routing weight (fp32), cast to bf16, index_add into the output."""
+
+    def __init__(self, gate_up: torch.Tensor, down: torch.Tensor):
+        super().__init__()
+        self.gu = nn.ModuleList(OracleW8A8Linear(gate_up[e]) for e in range(gate_up.shape[0]))
+        self.dn = nn.ModuleList(OracleW8A8Linear(down[e]) for e in range(down.shape[0]))
+
+    def forward(self, x2d, top_i, top_w):
+        final = torch.zeros_like(x2d)
+        E = len(self.gu)
+        mask = torch.nn.functional.one_hot(top_i, num_classes=E).permute(2, 1, 0)
+        for e in range(E):
+            pos, tok = torch.where(mask[e])
+            if tok.numel() == 0:
+                continue
+            gate, up = self.gu[e](x2d[tok]).chunk(2, dim=-1)
+            h = self.dn[e](torch.nn.functional.silu(gate) * up)
+            h = h * top_w[tok, pos, None]
+            final.index_add_(0, tok, h.to(final.dtype))
+        return final
+
+
+def adamw_step_ref(w_bf16: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray, step: int,
+                   lr: float, wd: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """numpy fp32 restatement of the reference's per-layer AdamW
+    (src/lema/_full_ft.py:204-229): decoupled weight decay, bias-corrected
+    moments, eps 1e-8, the update in fp32, the weight stored back in bf16.
+    w_bf16 is bf16 bits; returns (new weight bits, m, v)."""
+    beta1, beta2, eps = np.float32(0.9), np.float32(0.999), np.float32(1e-8)
+    b1 = 1 - 0.9 ** step
+    b2 = 1 - 0.999 ** step
+    w = O.bf16_bits_to_f32(w_bf16).astype(np.float32)
+    g = g.astype(np.float32)
+    if wd:
+        w = (w * np.float32(1 - lr * wd)).astype(np.float32)
+    m = (m * beta1 + g * np.float32(1 - 0.9)).astype(np.float32)
+    v = (v * beta2 + g * g * np.float32(1 - 0.999)).astype(np.float32)
+    denom = (np.sqrt(v) / np.float32(np.sqrt(b2)) + eps).astype(np.float32)
+    w = (w + np.float32(-(lr / b1)) * (m / denom)).astype(np.float32)
+    return O.f32_to_bf16_bits(w), m, v

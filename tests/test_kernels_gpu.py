@@ -335,3 +335,40 @@ def test_grouped_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
         acc = oracle.c_int8_gemm(xqn[r0:r1], wqn[e])
         ref = oracle.c_epilogue(acc, sxn[r0:r1], swn[e], None)
         np.testing.assert_array_equal(bits(y[r0:r1].contiguous()), ref, err_msg=f"expert {e}")
+
+
+@pytest.mark.parametrize("path", ["1sm128", "pair"])
+def test_grouped_dgrad_matches_oracle(cuda_device, oracle, monkeypatch, path):
+    """Per-expert straight-through dgrad over rows sorted by expert (empty and
+    ragged experts included) against the oracle's dequant + double GEMM."""
+    monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    dev = cuda_device
+    E, N, K = 5, 640, 384
+    counts = [300, 0, 129, 1, 200]
+    offsets = np.concatenate([[0], np.cumsum(counts)]).tolist()
+    T = offsets[-1]
+    w = rand_bf16((E * N, K), seed=51, scale=0.02, outliers=False)
+    wq, sw = ops.quantize_rows(w.to(dev))
+    dy = rand_bf16((T, N), seed=52, outliers=False)
+    dx = ops.grouped_w8a8_dgrad(dy.to(dev), wq.reshape(E, N, K), sw.reshape(E, N), offsets)
+    wqn, swn = wq.cpu().numpy().reshape(E, N, K), sw.cpu().numpy().reshape(E, N)
+    for e in range(E):
+        r0, r1 = offsets[e], offsets[e + 1]
+        if r1 == r0:
+            continue
+        wdT = oracle.c_dequant_transpose(wqn[e], swn[e])
+        _, ref = oracle.c_bf16_gemm_tn(bits(dy[r0:r1].contiguous()), wdT)
+        _dgrad_tol_check(bits(dx[r0:r1].contiguous()), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (77, 300, 200)])
+def test_wgrad_fp32_accumulators(cuda_device, oracle, M, N, K):
+    """dW = dy^T . x with fp32 output against a double-accumulated reference."""
+    dev = cuda_device
+    dy = rand_bf16((M, N), seed=61, outliers=False)
+    x = rand_bf16((M, K), seed=62, outliers=False)
+    dw = ops.w8a8_wgrad(dy.to(dev), x.to(dev)).cpu().numpy()
+    _, ref = oracle.c_bf16_gemm_tn(bits(dy.t().contiguous()), bits(x.t().contiguous()))
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+    err = np.abs(dw - ref)
+    assert np.all(err <= 1e-5 * np.abs(ref) + 1e-6 * rms + 1e-30), err.max()

@@ -59,3 +59,19 @@ def test_oracle_block_reproduces_reference_fixture():
         m = blk.projection(proj)
         assert (torch_bf16_to_bits(m.lora_A.grad) == d[f"grad/self_attn.{proj}.lora_A"]).all()
         assert (torch_bf16_to_bits(m.lora_B.grad) == d[f"grad/self_attn.{proj}.lora_B"]).all()
+
+
+def test_chunked_attention_equals_full_attention():
+    """Query-chunked causal attention (the reference's chunked_attention shape of
+    computation, used for long sequences) equals full causal attention."""
+    shape = LlamaShape(hidden=64, heads=4, kv_heads=2, intermediate=160, vocab=100, layers=1)
+    torch.manual_seed(1)
+    blk = LlamaBlock(shape, quantized=False, dtype=torch.float32)
+    for p in blk.parameters():
+        torch.nn.init.normal_(p, std=0.05)
+    x = torch.randn(2, 130, 64)
+    cos, sin = rope_cos_sin(shape, 130, "cpu", torch.float32)
+    full = blk(x, cos, sin)
+    blk.self_attn.attn_chunk = 32
+    chunked = blk(x, cos, sin)
+    assert torch.allclose(full, chunked, atol=1e-6, rtol=1e-5)

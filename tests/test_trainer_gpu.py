@@ -125,3 +125,20 @@ def test_trainer_kernel_mode_checkpoint(cuda_device):
     assert out[0] == out[2]
     for a, b in zip(out[1], out[3]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_attention_checkpointing_gives_the_same_step(cuda_device):
+    """gradient_checkpointing=True re-runs attention inside backward (the
+    reference's intra-layer recompute); the step must not change."""
+    ids = _ids(17, 2, 64, SMALL.vocab, cuda_device)
+    out = []
+    for gc in (False, True):
+        tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=1e-3, seed=4,
+                                 gradient_checkpointing=gc)
+        with sdpa_kernel(SDPBackend.MATH):
+            out.append(float(tr.train_step(ids)))
+        out.append([p.detach().clone() for p in tr.params])
+        tr.close()
+    assert out[0] == out[2]
+    for a, b in zip(out[1], out[3]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
