@@ -32,7 +32,7 @@ def test_full_ft_step_requantises_and_matches_reference_adamw(cuda_device):
     tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, targets=(), lr=1e-3,
                              weight_decay=0.01, seed=5, full_ft_layers=(2, 3))
     ft = tr.full_ft
-    before = {k: O.torch_bf16_to_bits(w) for k, w in ft.true.items()}
+    before = {k: O.torch_bf16_to_bits(w).copy() for k, w in ft.true.items()}  # not a view
     grads = {}
     orig = ft.step_layer
 

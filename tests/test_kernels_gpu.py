@@ -363,7 +363,8 @@ def test_grouped_dgrad_matches_oracle(cuda_device, oracle, monkeypatch, path):
 
 @pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (77, 300, 200)])
 def test_wgrad_fp32_accumulators(cuda_device, oracle, M, N, K):
-    """dW = dy^T . x with fp32 output against a double-accumulated reference."""
+    """dW = dy^T . x with fp32 output against a double-accumulated reference; the
+    bar is fp32 accumulation-order noise: 2e-5 * |ref| + 1e-5 * rms(ref)."""
     dev = cuda_device
     dy = rand_bf16((M, N), seed=61, outliers=False)
     x = rand_bf16((M, K), seed=62, outliers=False)
@@ -371,4 +372,4 @@ def test_wgrad_fp32_accumulators(cuda_device, oracle, M, N, K):
     _, ref = oracle.c_bf16_gemm_tn(bits(dy.t().contiguous()), bits(x.t().contiguous()))
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     err = np.abs(dw - ref)
-    assert np.all(err <= 1e-5 * np.abs(ref) + 1e-6 * rms + 1e-30), err.max()
+    assert np.all(err <= 2e-5 * np.abs(ref) + 1e-5 * rms + 1e-30), err.max()
