@@ -152,6 +152,45 @@ LEMA_API int lema_w8a8_dgrad(const void* dy_bf16, int64_t lddy,
                     void* dx_bf16, int64_t lddx, void* wdT_ws, int64_t ldt,
                     int64_t M, int64_t N, int64_t K, void* stream);
 
+/* ---- Fused producers of the W8A8 GEMM inputs (and their backward) ------ */
+/* RMSNorm of HF LlamaRMSNorm as adapters/_llama.py:238,248 apply it, in bf16:
+ * hn = bf16(g * bf16(x * rsqrt(mean(x^2) + eps))) per row; rstd[r] (fp32) for
+ * the backward; when q is not NULL also the per-row int8 quantisation of hn
+ * (the lema_quantize_rows rule) for the projections that read it. cols % 8 == 0,
+ * cols <= 16384, 16-byte aligned rows. */
+LEMA_API int lema_rmsnorm_quant(const void* x_bf16, int64_t ldx, const void* g_bf16,
+                                int64_t rows, int64_t cols, float eps, void* hn_bf16,
+                                int64_t ldh, int8_t* q, int64_t ldq, float* scale, float* rstd,
+                                void* stream);
+
+/* dx = rstd * (g*dhn - xhat * mean(g*dhn*xhat)), xhat = x * rstd (fp32, bf16 out). */
+LEMA_API int lema_rmsnorm_bwd(const void* x_bf16, int64_t ldx, const void* g_bf16,
+                              const float* rstd, const void* dhn_bf16, int64_t ldd,
+                              int64_t rows, int64_t cols, void* dx_bf16, int64_t lddx,
+                              void* stream);
+
+/* Rotary embedding of q and k rows (token t = b*seq + s uses cos/sin row s,
+ * [seq, head_dim] bf16): mode 0 = forward with the bf16 roundings of
+ * q*cos + rotate_half(q)*sin (HF apply_rotary_pos_emb, reached from
+ * adapters/_llama.py:242); mode 1 = backward (transposed rotation). Inputs may
+ * be strided rows (ld in elements); outputs are contiguous [tokens, heads*dim]. */
+LEMA_API int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int64_t ldk_in,
+                       const void* cos_bf16, const void* sin_bf16, int64_t tokens, int32_t seq,
+                       int32_t heads_q, int32_t heads_k, int32_t head_dim, void* q_out,
+                       void* k_out, int32_t mode, void* stream);
+
+/* SwiGLU of HF LlamaMLP (act(gate) * up) on rows of [gate | up] ([rows, 2*inter],
+ * row stride ldgu), quantised per row (lema_quantize_rows rule) for the down
+ * projection; m_bf16 (may be NULL) receives the bf16 product. */
+LEMA_API int lema_swiglu_quant(const void* gu_bf16, int64_t ldgu, int64_t rows, int64_t inter,
+                               int8_t* q, int64_t ldq, float* scale, void* m_bf16, int64_t ldm,
+                               void* stream);
+
+/* d[gate | up] from dm and the saved [gate | up] (fp32 math, bf16 out). */
+LEMA_API int lema_swiglu_bwd(const void* gu_bf16, int64_t ldgu, const void* dm_bf16,
+                             int64_t lddm, int64_t rows, int64_t inter, void* dgu_bf16,
+                             int64_t lddgu, void* stream);
+
 /* ---- K6: grouped W8A8 GEMM (MoE experts) -------------------------------- */
 /* Tokens are pre-sorted by expert: rows [offsets[e], offsets[e+1]) of xq/sx/y
  * belong to expert e, whose weights are wq + e*N*ldw, sw + e*N and

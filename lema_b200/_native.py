@@ -41,6 +41,11 @@ _SIGNATURES: dict[str, list] = {
     "lema_grouped_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, i64, i64, vp],
+    "lema_rmsnorm_quant": [vp, i64, vp, i64, i64, C.c_float, vp, i64, vp, i64, vp, vp, vp],
+    "lema_rmsnorm_bwd": [vp, i64, vp, vp, vp, i64, i64, i64, vp, i64, vp],
+    "lema_rope": [vp, i64, vp, i64, vp, vp, i64, i32, i32, i32, i32, vp, vp, i32, vp],
+    "lema_swiglu_quant": [vp, i64, i64, i64, vp, i64, vp, vp, i64, vp],
+    "lema_swiglu_bwd": [vp, i64, vp, i64, i64, i64, vp, i64, vp],
     "lema_ckpt_save": [vp, vp, sz, i32, vp, vp, vp],
     "lema_ckpt_restore": [vp, vp, sz, vp, vp, vp],
     "lema_mm_create": [i64, i64, i32, C.POINTER(vp)],

@@ -1,0 +1,447 @@
+// fused.cu — producers that feed the W8A8 GEMMs of a decoder block without
+// extra HBM round trips, and their backward kernels:
+//
+//   rmsnorm_quant   hn = bf16(g * bf16(x * rsqrt(mean(x^2) + eps))) per row
+//                   (the rounding sequence of HF LlamaRMSNorm in bf16), plus the
+//                   per-row int8 quantisation of hn (the K1 rule) for the
+//                   following projections, plus rstd for the backward.
+//   rmsnorm_bwd     dx = rstd * (g*dhn - xhat * mean(g*dhn*xhat)), xhat = x*rstd (fp32).
+//   rope            out = bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)) per head
+//                   (torch's rounding of q*cos + rotate_half(q)*sin in bf16),
+//                   reading strided q/k rows and writing contiguous rows; the
+//                   backward applies the transposed rotation in fp32.
+//   swiglu_quant    m = bf16(bf16(silu(gate)) * up) per row of [gate | up],
+//                   quantised per row (K1 rule) for the down projection.
+//   swiglu_bwd      d[gate | up] from dm and the saved [gate | up].
+//
+// All are HBM-bound; one CTA (128 threads) per row keeps the row in registers
+// (16-byte vectors) so each input byte is read once.
+#include <cuda_bf16.h>
+
+#include "internal.h"
+
+namespace lema {
+namespace {
+
+constexpr int kThreads = 128;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+
+// Quantiser of the operator contract: rint(x / s) clamped to +-127, the quotient
+// formed as a reciprocal product and re-done as an exact division near ties or
+// when the scale is subnormal (same rule as quantize.cu).
+__device__ __forceinline__ int8_t q1(float x, float s, float inv_s) {
+  const float y = __fmul_rn(x, inv_s);
+  const float frac = fabsf(y - truncf(y));
+  const float q0 = (inv_s == 0.f || fabsf(frac - 0.5f) < 1e-4f) ? __fdiv_rn(x, s) : y;
+  int q = __float2int_rn(q0);
+  q = max(-127, min(127, q));
+  return static_cast<int8_t>(q);
+}
+
+__device__ __forceinline__ void row_scale(float amax, float& s, float& inv_s) {
+  s = amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
+  inv_s = s >= 1.17549435e-38f ? __frcp_rn(s) : 0.f;
+}
+
+union V8 {
+  uint4 u;
+  __nv_bfloat16 h[8];
+};
+
+// ---------------------------------------------------------------- RMSNorm
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ g,
+    int cols, float eps, __nv_bfloat16* __restrict__ hn, int64_t ldh, int8_t* __restrict__ q,
+    int64_t ldq, float* __restrict__ scale, float* __restrict__ rstd_out) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const int nvec = cols / 8;
+  V8 v[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      v[i].u = __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = __bfloat162float(v[i].h[j]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float rstd = rsqrtf(ss / static_cast<float>(cols) + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      V8 gv;
+      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __nv_bfloat16 xh = __float2bfloat16_rn(__bfloat162float(v[i].h[j]) * rstd);
+        const __nv_bfloat16 o =
+            __float2bfloat16_rn(__bfloat162float(gv.h[j]) * __bfloat162float(xh));
+        v[i].h[j] = o;
+        amax = fmaxf(amax, fabsf(__bfloat162float(o)));
+      }
+      reinterpret_cast<uint4*>(hn + row * ldh)[idx] = v[i].u;
+    }
+  }
+  if (q != nullptr) {
+    amax = block_max(amax, red);
+    float s, inv_s;
+    row_scale(amax, s, inv_s);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nvec) {
+        __align__(8) int8_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = q1(__bfloat162float(v[i].h[j]), s, inv_s);
+        *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
+            *reinterpret_cast<const uint2*>(o);
+      }
+    }
+    if (threadIdx.x == 0) scale[row] = s;
+  }
+  if (threadIdx.x == 0 && rstd_out != nullptr) rstd_out[row] = rstd;
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ g,
+    const float* __restrict__ rstd_in, const __nv_bfloat16* __restrict__ dhn, int64_t ldd,
+    int cols, __nv_bfloat16* __restrict__ dx, int64_t lddx) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const int nvec = cols / 8;
+  const float rstd = rstd_in[row];
+  V8 xv[VPT], dv[VPT];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      xv[i].u = __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+      dv[i].u = __ldg(reinterpret_cast<const uint4*>(dhn + row * ldd) + idx);
+      V8 gv;
+      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float gd = __bfloat162float(gv.h[j]) * __bfloat162float(dv[i].h[j]);
+        dot = fmaf(gd, __bfloat162float(xv[i].h[j]) * rstd, dot);
+      }
+    }
+  }
+  dot = block_sum(dot, red) / static_cast<float>(cols);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      V8 gv, out;
+      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xhat = __bfloat162float(xv[i].h[j]) * rstd;
+        const float gd = __bfloat162float(gv.h[j]) * __bfloat162float(dv[i].h[j]);
+        out.h[j] = __float2bfloat16_rn(rstd * (gd - xhat * dot));
+      }
+      reinterpret_cast<uint4*>(dx + row * lddx)[idx] = out.u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- RoPE
+// One thread handles 8 consecutive dims i..i+7 of the first half of one head
+// and their partners i+d/2.. of one token. mode 0: forward with torch's bf16
+// roundings; mode 1: backward (transposed rotation, fp32, one rounding).
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ q_in, int64_t ldq_in,
+                            const __nv_bfloat16* __restrict__ k_in, int64_t ldk_in,
+                            const __nv_bfloat16* __restrict__ cosv,
+                            const __nv_bfloat16* __restrict__ sinv, int64_t tokens, int seq,
+                            int hq, int hk, int d, __nv_bfloat16* __restrict__ q_out,
+                            __nv_bfloat16* __restrict__ k_out, int mode) {
+  const int half = d / 2;
+  const int groups = half / 8;  // 8-wide groups per head half
+  const int per_token = (hq + hk) * groups;
+  const int64_t gid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (gid >= tokens * per_token) return;
+  const int64_t t = gid / per_token;
+  int r = static_cast<int>(gid % per_token);
+  const bool is_q = r < hq * groups;
+  if (!is_q) r -= hq * groups;
+  const int head = r / groups, grp = r % groups;
+  const int s = static_cast<int>(t % seq);
+  const __nv_bfloat16* src = is_q ? q_in + t * ldq_in : k_in + t * ldk_in;
+  __nv_bfloat16* dst = is_q ? q_out + t * static_cast<int64_t>(hq) * d
+                            : k_out + t * static_cast<int64_t>(hk) * d;
+  const int i0 = head * d + grp * 8;
+  V8 a, b, c1, s1, c2, s2, oa, ob;
+  a.u = *reinterpret_cast<const uint4*>(src + i0);
+  b.u = *reinterpret_cast<const uint4*>(src + i0 + half);
+  c1.u = *reinterpret_cast<const uint4*>(cosv + static_cast<int64_t>(s) * d + grp * 8);
+  s1.u = *reinterpret_cast<const uint4*>(sinv + static_cast<int64_t>(s) * d + grp * 8);
+  c2.u = *reinterpret_cast<const uint4*>(cosv + static_cast<int64_t>(s) * d + half + grp * 8);
+  s2.u = *reinterpret_cast<const uint4*>(sinv + static_cast<int64_t>(s) * d + half + grp * 8);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float xa = __bfloat162float(a.h[j]), xb = __bfloat162float(b.h[j]);
+    if (mode == 0) {
+      // out[i] = x[i]c[i] + (-x[i+h]) s[i];  out[i+h] = x[i+h]c[i+h] + x[i] s[i+h]
+      const float ta = __bfloat162float(__float2bfloat16_rn(xa * __bfloat162float(c1.h[j])));
+      const float tb = __bfloat162float(__float2bfloat16_rn(-xb * __bfloat162float(s1.h[j])));
+      oa.h[j] = __float2bfloat16_rn(ta + tb);
+      const float tc = __bfloat162float(__float2bfloat16_rn(xb * __bfloat162float(c2.h[j])));
+      const float td = __bfloat162float(__float2bfloat16_rn(xa * __bfloat162float(s2.h[j])));
+      ob.h[j] = __float2bfloat16_rn(tc + td);
+    } else {
+      // dx[i] = dout[i]c[i] + dout[i+h]s[i+h];  dx[i+h] = dout[i+h]c[i+h] - dout[i]s[i]
+      oa.h[j] = __float2bfloat16_rn(xa * __bfloat162float(c1.h[j]) +
+                                    xb * __bfloat162float(s2.h[j]));
+      ob.h[j] = __float2bfloat16_rn(xb * __bfloat162float(c2.h[j]) -
+                                    xa * __bfloat162float(s1.h[j]));
+    }
+  }
+  *reinterpret_cast<uint4*>(dst + i0) = oa.u;
+  *reinterpret_cast<uint4*>(dst + i0 + half) = ob.u;
+}
+
+// ---------------------------------------------------------------- SwiGLU
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(
+    const __nv_bfloat16* __restrict__ gu, int64_t ldgu, int inter, int8_t* __restrict__ q,
+    int64_t ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ m_out, int64_t ldm) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const int nvec = inter / 8;
+  const __nv_bfloat16* gate = gu + row * ldgu;
+  const __nv_bfloat16* up = gate + inter;
+  V8 mv[VPT];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      V8 gv, uv;
+      gv.u = __ldg(reinterpret_cast<const uint4*>(gate) + idx);
+      uv.u = __ldg(reinterpret_cast<const uint4*>(up) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __nv_bfloat16 a = __float2bfloat16_rn(silu_f(__bfloat162float(gv.h[j])));
+        const __nv_bfloat16 m =
+            __float2bfloat16_rn(__bfloat162float(a) * __bfloat162float(uv.h[j]));
+        mv[i].h[j] = m;
+        amax = fmaxf(amax, fabsf(__bfloat162float(m)));
+      }
+      if (m_out != nullptr) reinterpret_cast<uint4*>(m_out + row * ldm)[idx] = mv[i].u;
+    }
+  }
+  amax = block_max(amax, red);
+  float s, inv_s;
+  row_scale(amax, s, inv_s);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nvec) {
+      __align__(8) int8_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = q1(__bfloat162float(mv[i].h[j]), s, inv_s);
+      *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
+          *reinterpret_cast<const uint2*>(o);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
+                                  const __nv_bfloat16* __restrict__ dm, int64_t lddm,
+                                  int64_t rows, int inter, __nv_bfloat16* __restrict__ dgu,
+                                  int64_t lddgu) {
+  const int per_row = inter / 8;
+  const int64_t gid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (gid >= rows * per_row) return;
+  const int64_t r = gid / per_row;
+  const int c = static_cast<int>(gid % per_row) * 8;
+  V8 gv, uv, dv, og, ou;
+  gv.u = *reinterpret_cast<const uint4*>(gu + r * ldgu + c);
+  uv.u = *reinterpret_cast<const uint4*>(gu + r * ldgu + inter + c);
+  dv.u = *reinterpret_cast<const uint4*>(dm + r * lddm + c);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float g = __bfloat162float(gv.h[j]), u = __bfloat162float(uv.h[j]);
+    const float d = __bfloat162float(dv.h[j]);
+    const float sg = 1.f / (1.f + expf(-g));
+    og.h[j] = __float2bfloat16_rn(d * u * (sg * (1.f + g * (1.f - sg))));
+    ou.h[j] = __float2bfloat16_rn(d * g * sg);
+  }
+  *reinterpret_cast<uint4*>(dgu + r * lddgu + c) = og.u;
+  *reinterpret_cast<uint4*>(dgu + r * lddgu + inter + c) = ou.u;
+}
+
+int vpt_for(int cols) {
+  const int nv = (cols / 8 + kThreads - 1) / kThreads;
+  if (nv <= 4) return 4;
+  if (nv <= 8) return 8;
+  if (nv <= 12) return 12;
+  if (nv <= 16) return 16;
+  return 0;
+}
+
+bool rows_ok(const void* p, int64_t ld) { return aligned16(p) && ld % 8 == 0; }
+
+}  // namespace
+}  // namespace lema
+
+using namespace lema;
+
+// Launches KERNEL<VPT> for the register-vector count chosen by vpt_for();
+// ARGS is the parenthesised kernel argument list, the rest the launch config.
+#define LEMA_VPT_LAUNCH(vpt, KERNEL, ARGS, ...)              \
+  switch (vpt) {                                             \
+    case 4: KERNEL<4><<<__VA_ARGS__>>> ARGS; break;          \
+    case 8: KERNEL<8><<<__VA_ARGS__>>> ARGS; break;          \
+    case 12: KERNEL<12><<<__VA_ARGS__>>> ARGS; break;        \
+    default: KERNEL<16><<<__VA_ARGS__>>> ARGS; break;        \
+  }
+
+extern "C" int lema_rmsnorm_quant(const void* x_bf16, int64_t ldx, const void* g_bf16,
+                                  int64_t rows, int64_t cols, float eps, void* hn_bf16,
+                                  int64_t ldh, int8_t* q, int64_t ldq, float* scale, float* rstd,
+                                  void* stream) {
+  clear_error();
+  if (rows < 0 || cols <= 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size");
+  if (rows == 0) return LEMA_OK;
+  if (!x_bf16 || !g_bf16 || !hn_bf16 || (q && !scale))
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  const int vpt = vpt_for(static_cast<int>(cols));
+  if (cols % 8 != 0 || vpt == 0 || cols > INT32_MAX || rows > INT32_MAX)
+    return set_error(LEMA_ERR_UNSUPPORTED, "rmsnorm_quant needs cols % 8 == 0, cols <= 16384");
+  if (!rows_ok(x_bf16, ldx) || !rows_ok(hn_bf16, ldh) || !aligned16(g_bf16) ||
+      (q && (reinterpret_cast<uintptr_t>(q) % 8 != 0 || ldq % 8 != 0)))
+    return set_error(LEMA_ERR_MISALIGNED, "rmsnorm_quant needs 16-byte aligned rows");
+  auto s = static_cast<cudaStream_t>(stream);
+  LEMA_VPT_LAUNCH(vpt, rmsnorm_quant_kernel, (
+      static_cast<const __nv_bfloat16*>(x_bf16), ldx, static_cast<const __nv_bfloat16*>(g_bf16),
+      static_cast<int>(cols), eps, static_cast<__nv_bfloat16*>(hn_bf16), ldh, q, ldq, scale,
+      rstd),
+                  static_cast<unsigned>(rows), kThreads, 0, s);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_rmsnorm_bwd(const void* x_bf16, int64_t ldx, const void* g_bf16,
+                                const float* rstd, const void* dhn_bf16, int64_t ldd,
+                                int64_t rows, int64_t cols, void* dx_bf16, int64_t lddx,
+                                void* stream) {
+  clear_error();
+  if (rows < 0 || cols <= 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size");
+  if (rows == 0) return LEMA_OK;
+  if (!x_bf16 || !g_bf16 || !rstd || !dhn_bf16 || !dx_bf16)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  const int vpt = vpt_for(static_cast<int>(cols));
+  if (cols % 8 != 0 || vpt == 0)
+    return set_error(LEMA_ERR_UNSUPPORTED, "rmsnorm_bwd needs cols % 8 == 0, cols <= 16384");
+  if (!rows_ok(x_bf16, ldx) || !rows_ok(dhn_bf16, ldd) || !rows_ok(dx_bf16, lddx) ||
+      !aligned16(g_bf16))
+    return set_error(LEMA_ERR_MISALIGNED, "rmsnorm_bwd needs 16-byte aligned rows");
+  auto s = static_cast<cudaStream_t>(stream);
+  LEMA_VPT_LAUNCH(vpt, rmsnorm_bwd_kernel, (
+      static_cast<const __nv_bfloat16*>(x_bf16), ldx, static_cast<const __nv_bfloat16*>(g_bf16),
+      rstd, static_cast<const __nv_bfloat16*>(dhn_bf16), ldd, static_cast<int>(cols),
+      static_cast<__nv_bfloat16*>(dx_bf16), lddx),
+                  static_cast<unsigned>(rows), kThreads, 0, s);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int64_t ldk_in,
+                         const void* cos_bf16, const void* sin_bf16, int64_t tokens, int32_t seq,
+                         int32_t heads_q, int32_t heads_k, int32_t head_dim, void* q_out,
+                         void* k_out, int32_t mode, void* stream) {
+  clear_error();
+  if (tokens < 0 || seq <= 0 || heads_q < 0 || heads_k < 0 || head_dim <= 0 ||
+      (mode != 0 && mode != 1))
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size or mode");
+  if (tokens == 0) return LEMA_OK;
+  if (head_dim % 16 != 0)
+    return set_error(LEMA_ERR_UNSUPPORTED, "rope needs head_dim % 16 == 0");
+  if (!q_in || !k_in || !cos_bf16 || !sin_bf16 || !q_out || !k_out)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!rows_ok(q_in, ldq_in) || !rows_ok(k_in, ldk_in) || !aligned16(q_out) ||
+      !aligned16(k_out) || !aligned16(cos_bf16) || !aligned16(sin_bf16))
+    return set_error(LEMA_ERR_MISALIGNED, "rope needs 16-byte aligned rows");
+  const int64_t work = tokens * (heads_q + heads_k) * (head_dim / 16);
+  const int64_t blocks = (work + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(LEMA_ERR_UNSUPPORTED, "too many tokens");
+  rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q_in), ldq_in, static_cast<const __nv_bfloat16*>(k_in),
+      ldk_in, static_cast<const __nv_bfloat16*>(cos_bf16),
+      static_cast<const __nv_bfloat16*>(sin_bf16), tokens, seq, heads_q, heads_k, head_dim,
+      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), mode);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_swiglu_quant(const void* gu_bf16, int64_t ldgu, int64_t rows, int64_t inter,
+                                 int8_t* q, int64_t ldq, float* scale, void* m_bf16, int64_t ldm,
+                                 void* stream) {
+  clear_error();
+  if (rows < 0 || inter <= 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size");
+  if (rows == 0) return LEMA_OK;
+  if (!gu_bf16 || !q || !scale) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  const int vpt = vpt_for(static_cast<int>(inter));
+  if (inter % 8 != 0 || vpt == 0)
+    return set_error(LEMA_ERR_UNSUPPORTED, "swiglu_quant needs inter % 8 == 0, <= 16384");
+  if (!rows_ok(gu_bf16, ldgu) || reinterpret_cast<uintptr_t>(q) % 8 != 0 || ldq % 8 != 0 ||
+      (m_bf16 && !rows_ok(m_bf16, ldm)))
+    return set_error(LEMA_ERR_MISALIGNED, "swiglu_quant needs 16-byte aligned rows");
+  auto s = static_cast<cudaStream_t>(stream);
+  LEMA_VPT_LAUNCH(vpt, swiglu_quant_kernel, (
+      static_cast<const __nv_bfloat16*>(gu_bf16), ldgu, static_cast<int>(inter), q, ldq, scale,
+      static_cast<__nv_bfloat16*>(m_bf16), ldm),
+                  static_cast<unsigned>(rows), kThreads, 0, s);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_swiglu_bwd(const void* gu_bf16, int64_t ldgu, const void* dm_bf16,
+                               int64_t lddm, int64_t rows, int64_t inter, void* dgu_bf16,
+                               int64_t lddgu, void* stream) {
+  clear_error();
+  if (rows < 0 || inter <= 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size");
+  if (rows == 0) return LEMA_OK;
+  if (!gu_bf16 || !dm_bf16 || !dgu_bf16) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (inter % 8 != 0) return set_error(LEMA_ERR_UNSUPPORTED, "swiglu_bwd needs inter % 8 == 0");
+  if (!rows_ok(gu_bf16, ldgu) || !rows_ok(dm_bf16, lddm) || !rows_ok(dgu_bf16, lddgu))
+    return set_error(LEMA_ERR_MISALIGNED, "swiglu_bwd needs 16-byte aligned rows");
+  const int64_t work = rows * (inter / 8);
+  swiglu_bwd_kernel<<<static_cast<unsigned>((work + 255) / 256), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu_bf16), ldgu, static_cast<const __nv_bfloat16*>(dm_bf16),
+      lddm, rows, static_cast<int>(inter), static_cast<__nv_bfloat16*>(dgu_bf16), lddgu);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}

@@ -194,8 +194,28 @@ class LlamaBlock(nn.Module):
         return m.base_layer if isinstance(m, LoRALinear) else m
 
     gradient_checkpointing = False
+    # Stacked int8 weights / scales of the projection groups ("qkv", "o", "gate_up",
+    # "down" + ".wq" / ".sw"), set when the block is bound to a weight segment.
+    fused_weights: dict | None = None
+    use_fused = True
+
+    def _can_fuse(self) -> bool:
+        if not (self.use_fused and self.fused_weights is not None):
+            return False
+        if self.gradient_checkpointing or self.self_attn.attn_impl != "sdpa":
+            return False
+        for name in PROJECTIONS:
+            m = self.projection(name)
+            if getattr(self.base_projection(name), "wgrad_acc", None) is not None:
+                return False  # trainable projections take the per-projection path
+            if isinstance(m, LoRALinear) and name in ("o_proj", "gate_proj", "up_proj",
+                                                      "down_proj"):
+                return False
+        return True
 
     def forward(self, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        if h.is_cuda and self._can_fuse():
+            return self._forward_fused(h, cos, sin)
         residual = h
         h = self.input_layernorm(h)
         if self.gradient_checkpointing and torch.is_grad_enabled():
@@ -210,6 +230,60 @@ class LlamaBlock(nn.Module):
         h = self.post_attention_layernorm(h)
         h = self.mlp(h)
         return residual + h
+
+
+    @torch.no_grad()
+    def build_fused_weights(self) -> None:
+        """Stacks this block's own W8A8 projections into the group tensors of the
+        fused path (a copy; streamed blocks get views of their segment instead)."""
+        def cat(names, what):
+            return torch.cat([getattr(self.base_projection(n), what) for n in names], dim=0)
+        self.fused_weights = {}
+        for group, names in (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
+                             ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",))):
+            self.fused_weights[group + ".wq"] = cat(names, "weight").contiguous()
+            self.fused_weights[group + ".sw"] = cat(names, "weight_scale").contiguous()
+
+    def _forward_fused(self, h, cos, sin):
+        """The same layer through the fused producers: RMSNorm -> quantise (one
+        kernel), one stacked q/k/v W8A8 GEMM, LoRA on q/k/v, one RoPE kernel, SDPA,
+        o_proj, residual, RMSNorm -> quantise, stacked gate/up GEMM, SwiGLU ->
+        quantise (one kernel), down GEMM, residual."""
+        from . import ops
+        sh = self.shape
+        B, S, H = h.shape
+        d = sh.head_dim
+        nq, nk = sh.heads * d, sh.kv_heads * d
+        fw = self.fused_weights
+        x2d = h.reshape(-1, H)
+        hn, xq, sx = ops.RMSNormQuantFn.apply(x2d, self.input_layernorm.weight, sh.eps)
+        q, k, v = ops.QKVFn.apply(hn, xq, sx, fw["qkv.wq"], fw["qkv.sw"], nq, nk)
+        att = self.self_attn
+        outs = []
+        for name, t in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
+            m = getattr(att, name)
+            if isinstance(m, LoRALinear):
+                t = t + (hn @ m.lora_A.transpose(0, 1) @ m.lora_B.transpose(0, 1)) * m.scaling
+            outs.append(t)
+        q, k, v = outs
+        qr, kr = ops.RopeFn.apply(q, k, cos.reshape(-1, d), sin.reshape(-1, d), S, sh.heads,
+                                  sh.kv_heads, d)
+        qv = qr.view(B, S, sh.heads, d).transpose(1, 2)
+        kv = kr.view(B, S, sh.kv_heads, d).transpose(1, 2)
+        vv = v.reshape(B, S, sh.kv_heads, d).transpose(1, 2)
+        gqa = sh.heads != sh.kv_heads
+        if att.attn_chunk and S > att.attn_chunk:
+            o = _chunked_causal_attention(qv, kv, vv, d ** -0.5, att.attn_chunk, gqa)
+        else:
+            o = F.scaled_dot_product_attention(qv, kv, vv, is_causal=True, scale=d ** -0.5,
+                                               enable_gqa=gqa)
+        o2d = o.transpose(1, 2).reshape(B * S, nq)
+        h2 = h + att.o_proj(o2d).view(B, S, H)
+        hn2, xq2, sx2 = ops.RMSNormQuantFn.apply(h2.reshape(-1, H),
+                                                 self.post_attention_layernorm.weight, sh.eps)
+        y = ops.MLPFn.apply(hn2, xq2, sx2, fw["gate_up.wq"], fw["gate_up.sw"], fw["down.wq"],
+                            fw["down.sw"])
+        return h2 + y.view(B, S, H)
 
 
 def apply_lora(block: LlamaBlock, rank: int, alpha: float,

@@ -416,3 +416,170 @@ def w8a8_wgrad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         dyt = torch.nn.functional.pad(dyt, (0, M8 - dyt.shape[1]))
         xt = torch.nn.functional.pad(xt, (0, M8 - xt.shape[1]))
     return bf16_gemm_tn_f32(dyt, xt) if K else torch.zeros(dyt.shape[0], 0, device=dy.device)
+
+
+# ---------------------------------------------------------------------------
+# Fused producers of the decoder block (RMSNorm -> quantise, RoPE, SwiGLU ->
+# quantise) and the autograd functions of the fused block path
+# ---------------------------------------------------------------------------
+
+def rmsnorm_quant(x2d: torch.Tensor, g: torch.Tensor, eps: float, want_q: bool = True):
+    """(hn bf16 [M, H], xq int8 [M, H] | None, sx fp32 [M] | None, rstd fp32 [M])."""
+    dev = _require_cuda(x2d, g)
+    x2d = _rows_view(x2d)
+    M, H = x2d.shape
+    hn = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    rstd = torch.empty(M, dtype=torch.float32, device=dev)
+    xq = sx = None
+    if want_q:
+        xq = torch.empty(M, pad_to(H, 16), dtype=torch.int8, device=dev)[:, :H]
+        sx = torch.empty(M, dtype=torch.float32, device=dev)
+    N.call("lema_rmsnorm_quant", _ptr(x2d), _ld(x2d), _ptr(g.contiguous()), M, H, float(eps),
+           _ptr(hn), H, _ptr(xq), (xq.stride(0) if xq is not None else 0), _ptr(sx), _ptr(rstd),
+           _stream(dev))
+    return hn, xq, sx, rstd
+
+
+def rmsnorm_bwd(x2d, g, rstd, dhn):
+    dev = _require_cuda(x2d, g, rstd, dhn)
+    x2d, dhn = _rows_view(x2d), _rows_view(dhn.to(torch.bfloat16))
+    M, H = x2d.shape
+    dx = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    N.call("lema_rmsnorm_bwd", _ptr(x2d), _ld(x2d), _ptr(g.contiguous()), _ptr(rstd), _ptr(dhn),
+           _ld(dhn), M, H, _ptr(dx), H, _stream(dev))
+    return dx
+
+
+def rope(q2d, k2d, cos, sin, seq: int, hq: int, hk: int, d: int, mode: int = 0):
+    """Rotary embedding of q [T, hq*d] and k [T, hk*d] rows (may be strided);
+    cos/sin [seq, d] bf16. Returns contiguous (q_out, k_out)."""
+    dev = _require_cuda(q2d, k2d, cos, sin)
+    T = q2d.shape[0]
+    qo = torch.empty(T, hq * d, dtype=torch.bfloat16, device=dev)
+    ko = torch.empty(T, hk * d, dtype=torch.bfloat16, device=dev)
+    N.call("lema_rope", _ptr(q2d), q2d.stride(0), _ptr(k2d), k2d.stride(0),
+           _ptr(cos.contiguous()), _ptr(sin.contiguous()), T, seq, hq, hk, d, _ptr(qo), _ptr(ko),
+           mode, _stream(dev))
+    return qo, ko
+
+
+def swiglu_quant(gu: torch.Tensor, want_m: bool = False):
+    """Rows of [gate | up] -> (mq int8 [M, I], sm fp32 [M], m bf16 [M, I] | None)."""
+    dev = _require_cuda(gu)
+    M, I2 = gu.shape
+    I = I2 // 2
+    mq = torch.empty(M, pad_to(I, 16), dtype=torch.int8, device=dev)[:, :I]
+    sm = torch.empty(M, dtype=torch.float32, device=dev)
+    m = torch.empty(M, I, dtype=torch.bfloat16, device=dev) if want_m else None
+    N.call("lema_swiglu_quant", _ptr(gu), gu.stride(0), M, I, _ptr(mq), mq.stride(0), _ptr(sm),
+           _ptr(m), I, _stream(dev))
+    return mq, sm, m
+
+
+def swiglu_bwd(gu: torch.Tensor, dm: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(gu, dm)
+    dm = _rows_view(dm.to(torch.bfloat16))
+    M, I2 = gu.shape
+    dgu = torch.empty(M, I2, dtype=torch.bfloat16, device=dev)
+    N.call("lema_swiglu_bwd", _ptr(gu), gu.stride(0), _ptr(dm), _ld(dm), M, I2 // 2, _ptr(dgu),
+           I2, _stream(dev))
+    return dgu
+
+
+def gemm_from_quant(xq, sx, wq, sw) -> torch.Tensor:
+    """bf16 y = W8A8 GEMM of already-quantised rows (xq, sx) with (wq, sw)."""
+    dev = _require_cuda(xq, wq)
+    M, K = xq.shape
+    Nn = wq.shape[0]
+    y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
+    stream = _stream(dev)
+    if not GemmTimer.enabled:
+        N.call("lema_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), None,
+               _ptr(y), Nn, None, Nn, M, Nn, K, stream)
+        return y
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    N.call("lema_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), None,
+           _ptr(y), Nn, None, Nn, M, Nn, K, stream)
+    e1.record(s)
+    GemmTimer.records.append((e0, e1, 2.0 * M * Nn * K))
+    return y
+
+
+class RMSNormQuantFn(torch.autograd.Function):
+    """hn = RMSNorm(x) (bf16 rounding of HF LlamaRMSNorm) plus its int8 rows."""
+
+    @staticmethod
+    def forward(ctx, x2d, g, eps):
+        hn, xq, sx, rstd = rmsnorm_quant(x2d, g, eps)
+        ctx.save_for_backward(x2d, g, rstd)
+        ctx.mark_non_differentiable(xq, sx)
+        return hn, xq, sx
+
+    @staticmethod
+    def backward(ctx, dhn, _dxq, _dsx):
+        x2d, g, rstd = ctx.saved_tensors
+        return rmsnorm_bwd(x2d, g, rstd, dhn), None, None
+
+
+class QKVFn(torch.autograd.Function):
+    """Stacked q/k/v W8A8 projection of pre-quantised rows; returns (q, k, v) views.
+    Backward: one straight-through dgrad over the concatenated gradients."""
+
+    @staticmethod
+    def forward(ctx, hn, xq, sx, wq, sw, nq, nk):
+        y = gemm_from_quant(xq, sx, wq, sw)
+        ctx.save_for_backward(wq, sw)
+        ctx.split = (nq, nk)
+        return y[:, :nq], y[:, nq:nq + nk], y[:, nq + nk:]
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        wq, sw = ctx.saved_tensors
+        nq, nk = ctx.split
+        rows = next(g for g in (dq, dk, dv) if g is not None).shape[0]
+        parts = []
+        for g, n in ((dq, nq), (dk, nk), (dv, wq.shape[0] - nq - nk)):
+            parts.append(g if g is not None else
+                         torch.zeros(rows, n, dtype=torch.bfloat16, device=wq.device))
+        dy = torch.cat([p.to(torch.bfloat16) for p in parts], dim=1)
+        return w8a8_dgrad(dy, wq, sw), None, None, None, None, None, None
+
+
+class RopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q2d, k2d, cos, sin, seq, hq, hk, d):
+        ctx.save_for_backward(cos, sin)
+        ctx.meta = (seq, hq, hk, d)
+        return rope(q2d, k2d, cos, sin, seq, hq, hk, d, 0)
+
+    @staticmethod
+    def backward(ctx, dq, dk):
+        cos, sin = ctx.saved_tensors
+        seq, hq, hk, d = ctx.meta
+        dqi, dki = rope(dq.contiguous().to(torch.bfloat16), dk.contiguous().to(torch.bfloat16),
+                        cos, sin, seq, hq, hk, d, 1)
+        return dqi, dki, None, None, None, None, None, None
+
+
+class MLPFn(torch.autograd.Function):
+    """down(silu(gate) * up) with stacked [gate; up] W8A8 weights: gate_up GEMM on the
+    pre-quantised RMSNorm rows, fused SwiGLU -> quantise, down GEMM. Backward:
+    straight-through dgrads around the SwiGLU backward kernel."""
+
+    @staticmethod
+    def forward(ctx, hn, xq, sx, wq_gu, sw_gu, wq_dn, sw_dn):
+        gu = gemm_from_quant(xq, sx, wq_gu, sw_gu)
+        mq, sm, _ = swiglu_quant(gu)
+        y = gemm_from_quant(mq, sm, wq_dn, sw_dn)
+        ctx.save_for_backward(gu, wq_gu, sw_gu, wq_dn, sw_dn)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        gu, wq_gu, sw_gu, wq_dn, sw_dn = ctx.saved_tensors
+        dm = w8a8_dgrad(dy, wq_dn, sw_dn)
+        dgu = swiglu_bwd(gu, dm)
+        return w8a8_dgrad(dgu, wq_gu, sw_gu), None, None, None, None, None, None

@@ -100,6 +100,8 @@ class WeightSegments:
     manager's H2D copy stream."""
 
     ALIGN = 128
+    GROUPS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
+              ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",)))
 
     def __init__(self, shape: LlamaShape, num_blocks: int, device: torch.device):
         self.shape = shape
@@ -114,9 +116,20 @@ class WeightSegments:
             self.layout[name] = _Seg(off, nb, tuple(shp), dtype)
             off = (off + nb + self.ALIGN - 1) // self.ALIGN * self.ALIGN
 
-        for name, (o, i) in shape.proj_shapes().items():
-            add(name + ".wq", (o, i), torch.int8)
-            add(name + ".sw", (o,), torch.float32)
+        # Projections that read the same input are stacked (q|k|v, gate|up) so the
+        # block can run them as one GEMM; each projection is a row range of its group.
+        self.sub: dict[str, tuple[str, int, int]] = {}
+        ps = shape.proj_shapes()
+        for group, names in self.GROUPS:
+            rows = sum(ps[n][0] for n in names)
+            add(group + ".wq", (rows, ps[names[0]][1]), torch.int8)
+            add(group + ".sw", (rows,), torch.float32)
+            r0 = 0
+            for n in names:
+                r1 = r0 + ps[n][0]
+                self.sub[n + ".wq"] = (group + ".wq", r0, r1)
+                self.sub[n + ".sw"] = (group + ".sw", r0, r1)
+                r0 = r1
         add("input_layernorm", (shape.hidden,), torch.bfloat16)
         add("post_attention_layernorm", (shape.hidden,), torch.bfloat16)
         self.seg_bytes = off
@@ -150,6 +163,9 @@ class WeightSegments:
 
     # ---- filling RAM (pack time) -------------------------------------------
     def _view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        if name in self.sub:
+            group, r0, r1 = self.sub[name]
+            return self._view(buf, group)[r0:r1]
         seg = self.layout[name]
         raw = buf[seg.offset: seg.offset + seg.nbytes]
         return raw.view(seg.dtype).view(seg.shape)
@@ -182,7 +198,13 @@ class WeightSegments:
 
     def bind(self, block: LlamaBlock, slot: int) -> None:
         """Binds a block's W8A8 projections and norms to views of VRAM slot ``slot``."""
-        buf = self.vram[slot]
+        self.bind_buffer(block, self.vram[slot])
+
+    def bind_buffer(self, block: LlamaBlock, buf: torch.Tensor) -> None:
+        """Binds a block to views of any device copy of a segment; also gives the
+        block the stacked group weights for its fused path."""
+        block.fused_weights = {g + k: self._view(buf, g + k) for g, _ in self.GROUPS
+                               for k in (".wq", ".sw")}
         for name in PROJECTIONS:
             block.base_projection(name).bind(self._view(buf, name + ".wq"),
                                              self._view(buf, name + ".sw"))

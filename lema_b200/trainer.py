@@ -36,7 +36,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
-from .llama import PROJECTIONS, LlamaBlock, LlamaHead, LlamaShape, apply_lora, rope_cos_sin
+from .llama import LlamaBlock, LlamaHead, LlamaShape, apply_lora, rope_cos_sin
 from .modules import LoRALinear
 from .tensorstore import ActivationCheckpointStore, WeightSegments
 
@@ -181,12 +181,7 @@ class StreamedLoraTrainer:
         return blk
 
     def _bind_resident(self, blk: LlamaBlock, layer: int) -> None:
-        buf = self.resident[layer]
-        for name in PROJECTIONS:
-            blk.base_projection(name).bind(self.ws._view(buf, name + ".wq"),
-                                           self.ws._view(buf, name + ".sw"))
-        blk.input_layernorm.weight.data = self.ws._view(buf, "input_layernorm")
-        blk.post_attention_layernorm.weight.data = self.ws._view(buf, "post_attention_layernorm")
+        self.ws.bind_buffer(blk, self.resident[layer])
 
     def _release(self, layer: int) -> None:
         if layer >= len(self.resident):

@@ -246,3 +246,45 @@ def cfg1_inputs(seed: int = 0, M: int = 512, K: int = 4096, N: int = 4096,
 if __name__ == "__main__":
     print(build())
     os.environ.setdefault("OMP_NUM_THREADS", "1")
+
+
+# ---------------------------------------------------------------------------
+# fused producers (numpy restatements of HF LlamaRMSNorm, apply_rotary_pos_emb
+# and LlamaMLP's act(gate) * up, with the bf16 roundings torch applies)
+# ---------------------------------------------------------------------------
+
+def _bf(x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to bf16 and back to fp32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+def np_rmsnorm(x_bits: np.ndarray, g_bits: np.ndarray, eps: float) -> np.ndarray:
+    """hn bits = bf16(g * bf16(x * rsqrt(mean(x^2) + eps))), statistics in fp32."""
+    x = bf16_bits_to_f32(x_bits)
+    g = bf16_bits_to_f32(g_bits)
+    var = (np.sum(x.astype(np.float64) ** 2, axis=1) / x.shape[1]).astype(np.float32)
+    rstd = (1.0 / np.sqrt(var.astype(np.float64) + eps)).astype(np.float32)
+    xh = _bf(x * rstd[:, None])
+    return f32_to_bf16_bits(g[None, :] * xh)
+
+
+def np_rope(x_bits: np.ndarray, cos_bits: np.ndarray, sin_bits: np.ndarray, seq: int,
+            heads: int, d: int) -> np.ndarray:
+    """x [T, heads*d] bits -> bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)) bits."""
+    x = bf16_bits_to_f32(x_bits).reshape(-1, heads, d)
+    T = x.shape[0]
+    pos = np.arange(T) % seq
+    c = bf16_bits_to_f32(cos_bits)[pos][:, None, :]
+    s = bf16_bits_to_f32(sin_bits)[pos][:, None, :]
+    rot = np.concatenate([-x[..., d // 2:], x[..., : d // 2]], axis=-1)
+    out = _bf(_bf(x * c) + _bf(rot * s))
+    return f32_to_bf16_bits(out.reshape(T, heads * d))
+
+
+def np_swiglu(gu_bits: np.ndarray) -> np.ndarray:
+    """rows of [gate | up] bits -> bf16(bf16(silu(gate)) * up) bits."""
+    gu = bf16_bits_to_f32(gu_bits)
+    I = gu.shape[1] // 2
+    gate, up = gu[:, :I], gu[:, I:]
+    a = _bf((gate / (np.float32(1) + np.exp(-gate))).astype(np.float32))
+    return f32_to_bf16_bits(a * up)

@@ -147,6 +147,7 @@ def test_streamed_segments_bind_views_bitexact(cuda_device):
         ws.pack_block(b, tensors)
         blocks.append(blk)
     streamed = LlamaBlock(shape, quantized=True, device=dev)
+    streamed.use_fused = False  # same per-projection path as the reference blocks
     x = torch.randn(2, 64, shape.hidden, device=dev).to(torch.bfloat16)
     cos, sin = rope_cos_sin(shape, 64, dev, torch.bfloat16)
     ws.upload(0, 0)
@@ -199,3 +200,32 @@ def test_w8a8linear_drops_into_hf_decoder_layer(cuda_device):
         cos, sin = rope_cos_sin(shape, 48, dev, torch.bfloat16)
         out = mine(x, cos, sin)
     close(out, ref, 1e-2, 0.1, "hf layer")
+
+
+def test_fused_block_matches_unfused_and_fixture(cuda_device):
+    """The fused path (RMSNorm -> quantise, stacked QKV GEMM, RoPE kernel, fused
+    SwiGLU -> quantise) against the per-projection path of the same block and
+    against the reference-path fixture, forward and backward."""
+    d, shape, rank, alpha = load()
+    blk = block_from_fixture(d, shape, rank, alpha, cuda_device, quantized=True)
+    blk.build_fused_weights()
+    x = bf16(d["x"]).to(cuda_device)
+    dy = bf16(d["dy"]).to(cuda_device)
+    cos, sin = rope_cos_sin(shape, x.shape[1], cuda_device, torch.bfloat16)
+    res = {}
+    for fused in (False, True):
+        blk.use_fused = fused
+        xi = x.clone().requires_grad_(True)
+        y = blk(xi, cos, sin)
+        y.backward(dy)
+        res[fused] = (y.detach(), xi.grad, [blk.projection(p).lora_A.grad.clone()
+                                            for p in ("q_proj", "v_proj")])
+        for p in ("q_proj", "v_proj"):
+            blk.projection(p).lora_A.grad = None
+            blk.projection(p).lora_B.grad = None
+    close(res[True][0], res[False][0], 1e-2, 0.1, "fused vs unfused y")
+    close(res[True][1], res[False][1], 2e-2, 0.25, "fused vs unfused dx")
+    for a, b in zip(res[True][2], res[False][2]):
+        close(a, b, 5e-2, 1.0, "fused vs unfused dA")
+    close(res[True][0], bf16(d["y"]), what="fused y vs fixture")
+    close(res[True][1], bf16(d["dx"]), what="fused dx vs fixture")

@@ -135,6 +135,8 @@ def test_attention_checkpointing_gives_the_same_step(cuda_device):
     for gc in (False, True):
         tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=1e-3, seed=4,
                                  gradient_checkpointing=gc)
+        for blk in tr.blocks:
+            blk.use_fused = False  # checkpointing runs on the per-projection path
         with sdpa_kernel(SDPBackend.MATH):
             out.append(float(tr.train_step(ids)))
         out.append([p.detach().clone() for p in tr.params])
@@ -142,3 +144,34 @@ def test_attention_checkpointing_gives_the_same_step(cuda_device):
     assert out[0] == out[2]
     for a, b in zip(out[1], out[3]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_fused_step_close_to_unfused_step(cuda_device):
+    """The trainer's fused block path and the per-projection path give the same
+    loss and LoRA gradients to bf16 tolerance."""
+    ids = _ids(19, 2, 64, SMALL.vocab, cuda_device)
+    grads = []
+    for fused in (True, False):
+        tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=0.0, seed=8)
+        with torch.no_grad():
+            g = torch.Generator(device=cuda_device).manual_seed(9)
+            for layer in tr.lora:
+                for a, b in layer.values():
+                    b.copy_(torch.randn(b.shape, device=cuda_device, generator=g) * 0.02)
+        for blk in tr.blocks:
+            blk.use_fused = fused
+        captured = []
+        orig = tr.opt.step
+
+        def grab(orig=orig, captured=captured, tr=tr):
+            captured.extend(p.grad.detach().float().clone() for p in tr.params)
+            return orig()
+        tr.opt.step = grab
+        loss = float(tr.train_step(ids))
+        grads.append((loss, captured))
+        tr.close()
+    (l0, g0), (l1, g1) = grads
+    assert abs(l0 - l1) <= 2e-3 * abs(l1)
+    for a, b in zip(g0, g1):
+        rms = b.pow(2).mean().sqrt().item() + 1e-30
+        assert (a - b).pow(2).mean().sqrt().item() / rms <= 5e-2
