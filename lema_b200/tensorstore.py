@@ -174,7 +174,8 @@ class WeightSegments:
         """Writes one block's quantised tensors (device or host) into RAM segment b."""
         ram = self.ram[b]
         for name, t in tensors.items():
-            self._view(ram, name).copy_(t.detach().reshape(self.layout[name].shape))
+            v = self._view(ram, name)
+            v.copy_(t.detach().reshape(v.shape))
 
     # ---- streaming -----------------------------------------------------------
     def upload(self, b: int, slot: int) -> None:

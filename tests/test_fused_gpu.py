@@ -1,7 +1,7 @@
 """The fused producers of the block's fast path against numpy restatements of
-the torch/HF math they replace: RoPE bit-exact; RMSNorm and SwiGLU within one
-bf16 ulp (the device's rsqrt / exp differ from the host's in the last fp32 bit,
-which can move a bf16 rounding), with the int8 rows then bit-exact against the
+the torch/HF math they replace: RoPE bit-exact; SwiGLU within one bf16 ulp and
+RMSNorm within two (the device's rsqrt / exp differ from the host's in the last
+fp32 bit, which can move a bf16 rounding), with the int8 rows then bit-exact against the
 quantiser applied to the device's own bf16 output; backward kernels against
 fp64 formulas at bf16 tolerance."""
 import numpy as np
@@ -18,9 +18,9 @@ def bits(t):
     return torch_bf16_to_bits(t)
 
 
-def _ulp_check(got_bits, ref_bits, frac_exact=0.999):
+def _ulp_check(got_bits, ref_bits, frac_exact=0.999, max_ulp=1):
     d = np.abs(got_bits.astype(np.int32) - ref_bits.astype(np.int32))
-    assert d.max() <= 1, d.max()
+    assert d.max() <= max_ulp, d.max()
     assert (d == 0).mean() >= frac_exact, (d == 0).mean()
 
 
@@ -30,7 +30,9 @@ def test_rmsnorm_quant(cuda_device, oracle, M, H):
     x = (torch.randn(M, H, generator=g) * 3).to(torch.bfloat16)
     w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
     hn, xq, sx, rstd = ops.rmsnorm_quant(x.to(cuda_device), w.to(cuda_device), 1e-5)
-    _ulp_check(bits(hn), oracle.np_rmsnorm(bits(x), bits(w), 1e-5))
+    # two stacked bf16 roundings (x*rstd, then g*.): a last-bit rstd difference
+    # can move the result by up to 2 ulps
+    _ulp_check(bits(hn), oracle.np_rmsnorm(bits(x), bits(w), 1e-5), max_ulp=2)
     q_ref, s_ref = oracle.c_quantize_rows(bits(hn))
     np.testing.assert_array_equal(xq.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(sx.cpu().numpy(), s_ref)
