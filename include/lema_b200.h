@@ -179,6 +179,18 @@ LEMA_API int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int64
                        int32_t heads_q, int32_t heads_k, int32_t head_dim, void* q_out,
                        void* k_out, int32_t mode, void* stream);
 
+/* lema_rope for the three outputs of a stacked q/k/v projection: v_in (may be
+ * NULL) is copied, not rotated, into contiguous v_out; q_add / k_add / v_add
+ * (may be NULL; contiguous [tokens, heads*dim]) are added first with bf16
+ * rounding (LoRA outputs, _lora.py:23-26). Backward (mode 1) ignores v and the
+ * addends. */
+LEMA_API int lema_rope_qkv(const void* q_in, int64_t ldq, const void* k_in, int64_t ldk,
+                           const void* v_in, int64_t ldv, const void* q_add, const void* k_add,
+                           const void* v_add, const void* cos_bf16, const void* sin_bf16,
+                           int64_t tokens, int32_t seq, int32_t heads_q, int32_t heads_k,
+                           int32_t head_dim, void* q_out, void* k_out, void* v_out,
+                           int32_t mode, void* stream);
+
 /* SwiGLU of HF LlamaMLP (act(gate) * up) on rows of [gate | up] ([rows, 2*inter],
  * row stride ldgu), quantised per row (lema_quantize_rows rule) for the down
  * projection; m_bf16 (may be NULL) receives the bf16 product. */

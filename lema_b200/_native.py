@@ -44,6 +44,8 @@ _SIGNATURES: dict[str, list] = {
     "lema_rmsnorm_quant": [vp, i64, vp, i64, i64, C.c_float, vp, i64, vp, i64, vp, vp, vp],
     "lema_rmsnorm_bwd": [vp, i64, vp, vp, vp, i64, i64, i64, vp, i64, vp],
     "lema_rope": [vp, i64, vp, i64, vp, vp, i64, i32, i32, i32, i32, vp, vp, i32, vp],
+    "lema_rope_qkv": [vp, i64, vp, i64, vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32,
+                      vp, vp, vp, i32, vp],
     "lema_swiglu_quant": [vp, i64, i64, i64, vp, i64, vp, vp, i64, vp],
     "lema_swiglu_bwd": [vp, i64, vp, i64, i64, i64, vp, i64, vp],
     "lema_ckpt_save": [vp, vp, sz, i32, vp, vp, vp],

@@ -25,22 +25,32 @@ namespace {
 
 constexpr int kThreads = 128;
 
+// Block-wide reductions over NW warps (red holds NW floats); every thread gets
+// the result. A leading barrier lets two reductions share one red array.
+template <int NW = 4>
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  __syncthreads();  // red may still be read by a previous reduction
+  __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  return (red[0] + red[1]) + (red[2] + red[3]);
+  float r = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) r += red[w];
+  return r;
 }
 
+template <int NW = 4>
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float r = red[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) r = fmaxf(r, red[w]);
+  return r;
 }
 
 // Quantiser of the operator contract: rint(x / s) clamped to +-127, the quotient
@@ -174,39 +184,69 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_kernel(
 
 // ---------------------------------------------------------------- RoPE
 // One thread handles 8 consecutive dims i..i+7 of the first half of one head
-// and their partners i+d/2.. of one token. mode 0: forward with torch's bf16
-// roundings; mode 1: backward (transposed rotation, fp32, one rounding).
-__global__ void rope_kernel(const __nv_bfloat16* __restrict__ q_in, int64_t ldq_in,
-                            const __nv_bfloat16* __restrict__ k_in, int64_t ldk_in,
+// and their partners i+d/2.. of one token. Heads [0, hq) are q, [hq, hq+hk) k,
+// [hq+hk, hq+2hk) v (when v_in is given; v is not rotated). An optional addend
+// per tensor (contiguous rows, e.g. a LoRA output) is added first with bf16
+// rounding, as torch's `t + lora` does. mode 0: forward with torch's bf16
+// roundings; mode 1: backward (transposed rotation, fp32, one rounding; addends
+// and v are not used).
+struct RopeArgs {
+  const __nv_bfloat16* in[3];
+  int64_t ld[3];
+  const __nv_bfloat16* add[3];
+  __nv_bfloat16* out[3];
+  int heads[3];
+};
+
+__global__ void rope_kernel(const __grid_constant__ RopeArgs a,
                             const __nv_bfloat16* __restrict__ cosv,
                             const __nv_bfloat16* __restrict__ sinv, int64_t tokens, int seq,
-                            int hq, int hk, int d, __nv_bfloat16* __restrict__ q_out,
-                            __nv_bfloat16* __restrict__ k_out, int mode) {
+                            int d, int mode) {
   const int half = d / 2;
-  const int groups = half / 8;  // 8-wide groups per head half
-  const int per_token = (hq + hk) * groups;
+  const int groups = half / 8;
+  const int htot = a.heads[0] + a.heads[1] + a.heads[2];
+  const int per_token = htot * groups;
   const int64_t gid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (gid >= tokens * per_token) return;
   const int64_t t = gid / per_token;
   int r = static_cast<int>(gid % per_token);
-  const bool is_q = r < hq * groups;
-  if (!is_q) r -= hq * groups;
+  int which = 0;
+  while (which < 2 && r >= a.heads[which] * groups) {
+    r -= a.heads[which] * groups;
+    ++which;
+  }
   const int head = r / groups, grp = r % groups;
   const int s = static_cast<int>(t % seq);
-  const __nv_bfloat16* src = is_q ? q_in + t * ldq_in : k_in + t * ldk_in;
-  __nv_bfloat16* dst = is_q ? q_out + t * static_cast<int64_t>(hq) * d
-                            : k_out + t * static_cast<int64_t>(hk) * d;
+  const __nv_bfloat16* src = a.in[which] + t * a.ld[which];
+  const int64_t orow = t * static_cast<int64_t>(a.heads[which]) * d;
+  __nv_bfloat16* dst = a.out[which] + orow;
   const int i0 = head * d + grp * 8;
-  V8 a, b, c1, s1, c2, s2, oa, ob;
-  a.u = *reinterpret_cast<const uint4*>(src + i0);
-  b.u = *reinterpret_cast<const uint4*>(src + i0 + half);
+  V8 va, vb, oa, ob;
+  va.u = *reinterpret_cast<const uint4*>(src + i0);
+  vb.u = *reinterpret_cast<const uint4*>(src + i0 + half);
+  if (mode == 0 && a.add[which] != nullptr) {
+    V8 pa, pb;
+    pa.u = *reinterpret_cast<const uint4*>(a.add[which] + orow + i0);
+    pb.u = *reinterpret_cast<const uint4*>(a.add[which] + orow + i0 + half);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      va.h[j] = __float2bfloat16_rn(__bfloat162float(va.h[j]) + __bfloat162float(pa.h[j]));
+      vb.h[j] = __float2bfloat16_rn(__bfloat162float(vb.h[j]) + __bfloat162float(pb.h[j]));
+    }
+  }
+  if (which == 2) {  // v: no rotation
+    *reinterpret_cast<uint4*>(dst + i0) = va.u;
+    *reinterpret_cast<uint4*>(dst + i0 + half) = vb.u;
+    return;
+  }
+  V8 c1, s1, c2, s2;
   c1.u = *reinterpret_cast<const uint4*>(cosv + static_cast<int64_t>(s) * d + grp * 8);
   s1.u = *reinterpret_cast<const uint4*>(sinv + static_cast<int64_t>(s) * d + grp * 8);
   c2.u = *reinterpret_cast<const uint4*>(cosv + static_cast<int64_t>(s) * d + half + grp * 8);
   s2.u = *reinterpret_cast<const uint4*>(sinv + static_cast<int64_t>(s) * d + half + grp * 8);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float xa = __bfloat162float(a.h[j]), xb = __bfloat162float(b.h[j]);
+    const float xa = __bfloat162float(va.h[j]), xb = __bfloat162float(vb.h[j]);
     if (mode == 0) {
       // out[i] = x[i]c[i] + (-x[i+h]) s[i];  out[i+h] = x[i+h]c[i+h] + x[i] s[i+h]
       const float ta = __bfloat162float(__float2bfloat16_rn(xa * __bfloat162float(c1.h[j])));
@@ -230,11 +270,13 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ q_in, int64_t ldq_
 // ---------------------------------------------------------------- SwiGLU
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
 
+constexpr int kSwThreads = 256;  // wide rows (I = 11008 / 14336): 256 threads per row
+
 template <int VPT>
-__global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(
+__global__ void __launch_bounds__(kSwThreads) swiglu_quant_kernel(
     const __nv_bfloat16* __restrict__ gu, int64_t ldgu, int inter, int8_t* __restrict__ q,
     int64_t ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ m_out, int64_t ldm) {
-  __shared__ float red[4];
+  __shared__ float red[kSwThreads / 32];
   const int64_t row = blockIdx.x;
   const int nvec = inter / 8;
   const __nv_bfloat16* gate = gu + row * ldgu;
@@ -243,7 +285,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+    const int idx = threadIdx.x + i * kSwThreads;
     if (idx < nvec) {
       V8 gv, uv;
       gv.u = __ldg(reinterpret_cast<const uint4*>(gate) + idx);
@@ -259,12 +301,12 @@ __global__ void __launch_bounds__(kThreads) swiglu_quant_kernel(
       if (m_out != nullptr) reinterpret_cast<uint4*>(m_out + row * ldm)[idx] = mv[i].u;
     }
   }
-  amax = block_max(amax, red);
+  amax = block_max<kSwThreads / 32>(amax, red);
   float s, inv_s;
   row_scale(amax, s, inv_s);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+    const int idx = threadIdx.x + i * kSwThreads;
     if (idx < nvec) {
       __align__(8) int8_t o[8];
 #pragma unroll
@@ -377,10 +419,12 @@ extern "C" int lema_rmsnorm_bwd(const void* x_bf16, int64_t ldx, const void* g_b
   return LEMA_OK;
 }
 
-extern "C" int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int64_t ldk_in,
-                         const void* cos_bf16, const void* sin_bf16, int64_t tokens, int32_t seq,
-                         int32_t heads_q, int32_t heads_k, int32_t head_dim, void* q_out,
-                         void* k_out, int32_t mode, void* stream) {
+extern "C" int lema_rope_qkv(const void* q_in, int64_t ldq, const void* k_in, int64_t ldk,
+                             const void* v_in, int64_t ldv, const void* q_add, const void* k_add,
+                             const void* v_add, const void* cos_bf16, const void* sin_bf16,
+                             int64_t tokens, int32_t seq, int32_t heads_q, int32_t heads_k,
+                             int32_t head_dim, void* q_out, void* k_out, void* v_out,
+                             int32_t mode, void* stream) {
   clear_error();
   if (tokens < 0 || seq <= 0 || heads_q < 0 || heads_k < 0 || head_dim <= 0 ||
       (mode != 0 && mode != 1))
@@ -388,21 +432,46 @@ extern "C" int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int
   if (tokens == 0) return LEMA_OK;
   if (head_dim % 16 != 0)
     return set_error(LEMA_ERR_UNSUPPORTED, "rope needs head_dim % 16 == 0");
-  if (!q_in || !k_in || !cos_bf16 || !sin_bf16 || !q_out || !k_out)
+  if (!q_in || !k_in || !cos_bf16 || !sin_bf16 || !q_out || !k_out || (v_in && !v_out))
     return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
-  if (!rows_ok(q_in, ldq_in) || !rows_ok(k_in, ldk_in) || !aligned16(q_out) ||
-      !aligned16(k_out) || !aligned16(cos_bf16) || !aligned16(sin_bf16))
+  const void* ptrs[] = {q_out, k_out, v_out, q_add, k_add, v_add, cos_bf16, sin_bf16};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return set_error(LEMA_ERR_MISALIGNED, "rope needs 16-byte aligned rows");
+  if (!rows_ok(q_in, ldq) || !rows_ok(k_in, ldk) || (v_in && !rows_ok(v_in, ldv)))
     return set_error(LEMA_ERR_MISALIGNED, "rope needs 16-byte aligned rows");
-  const int64_t work = tokens * (heads_q + heads_k) * (head_dim / 16);
+  RopeArgs a;
+  a.in[0] = static_cast<const __nv_bfloat16*>(q_in);
+  a.in[1] = static_cast<const __nv_bfloat16*>(k_in);
+  a.in[2] = static_cast<const __nv_bfloat16*>(v_in);
+  a.ld[0] = ldq;
+  a.ld[1] = ldk;
+  a.ld[2] = ldv;
+  a.add[0] = static_cast<const __nv_bfloat16*>(q_add);
+  a.add[1] = static_cast<const __nv_bfloat16*>(k_add);
+  a.add[2] = static_cast<const __nv_bfloat16*>(v_add);
+  a.out[0] = static_cast<__nv_bfloat16*>(q_out);
+  a.out[1] = static_cast<__nv_bfloat16*>(k_out);
+  a.out[2] = static_cast<__nv_bfloat16*>(v_out);
+  a.heads[0] = heads_q;
+  a.heads[1] = heads_k;
+  a.heads[2] = (v_in && mode == 0) ? heads_k : 0;
+  const int64_t work = tokens * (a.heads[0] + a.heads[1] + a.heads[2]) * (head_dim / 16);
   const int64_t blocks = (work + 255) / 256;
   if (blocks > INT32_MAX) return set_error(LEMA_ERR_UNSUPPORTED, "too many tokens");
   rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q_in), ldq_in, static_cast<const __nv_bfloat16*>(k_in),
-      ldk_in, static_cast<const __nv_bfloat16*>(cos_bf16),
-      static_cast<const __nv_bfloat16*>(sin_bf16), tokens, seq, heads_q, heads_k, head_dim,
-      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), mode);
+      a, static_cast<const __nv_bfloat16*>(cos_bf16), static_cast<const __nv_bfloat16*>(sin_bf16),
+      tokens, seq, head_dim, mode);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
+}
+
+extern "C" int lema_rope(const void* q_in, int64_t ldq_in, const void* k_in, int64_t ldk_in,
+                         const void* cos_bf16, const void* sin_bf16, int64_t tokens, int32_t seq,
+                         int32_t heads_q, int32_t heads_k, int32_t head_dim, void* q_out,
+                         void* k_out, int32_t mode, void* stream) {
+  return lema_rope_qkv(q_in, ldq_in, k_in, ldk_in, nullptr, 0, nullptr, nullptr, nullptr,
+                       cos_bf16, sin_bf16, tokens, seq, heads_q, heads_k, head_dim, q_out, k_out,
+                       nullptr, mode, stream);
 }
 
 extern "C" int lema_swiglu_quant(const void* gu_bf16, int64_t ldgu, int64_t rows, int64_t inter,
@@ -412,17 +481,25 @@ extern "C" int lema_swiglu_quant(const void* gu_bf16, int64_t ldgu, int64_t rows
   if (rows < 0 || inter <= 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad size");
   if (rows == 0) return LEMA_OK;
   if (!gu_bf16 || !q || !scale) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
-  const int vpt = vpt_for(static_cast<int>(inter));
-  if (inter % 8 != 0 || vpt == 0)
+  const int64_t nv = (inter / 8 + kSwThreads - 1) / kSwThreads;
+  if (inter % 8 != 0 || nv > 8)
     return set_error(LEMA_ERR_UNSUPPORTED, "swiglu_quant needs inter % 8 == 0, <= 16384");
   if (!rows_ok(gu_bf16, ldgu) || reinterpret_cast<uintptr_t>(q) % 8 != 0 || ldq % 8 != 0 ||
       (m_bf16 && !rows_ok(m_bf16, ldm)))
     return set_error(LEMA_ERR_MISALIGNED, "swiglu_quant needs 16-byte aligned rows");
   auto s = static_cast<cudaStream_t>(stream);
-  LEMA_VPT_LAUNCH(vpt, swiglu_quant_kernel, (
-      static_cast<const __nv_bfloat16*>(gu_bf16), ldgu, static_cast<int>(inter), q, ldq, scale,
-      static_cast<__nv_bfloat16*>(m_bf16), ldm),
-                  static_cast<unsigned>(rows), kThreads, 0, s);
+  const int vpt = nv <= 2 ? 2 : (nv <= 4 ? 4 : (nv <= 6 ? 6 : 8));
+  auto args = [&](auto kern) {
+    kern<<<static_cast<unsigned>(rows), kSwThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(gu_bf16), ldgu, static_cast<int>(inter), q, ldq, scale,
+        static_cast<__nv_bfloat16*>(m_bf16), ldm);
+  };
+  switch (vpt) {
+    case 2: args(swiglu_quant_kernel<2>); break;
+    case 4: args(swiglu_quant_kernel<4>); break;
+    case 6: args(swiglu_quant_kernel<6>); break;
+    default: args(swiglu_quant_kernel<8>); break;
+  }
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }

@@ -246,7 +246,8 @@ class LlamaBlock(nn.Module):
 
     def _forward_fused(self, h, cos, sin):
         """The same layer through the fused producers: RMSNorm -> quantise (one
-        kernel), one stacked q/k/v W8A8 GEMM, LoRA on q/k/v, one RoPE kernel, SDPA,
+        kernel), one stacked q/k/v W8A8 GEMM, one kernel adding the LoRA outputs,
+        rotating q/k and laying v out contiguously, SDPA,
         o_proj, residual, RMSNorm -> quantise, stacked gate/up GEMM, SwiGLU ->
         quantise (one kernel), down GEMM, residual."""
         from . import ops
@@ -259,18 +260,16 @@ class LlamaBlock(nn.Module):
         hn, xq, sx = ops.RMSNormQuantFn.apply(x2d, self.input_layernorm.weight, sh.eps)
         q, k, v = ops.QKVFn.apply(hn, xq, sx, fw["qkv.wq"], fw["qkv.sw"], nq, nk)
         att = self.self_attn
-        outs = []
-        for name, t in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
+        lora = []
+        for name in ("q_proj", "k_proj", "v_proj"):
             m = getattr(att, name)
-            if isinstance(m, LoRALinear):
-                t = t + (hn @ m.lora_A.transpose(0, 1) @ m.lora_B.transpose(0, 1)) * m.scaling
-            outs.append(t)
-        q, k, v = outs
-        qr, kr = ops.RopeFn.apply(q, k, cos.reshape(-1, d), sin.reshape(-1, d), S, sh.heads,
-                                  sh.kv_heads, d)
+            lora.append((hn @ m.lora_A.transpose(0, 1) @ m.lora_B.transpose(0, 1)) * m.scaling
+                        if isinstance(m, LoRALinear) else None)
+        qr, kr, vc = ops.RopeQKVFn.apply(q, k, v, *lora, cos.reshape(-1, d), sin.reshape(-1, d),
+                                         S, sh.heads, sh.kv_heads, d)
         qv = qr.view(B, S, sh.heads, d).transpose(1, 2)
         kv = kr.view(B, S, sh.kv_heads, d).transpose(1, 2)
-        vv = v.reshape(B, S, sh.kv_heads, d).transpose(1, 2)
+        vv = vc.view(B, S, sh.kv_heads, d).transpose(1, 2)
         gqa = sh.heads != sh.kv_heads
         if att.attn_chunk and S > att.attn_chunk:
             o = _chunked_causal_attention(qv, kv, vv, d ** -0.5, att.attn_chunk, gqa)

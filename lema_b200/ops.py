@@ -583,3 +583,41 @@ class MLPFn(torch.autograd.Function):
         dm = w8a8_dgrad(dy, wq_dn, sw_dn)
         dgu = swiglu_bwd(gu, dm)
         return w8a8_dgrad(dgu, wq_gu, sw_gu), None, None, None, None, None, None
+
+
+def rope_qkv(q2d, k2d, v2d, q_add, k_add, v_add, cos, sin, seq, hq, hk, d):
+    """Forward RoPE of q and k plus the contiguous copy of v, each after adding its
+    optional LoRA output (bf16 rounding). Returns contiguous (q_out, k_out, v_out)."""
+    dev = _require_cuda(q2d, k2d, v2d, cos, sin)
+    T = q2d.shape[0]
+    qo = torch.empty(T, hq * d, dtype=torch.bfloat16, device=dev)
+    ko = torch.empty(T, hk * d, dtype=torch.bfloat16, device=dev)
+    vo = torch.empty(T, hk * d, dtype=torch.bfloat16, device=dev)
+    adds = [None if t is None else t.contiguous().to(torch.bfloat16) for t in (q_add, k_add, v_add)]
+    N.call("lema_rope_qkv", _ptr(q2d), q2d.stride(0), _ptr(k2d), k2d.stride(0), _ptr(v2d),
+           v2d.stride(0), _ptr(adds[0]), _ptr(adds[1]), _ptr(adds[2]), _ptr(cos.contiguous()),
+           _ptr(sin.contiguous()), T, seq, hq, hk, d, _ptr(qo), _ptr(ko), _ptr(vo), 0,
+           _stream(dev))
+    return qo, ko, vo
+
+
+class RopeQKVFn(torch.autograd.Function):
+    """(q + lq, k + lk) rotated and v + lv made contiguous in one kernel."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lq, lk, lv, cos, sin, seq, hq, hk, d):
+        ctx.save_for_backward(cos, sin)
+        ctx.meta = (seq, hq, hk, d)
+        ctx.has_add = (lq is not None, lk is not None, lv is not None)
+        return rope_qkv(q, k, v, lq, lk, lv, cos, sin, seq, hq, hk, d)
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos, sin = ctx.saved_tensors
+        seq, hq, hk, d = ctx.meta
+        dqi, dki = rope(dq.contiguous().to(torch.bfloat16), dk.contiguous().to(torch.bfloat16),
+                        cos, sin, seq, hq, hk, d, 1)
+        dv = dv.contiguous()
+        hq_, hk_, hv_ = ctx.has_add
+        return (dqi, dki, dv, dqi if hq_ else None, dki if hk_ else None, dv if hv_ else None,
+                None, None, None, None, None, None)

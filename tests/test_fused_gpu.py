@@ -102,3 +102,25 @@ def test_swiglu_quant_and_bwd(cuda_device, oracle, M, I):
     ref = torch.cat([gate.grad, up.grad], 1)
     err = (dgu - ref).abs()
     assert (err <= 2 ** -7 * ref.abs() + 1e-5).all(), err.max()
+
+
+def test_rope_qkv_with_lora_addends(cuda_device, oracle):
+    """q/k/v of a stacked projection plus LoRA addends: rotate(bf16(q + lq)),
+    rotate(bf16(k)), bf16(v + lv) made contiguous — bit-exact against torch's
+    composition of the same bf16 ops."""
+    from lema_b200.llama import LlamaShape, apply_rope, rope_cos_sin
+    d, S, B, hq, hk = 128, 64, 2, 32, 8
+    shape = LlamaShape(hidden=hq * d, heads=hq, kv_heads=hk)
+    cos, sin = rope_cos_sin(shape, S, cuda_device, torch.bfloat16)
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    qkv = torch.randn(B * S, (hq + 2 * hk) * d, device=cuda_device, generator=g).to(torch.bfloat16)
+    q, k, v = qkv[:, :hq * d], qkv[:, hq * d:(hq + hk) * d], qkv[:, (hq + hk) * d:]
+    lq = torch.randn(B * S, hq * d, device=cuda_device, generator=g).to(torch.bfloat16) * 0.1
+    lv = torch.randn(B * S, hk * d, device=cuda_device, generator=g).to(torch.bfloat16) * 0.1
+    qo, ko, vo = ops.rope_qkv(q, k, v, lq, None, lv, cos[0], sin[0], S, hq, hk, d)
+    qt = (q + lq).view(B, S, hq, d).transpose(1, 2)
+    kt = k.reshape(B, S, hk, d).transpose(1, 2)
+    qr, kr = apply_rope(qt, kt, cos, sin)
+    assert torch.equal(qo.view(torch.int16), qr.transpose(1, 2).reshape(B * S, -1).view(torch.int16))
+    assert torch.equal(ko.view(torch.int16), kr.transpose(1, 2).reshape(B * S, -1).view(torch.int16))
+    assert torch.equal(vo.view(torch.int16), (v + lv).view(torch.int16))
