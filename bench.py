@@ -9,6 +9,11 @@ Workloads (``--workload``):
                     RAM per layer, boundary activations offloaded to pinned
                     host and restored for the recompute, data-parallel LoRA
                     gradient all-reduce (NCCL) for N > 1. Metric: tokens/s.
+  llama7b_selective_ft_2048
+                    the long-sequence case: bs 1 x seq 2048, 512-token chunked
+                    attention, activations offloaded, selective full
+                    fine-tuning of q/k/v/o in the last 4 layers (fp32 AdamW
+                    states in pinned host RAM). Metric: tokens/s.
   w8a8_linear_4096  one W8A8 linear forward step (K1 quantise + K2/K3 GEMM with
                     fused epilogue) at M=N=K=4096, the per-layer shape of the
                     7B streamed model at bs=8 x seq=512. Metric: int8 TOPS.
@@ -373,10 +378,28 @@ def run_train(args, world, rank, local) -> dict | None:
 
     dev = torch.device("cuda", local)
     shape = LlamaShape(layers=args.layers)
-    batch, seq = 8, 512
+    long_ft = args.workload == "llama7b_selective_ft_2048"
+    if long_ft:
+        # bs 1 x seq 2048, 512-token chunked attention, activations offloaded, selective
+        # full fine-tuning of q/k/v/o in the last 4 layers (fp32 AdamW states in host RAM)
+        batch, seq = 1, 2048
+        last4 = tuple(range(max(0, shape.layers - 4), shape.layers))
+        tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, targets=(), seed=0,
+                                 resident_layers=args.resident_layers, attn_chunk=512,
+                                 full_ft_layers=last4)
+        workload = (f"llama7b_selective_ft_2048: {shape.layers} x [hidden 4096, 32x128 heads, "
+                    "MLP 11008], vocab 32000, bs 1 x seq 2048, 512-token chunked causal "
+                    "attention, W8A8 projections streamed from pinned RAM, activation "
+                    f"checkpoints offloaded, full fine-tuning of q/k/v/o in layers {list(last4)} "
+                    "(fp32 AdamW states in pinned host RAM, re-quantised each step)")
+    else:
+        batch, seq = 8, 512
+        tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
+                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers)
+        workload = (f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 heads, MLP "
+                    "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections streamed "
+                    "from pinned RAM, activation checkpoints offloaded")
     tokens_per_step = batch * seq
-    tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16, lora_alpha=32.0,
-                             seed=0, resident_layers=args.resident_layers)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     n_batches = 4
     ids_dev = [torch.randint(0, shape.vocab, (batch, seq), device=dev, generator=gen)
@@ -427,6 +450,10 @@ def run_train(args, world, rank, local) -> dict | None:
     h2d_per_step = (2 * streamed - min(2, streamed)) * seg_bytes + \
         tr.ckpt.nbytes * shape.layers
     d2h_per_step = tr.ckpt.nbytes * shape.layers
+    if tr.full_ft is not None:  # bf16 weight + fp32 m, v in; the same + int8 rows out
+        n_ft = sum(w.numel() for w in tr.full_ft.true.values())
+        h2d_per_step += n_ft * 10
+        d2h_per_step += n_ft * 11
     tr.close()
     if rank != 0:
         return None
@@ -449,10 +476,7 @@ def run_train(args, world, rank, local) -> dict | None:
         "dtype": "int8 W8A8 projections (bf16 activations; bf16 attention, LoRA, lm_head)",
         "data": "synthetic (random-init Llama-2-7B-shaped weights, token ids uniform in "
                 "[0, 32000), labels = inputs)",
-        "config": {"workload": f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 "
-                               "heads, MLP 11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 "
-                               "projections streamed from pinned RAM, activation checkpoints "
-                               "offloaded",
+        "config": {"workload": workload,
                    "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}",
                    "resident_layers": args.resident_layers,
@@ -513,7 +537,7 @@ def run_reference(args) -> dict | None:
         return None
     threads = os.cpu_count() or 1
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.workload == "llama7b_streamed_lora":
+    if args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048"):
         vals = [cpu_train_sample(args.cpu_seq, threads) for _ in range(args.steps)]
         tps = statistics.median(v["tokens_per_s"] for v in vals)
         return {
@@ -559,7 +583,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama7b_streamed_lora",
-                    choices=["llama7b_streamed_lora", "w8a8_linear_4096"])
+                    choices=["llama7b_streamed_lora", "llama7b_selective_ft_2048",
+                             "w8a8_linear_4096"])
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)
@@ -570,7 +595,7 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--int8-peak-tops", type=float, default=0.0)
     args = ap.parse_args()
-    train = args.workload == "llama7b_streamed_lora"
+    train = args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048")
     if args.steps is None:
         args.steps = (3 if args.impl == "reference" else 10) if train else 50
     if args.warmup is None:
