@@ -44,6 +44,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "W8A8 GEMM TOPS (% INT8 peak); 7B streamed LoRA tokens/s at 1/2/4/8 B200"
 INT8_SPEC_TOPS = 4500.0
+# DRAM bytes per GEMM launch measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum)
+LINEAR_GEMM_TRAFFIC_BYTES = 33_630_464 + 668_672      # M=N=K=4096, CTA-pair kernel
+TRAIN_GEMM_TRAFFIC_BYTES = 136_200_000                # mean of qkv / o / gate_up / down
 L2_BYTES = 126 * 2**20
 
 
@@ -297,7 +300,9 @@ def run_linear(args, world, rank, local) -> dict | None:
                      "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
                      "peak_source": "measured cuBLASLt int8 GEMM (torch._int_mm 8192^3, burst)",
                      "frac_of_spec_4500": round(achieved / INT8_SPEC_TOPS, 4),
-                     "traffic": None,
+                     # DRAM bytes (read + write) per launch of the CTA-pair kernel at
+                     # 4096^3 from an ncu capture (--set full, one launch)
+                     "traffic": LINEAR_GEMM_TRAFFIC_BYTES,
                      "algorithmic_ops_per_launch": ops_per_step,
                      "avg_launch_ms": round(gemm_ms, 5)},
         "clocks": clk,
@@ -489,7 +494,10 @@ def run_train(args, world, rank, local) -> dict | None:
                      "frac": round(achieved / int8_peak, 4),
                      "peak_source": "measured cuBLASLt int8 GEMM (torch._int_mm 8192^3, burst)",
                      "frac_of_spec_4500": round(achieved / INT8_SPEC_TOPS, 4),
-                     "traffic": None, "gemm_launches": gemm_launches,
+                     # DRAM bytes (read + write) per launch, averaged over a layer's four
+                     # int8 GEMMs, from an ncu capture of this workload (4 metrics, 8 launches)
+                     "traffic": TRAIN_GEMM_TRAFFIC_BYTES if not long_ft else None,
+                     "gemm_launches": gemm_launches,
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
                      "algorithmic_ops_per_step": gemm_ops / args.steps},
         "pcie": {"h2d_gbs_measured": round(h2d_gbs, 1),
