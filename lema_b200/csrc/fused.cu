@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 
 #include "internal.h"
+#include "quant_core.cuh"
 
 namespace lema {
 namespace {
@@ -53,21 +54,9 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
-// Quantiser of the operator contract: rint(x / s) clamped to +-127, the quotient
-// formed as a reciprocal product and re-done as an exact division near ties or
-// when the scale is subnormal (same rule as quantize.cu).
-__device__ __forceinline__ int8_t q1(float x, float s, float inv_s) {
-  const float y = __fmul_rn(x, inv_s);
-  const float frac = fabsf(y - truncf(y));
-  const float q0 = (inv_s == 0.f || fabsf(frac - 0.5f) < 1e-4f) ? __fdiv_rn(x, s) : y;
-  int q = __float2int_rn(q0);
-  q = max(-127, min(127, q));
-  return static_cast<int8_t>(q);
-}
-
 __device__ __forceinline__ void row_scale(float amax, float& s, float& inv_s) {
-  s = amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
-  inv_s = s >= 1.17549435e-38f ? __frcp_rn(s) : 0.f;
+  s = quant_row_scale(amax);
+  inv_s = quant_row_inv_scale(s);
 }
 
 union V8 {
@@ -126,11 +115,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     for (int i = 0; i < VPT; ++i) {
       const int idx = threadIdx.x + i * kThreads;
       if (idx < nvec) {
-        __align__(8) int8_t o[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = q1(__bfloat162float(v[i].h[j]), s, inv_s);
         *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
-            *reinterpret_cast<const uint2*>(o);
+            quant8_bf16(v[i].u, s, inv_s);
       }
     }
     if (threadIdx.x == 0) scale[row] = s;
@@ -308,11 +294,8 @@ __global__ void __launch_bounds__(kSwThreads) swiglu_quant_kernel(
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kSwThreads;
     if (idx < nvec) {
-      __align__(8) int8_t o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = q1(__bfloat162float(mv[i].h[j]), s, inv_s);
       *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
-          *reinterpret_cast<const uint2*>(o);
+          quant8_bf16(mv[i].u, s, inv_s);
     }
   }
   if (threadIdx.x == 0) scale[row] = s;

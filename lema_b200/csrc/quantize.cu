@@ -6,16 +6,18 @@
 // K1 is HBM-bound: one CTA of 128 threads owns one row, reads it once with
 // 128-bit loads into registers (up to 16 vectors per thread = 16384 bf16),
 // reduces |x| with warp shuffles + a 4-entry shared array, then quantises from
-// registers and writes int8 with 64-bit stores. Rows longer than the register
-// budget, unaligned rows and ragged column counts take a two-pass scalar path.
-// The result is the operator contract's: rint (half to even) of the IEEE fp32
-// quotient x / s, clamped to [-127, 127]; the quotient is formed as a
-// reciprocal product and re-done as an exact division only near ties.
+// registers and writes int8 with 64-bit stores. For 4096-column rows twelve
+// such CTAs fit an SM (~100 KB of loads in flight per SM). Rows longer than the
+// register budget, unaligned rows and ragged column counts take a two-pass
+// scalar path. The result is the operator contract's: rint (half to even) of
+// the IEEE fp32 quotient x / s, clamped to [-127, 127]; the element arithmetic
+// is in quant_core.cuh (reciprocal product, exact division near ties).
 #include <cuda_bf16.h>
 
 #include <algorithm>
 
 #include "internal.h"
+#include "quant_core.cuh"
 
 namespace lema {
 
@@ -48,30 +50,6 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
-__device__ __forceinline__ float row_scale(float amax) {
-  return amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
-}
-
-// q = clamp(rint(RN(x / s)), -127, 127) without a full division per element.
-// For a normal scale s, y = RN(x * RN(1/s)) is within 2^-23 relative
-// (|y| <= 127.5, so within 2.3e-5 absolute) of the correctly rounded quotient
-// RN(x / s); when y is farther than 1e-4 from every half-integer both round to
-// the same integer. Otherwise (about 1e-4 of inputs), and for every element
-// of a row whose scale is subnormal (inv_s passed as 0), the exact IEEE
-// quotient is computed.
-__device__ __forceinline__ float row_inv_scale(float s) {
-  return s >= 1.17549435e-38f ? __frcp_rn(s) : 0.f;
-}
-
-__device__ __forceinline__ int8_t quant1(float x, float s, float inv_s) {
-  const float y = __fmul_rn(x, inv_s);
-  const float frac = fabsf(y - truncf(y));
-  const float q0 = (inv_s == 0.f || fabsf(frac - 0.5f) < 1e-4f) ? __fdiv_rn(x, s) : y;
-  int q = __float2int_rn(q0);
-  q = max(-127, min(127, q));
-  return static_cast<int8_t>(q);
-}
-
 template <typename T>
 struct Vec;
 template <>
@@ -83,10 +61,9 @@ struct Vec<__nv_bfloat16> {
     m = __hmax2(m, __hmax2(__habs2(h[2]), __habs2(h[3])));
     return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
   }
-  __device__ static void quant(const uint4& v, float s, float inv_s, int8_t* out) {
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) out[i] = quant1(__bfloat162float(h[i]), s, inv_s);
+  // 8 int8 packed little-endian
+  __device__ static uint2 quant(const uint4& v, float s, float inv_s) {
+    return quant8_bf16(v, s, inv_s);
   }
   __device__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 };
@@ -97,11 +74,10 @@ struct Vec<float> {
     return fmaxf(fmaxf(fabsf(__uint_as_float(v.x)), fabsf(__uint_as_float(v.y))),
                  fmaxf(fabsf(__uint_as_float(v.z)), fabsf(__uint_as_float(v.w))));
   }
-  __device__ static void quant(const uint4& v, float s, float inv_s, int8_t* out) {
-    out[0] = quant1(__uint_as_float(v.x), s, inv_s);
-    out[1] = quant1(__uint_as_float(v.y), s, inv_s);
-    out[2] = quant1(__uint_as_float(v.z), s, inv_s);
-    out[3] = quant1(__uint_as_float(v.w), s, inv_s);
+  // 4 int8 packed little-endian
+  __device__ static uint32_t quant(const uint4& v, float s, float inv_s) {
+    return quant4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z),
+                  __uint_as_float(v.w), s, inv_s);
   }
   __device__ static float to_f(float x) { return x; }
 };
@@ -138,22 +114,15 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __re
     }
   }
   amax = block_max(amax, red);
-  const float s = row_scale(amax);
-  const float inv_s = row_inv_scale(s);
+  const float s = quant_row_scale(amax);
+  const float inv_s = quant_row_inv_scale(s);
   int8_t* qr = q + row * ldq;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kQThreads;
-    if (idx < nvec) {
-      __align__(8) int8_t out[E];
-      Vec<T>::quant(v[i], s, inv_s, out);
-      if (E == 8)
-        *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(idx) * E) =
-            *reinterpret_cast<const uint2*>(out);
-      else
-        *reinterpret_cast<uint32_t*>(qr + static_cast<int64_t>(idx) * E) =
-            *reinterpret_cast<const uint32_t*>(out);
-    }
+    if (idx < nvec)
+      *reinterpret_cast<decltype(Vec<T>::quant(v[i], s, inv_s))*>(
+          qr + static_cast<int64_t>(idx) * E) = Vec<T>::quant(v[i], s, inv_s);
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
@@ -172,11 +141,10 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_generic_kernel(const T* 
   for (int64_t c = threadIdx.x; c < cols; c += kQThreads)
     amax = fmaxf(amax, fabsf(Vec<T>::to_f(xr[c])));
   amax = block_max(amax, red);
-  const float s = row_scale(amax);
-  const float inv_s = row_inv_scale(s);
+  const float s = quant_row_scale(amax);
   int8_t* qr = q + row * ldq;
   for (int64_t c = threadIdx.x; c < cols; c += kQThreads)
-    qr[c] = quant1(Vec<T>::to_f(xr[c]), s, inv_s);
+    qr[c] = static_cast<int8_t>(quant_exact(Vec<T>::to_f(xr[c]), s));
   if (threadIdx.x == 0) scale[row] = s;
 }
 
@@ -267,7 +235,7 @@ __global__ void __launch_bounds__(256) dequant_transpose_kernel(const int8_t* __
 }  // namespace
 
 int quant_read_device_error(int32_t* out) {
-  *out = 0;
+  *out = 0;  // no kernel of this file waits on anything
   return LEMA_OK;
 }
 

@@ -49,7 +49,9 @@ def test_gemm_tiny_s32_exact(cuda_device, oracle):
 # --------------------------------------------------------------------------- K1
 
 @pytest.mark.parametrize("shape", [(512, 4096), (3, 11008), (17, 14336), (5, 20000),
-                                   (64, 4104), (9, 33), (1, 8), (300, 1)])
+                                   (64, 4104), (9, 33), (1, 8), (300, 1),
+                                   # row-pipelined kernel: several rows per CTA, 2-8 stages
+                                   (2000, 4096), (700, 11008), (301, 24576), (1000, 1032)])
 def test_quantize_rows_bitexact(cuda_device, oracle, shape):
     x = rand_bf16(shape, seed=shape[0] + shape[1])
     if shape[0] > 2:
@@ -67,11 +69,12 @@ def test_quantize_rows_strided_and_f32(cuda_device, oracle):
     qr, sr = oracle.c_quantize_rows(bits(view.cpu()))
     np.testing.assert_array_equal(q.cpu().numpy(), qr)
     np.testing.assert_array_equal(s.cpu().numpy(), sr)
-    xf = torch.randn(33, 4096, generator=torch.Generator().manual_seed(9)) * 0.02
-    q, s = ops.quantize_rows(xf.to(cuda_device))
-    qr, sr = oracle.c_quantize_rows_f32(xf.numpy())
-    np.testing.assert_array_equal(q.cpu().numpy(), qr)
-    np.testing.assert_array_equal(s.cpu().numpy(), sr)
+    for shape in ((33, 4096), (1000, 3000)):
+        xf = torch.randn(*shape, generator=torch.Generator().manual_seed(9)) * 0.02
+        q, s = ops.quantize_rows(xf.to(cuda_device))
+        qr, sr = oracle.c_quantize_rows_f32(xf.numpy())
+        np.testing.assert_array_equal(q.cpu().numpy(), qr)
+        np.testing.assert_array_equal(s.cpu().numpy(), sr)
 
 
 def test_quantize_adversarial_rows(cuda_device, oracle):
@@ -311,6 +314,47 @@ def test_bf16_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
     y = ops.bf16_gemm_tn(a.to(dev), b.to(dev))
     _, ref = oracle.c_bf16_gemm_tn(bits(a), bits(b))
     _dgrad_tol_check(bits(y), ref)
+
+
+# Split tail: when the last wave of tiles would leave workers idle, its tiles
+# are cut along K over all workers, the partial s32 sums published to a
+# per-stream workspace and added by the tile's owner. These shapes give few
+# tiles and long K, so each tile has several contributors.
+SPLIT_CASES = [("pair", 768, 1024, 4096),    # 12 tiles over 74 pairs: ~6 workers per tile
+               ("pair", 300, 520, 8208),     # ragged M, N and K tail
+               ("1sm256", 384, 1024, 16384),  # 12 tiles over 148 CTAs
+               ("1sm128", 333, 600, 11008)]
+
+
+@pytest.mark.parametrize("path,M,N,K", SPLIT_CASES)
+def test_gemm_split_tail_bitexact(cuda_device, oracle, monkeypatch, path, M, N, K):
+    monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(M * 7 + K)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+    sx = torch.rand(M, device=dev, generator=g) * 0.01 + 1e-4
+    sw = torch.rand(N, device=dev, generator=g) * 1e-3 + 1e-5
+    for _ in range(2):  # the second launch reuses the workspace and its reset counters
+        y, acc = ops.w8a8_gemm(a, sx, b, sw, want_acc=True)
+        np.testing.assert_array_equal(acc.cpu().numpy(),
+                                      oracle.c_int8_gemm(a.cpu().numpy(), b.cpu().numpy()))
+        yref = oracle.c_epilogue(acc.cpu().numpy(), sx.cpu().numpy(), sw.cpu().numpy(), None)
+        np.testing.assert_array_equal(bits(y), yref)
+
+
+def test_bf16_gemm_split_tail_deterministic(cuda_device, oracle, monkeypatch):
+    """bf16 kind: the owner adds fp32 partials in a fixed order, so a split GEMM
+    is within the bf16 bar and identical from run to run."""
+    monkeypatch.setenv("LEMA_GEMM_TILE", "pair")
+    dev = cuda_device
+    a = rand_bf16((512, 8192), seed=51, outliers=False).to(dev)
+    b = rand_bf16((512, 8192), seed=52, outliers=False).to(dev)
+    y1 = ops.bf16_gemm_tn(a, b)
+    y2 = ops.bf16_gemm_tn(a, b)
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    _, ref = oracle.c_bf16_gemm_tn(bits(a.cpu()), bits(b.cpu()))
+    _dgrad_tol_check(bits(y1), ref)
 
 
 @pytest.mark.parametrize("path", ["1sm128", "pair"])
