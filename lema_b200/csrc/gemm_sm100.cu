@@ -21,7 +21,9 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -55,7 +57,97 @@ struct GemmParams {
   int32_t* acc;                        // raw s32 accumulators or null (int8 kind)
   int64_t ldacc;
   int32_t* err;                        // device error word
+  // Split tail: tiles [0, dp_tiles) run whole, round-robin over the workers
+  // (CTAs, or CTA pairs); each of the last split_tiles tiles is cut into two
+  // K-halves run by two workers (see WorkIter).
+  int32_t dp_tiles;
+  int32_t split_tiles;
+  int32_t* ws;        // partial accumulators: one kSlotElems slot per CTA
+  int32_t* ws_flags;  // one publish flag per slot and epilogue warp
+  int32_t y_tma;      // y is written by TMA stores through the y tensor map
+  int32_t total_rows; // rows of A (and of y)
 };
+
+// A partial slot holds one CTA's 128 rows x 256 columns of 32-bit accumulators
+// as four 32 KB blocks, one per epilogue warp (32 rows each); inside a block,
+// element (row, col) sits at col * 32 + row, so the warp's lanes store and the
+// owner's lanes read consecutive words.
+constexpr int kSlotElems = 128 * 256;
+constexpr int kSlotWarpElems = 32 * 256;
+
+enum WorkRole : int { kRoleWhole = 0, kRolePartial = 1, kRoleOwner = 2 };
+
+struct Work {
+  int tile;
+  int kb0, kb1;  // K-slices [kb0, kb1) of the tile
+  int role;
+  int contrib;   // owner: the worker that computes the other K-half
+};
+
+// The work list of one worker, identical in its producer, MMA and epilogue
+// roles: whole tiles worker, worker + W, ... < dp_tiles, then, for workers
+// w < 2 * split_tiles, one K-half of tail tile dp_tiles + w / 2: the first half
+// (even w) makes w the tile's owner, which adds the second half's partial
+// accumulators, published by worker w + 1, before writing the tile.
+struct WorkIter {
+  int w, W;
+  int next_dp;
+  bool tail_done;
+  __device__ WorkIter(const GemmParams& p, int worker, int workers)
+      : w(worker), W(workers), next_dp(worker), tail_done(false) {}
+  __device__ bool next(const GemmParams& p, Work& out) {
+    if (next_dp < p.dp_tiles) {
+      out.tile = next_dp;
+      out.kb0 = 0;
+      out.kb1 = p.num_kb;
+      out.role = kRoleWhole;
+      out.contrib = 0;
+      next_dp += W;
+      return true;
+    }
+    if (tail_done || w >= 2 * p.split_tiles) return false;
+    tail_done = true;
+    const int half = w & 1;
+    const int h = p.num_kb / 2;
+    out.tile = p.dp_tiles + w / 2;
+    out.kb0 = half ? h : 0;
+    out.kb1 = half ? p.num_kb : h;
+    out.role = half ? kRolePartial : kRoleOwner;
+    out.contrib = w + 1;
+    return true;
+  }
+};
+
+__device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* ptr) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int32_t* ptr, int32_t v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// Bounded wait until a warp block's partial is published. Lane 0 polls and the
+// outcome is broadcast, so the whole warp takes the same branch (the
+// epilogue's tcgen05.ld needs the full warp); each lane then performs its own
+// acquire load before it reads the block.
+__device__ __forceinline__ bool warp_wait_published(const int32_t* flag, int lane) {
+  int ok = 1;
+  if (lane == 0 && ld_acquire_gpu(flag) == 0) {
+    const long long t0 = clock64();
+    while (ld_acquire_gpu(flag) == 0) {
+      if (clock64() - t0 > ptx::kWaitBudgetCycles) {
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)ld_acquire_gpu(flag);
+  return ok != 0;
+}
 
 __device__ int32_t g_gemm_err = 0;
 
@@ -93,16 +185,43 @@ struct SmemLayout {
   static constexpr int kBarOffset = STAGES * kStageBytes;
   // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
-  static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  // Per epilogue warp: two 2 KB staging buffers for TMA stores (32 rows x 64 B,
+  // 64-byte swizzle, 1024-byte aligned), the tile's 256 column scales (fp32) and
+  // 256 biases (bf16).
+  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 1023) / 1024 * 1024;
+  static constexpr int kEpiWarpBytes = 6144;
+  static constexpr int kTotal = kEpiOffset + 4 * kEpiWarpBytes + 1024;  // + alignment slack
 };
+
+constexpr int kEpiStageBytes = 2048;
+constexpr int kEpiSwOffset = 2 * kEpiStageBytes;
+constexpr int kEpiBiasOffset = kEpiSwOffset + 256 * 4;
+
+// v[j] += partial[j * 32] (the other K-half of a split tile, in shared memory).
+template <int KIND>
+__device__ __forceinline__ void add_partial(uint32_t (&v)[32], const int32_t* pc) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int32_t add = pc[j * 32];
+    if (KIND == kKindI8)
+      v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + add);
+    else
+      v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __int_as_float(add)));
+  }
+}
 
 // Epilogue of one 128-row x (NCHUNK*32)-column accumulator block held in TMEM
 // columns [col0, col0 + NCHUNK*32) of this warp's lane quarter. Row r of the
-// output is this thread's row; columns start at n0.
+// output is this thread's row (row lr of the CTA's 128); columns start at n0.
+// slot != null (a partial K-range): the raw accumulators go to this warp's
+// block of the slot and nothing else is written. part != null (the owner of a
+// split tile): the other K-half's accumulators, copied to shared memory in the
+// same block layout, are added first (exact for s32; one fp32 add for bf16).
 template <int KIND, int NCHUNK>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem_row_base,
                                               uint32_t col0, int r, bool rvalid, int g, int n0,
-                                              bool y_vec, bool acc_vec) {
+                                              bool y_vec, bool acc_vec, int lane,
+                                              const int32_t* part, int32_t* slot) {
   float sxr = 0.f;
   if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
   const float* swg = (KIND == kKindI8) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
@@ -113,8 +232,15 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
     __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
     ptx::tmem_ld_32x32b_x32(tmem_row_base + col0 + static_cast<uint32_t>(c * 32), v);
     ptx::tmem_ld_wait();
+    if (slot != nullptr) {
+      int32_t* sc = slot + c * 32 * 32 + lane;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sc[j * 32] = static_cast<int32_t>(v[j]);
+      continue;
+    }
     const int n = n0 + c * 32;
     if (!rvalid || n >= p.n) continue;
+    if (part != nullptr) add_partial<KIND>(v, part + c * 32 * 32 + lane);
     const bool full_chunk = (n + 32) <= p.n;
     if (p.acc != nullptr) {  // raw accumulators: s32 (int8 kind) or fp32 bits (bf16 kind)
       int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
@@ -164,12 +290,167 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
   }
 }
 
+// Epilogue of one warp's 32 rows x (NCHUNK*32) columns through shared memory
+// and TMA stores: per 32-column chunk, the warp's results (one row per lane,
+// 64 B) go to a 64-byte-swizzled staging buffer (conflict-free 16-byte writes)
+// and one lane stores the 32 x 32 block with cp.async.bulk.tensor; two buffers
+// alternate so the next chunk is computed while the previous one is stored.
+// The column scales and biases of the tile are staged in shared memory once
+// per tile and read as warp-wide broadcasts. This keeps the epilogue's traffic
+// through the SM's L1/shared-memory path small: that path also carries the
+// main loop's TMA writes and MMA operand reads. Row r_base + lane of the
+// output; rows past the tensor map's extent and columns >= n are clipped.
+template <int KIND, int NCHUNK>
+__device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensorMap* tmap_y,
+                                             uint8_t* epi, uint32_t& store_count,
+                                             uint32_t tmem_row_base, uint32_t col0, int r_base,
+                                             int lane, bool rvalid, int g, int n0,
+                                             const int32_t* part) {
+  float* sw_s = reinterpret_cast<float*>(epi + kEpiSwOffset);
+  __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(epi + kEpiBiasOffset);
+  const bool has_bias = p.bias != nullptr;
+  __syncwarp();  // every lane is done with the previous tile's scales
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = lane * 8 + j;
+    const int n = n0 + c;
+    const bool in = n < p.n && c < NCHUNK * 32;
+    if (KIND == kKindI8) sw_s[c] = in ? __ldg(p.sw + static_cast<int64_t>(g) * p.n + n) : 0.f;
+    if (has_bias)
+      bias_s[c] = in ? p.bias[static_cast<int64_t>(g) * p.n + n] : __float2bfloat16_rn(0.f);
+  }
+  __syncwarp();
+  const int r = r_base + lane;
+  float sxr = 0.f;
+  if (KIND == kKindI8 && rvalid) sxr = p.sx[r];
+#pragma unroll 1
+  for (int c = 0; c < NCHUNK; ++c) {
+    uint32_t v[32];
+    __syncwarp();
+    ptx::tmem_ld_32x32b_x32(tmem_row_base + col0 + static_cast<uint32_t>(c * 32), v);
+    ptx::tmem_ld_wait();
+    const int n = n0 + c * 32;
+    if (n >= p.n) continue;  // uniform over the warp
+    if (part != nullptr) add_partial<KIND>(v, part + c * 32 * 32 + lane);
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float f[4];
+      if (KIND == kKindI8) {
+        const float4 s4 = *reinterpret_cast<const float4*>(sw_s + c * 32 + j);
+        f[0] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr), s4.x);
+        f[1] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j + 1])), sxr), s4.y);
+        f[2] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j + 2])), sxr), s4.z);
+        f[3] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j + 3])), sxr), s4.w);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) f[t] = __uint_as_float(v[j + t]);
+      }
+      if (has_bias) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          f[t] = __fadd_rn(f[t], __bfloat162float(bias_s[c * 32 + j + t]));
+      }
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(f[0], f[1]);
+      const __nv_bfloat162 hi = __floats2bfloat162_rn(f[2], f[3]);
+      packed[j / 2] = *reinterpret_cast<const uint32_t*>(&lo);
+      packed[j / 2 + 1] = *reinterpret_cast<const uint32_t*>(&hi);
+    }
+    uint8_t* buf = epi + (store_count & 1u) * kEpiStageBytes;
+    if (lane == 0) ptx::bulk_wait_group_read<1>();  // this buffer's previous store has read it
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int phys = q ^ ((lane >> 1) & 3);  // 64-byte swizzle: 16-B chunk ^ row bits [1,3)
+      *reinterpret_cast<uint4*>(buf + lane * 64 + phys * 16) =
+          make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::tma_store_2d(tmap_y, buf, n, r_base);
+      ptx::bulk_commit_group();
+    }
+    ++store_count;
+  }
+}
+
+// Epilogue of one work item by one epilogue warp (CTAS = CTAs per worker,
+// quarter = the warp's 32-row block of the CTA's 128 rows). The owner of a
+// split tile first waits for the matching warp of the contributor to publish
+// its block, then copies the block into the CTA's operand ring (idle once the
+// tile's MMAs are done: a split half is every worker's last item) with
+// cp.async and adds it from there. Returns false when that wait ran out (the
+// error is recorded).
+template <int KIND, int NCHUNK, int CTAS>
+__device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w, int worker,
+                                              int rank, const CUtensorMap* tmap_y, uint8_t* epi,
+                                              uint8_t* ring, uint32_t& store_count,
+                                              uint32_t tmem_row_base, uint32_t col0, int r_base,
+                                              int row_end, int g, int n0, bool y_vec,
+                                              bool acc_vec, int quarter, int lane,
+                                              int* abort_flag) {
+  if (r_base >= row_end) return true;  // no row of this warp is in the tile (owner and
+                                       // contributor agree: same tile, same rows)
+  const int r = r_base + lane;
+  const bool rvalid = r < row_end;
+  const int32_t* part = nullptr;
+  int32_t* slot = nullptr;
+  if (w.role == kRoleOwner) {
+    const int cslot = w.contrib * CTAS + rank;
+    if (!warp_wait_published(p.ws_flags + cslot * 4 + quarter, lane)) {
+      record_error(p.err, kDevErrSplitTimeout, abort_flag);
+      return false;
+    }
+    const int32_t* src =
+        p.ws + static_cast<int64_t>(cslot) * kSlotElems + quarter * kSlotWarpElems;
+    int32_t* dst = reinterpret_cast<int32_t*>(ring) + quarter * kSlotWarpElems;
+#pragma unroll 8
+    for (int i = lane; i < kSlotWarpElems / 4; i += 32) ptx::cp_async_16(dst + 4 * i, src + 4 * i);
+    ptx::cp_async_wait_all();
+    __syncwarp();
+    part = dst;
+  } else if (w.role == kRolePartial) {
+    slot = p.ws + static_cast<int64_t>(worker * CTAS + rank) * kSlotElems +
+           quarter * kSlotWarpElems;
+  }
+  // TMA stores when the warp's 32 rows are all in the group, or the rows past
+  // the group's end are past y's end too (the tensor map clips them).
+  const bool tma = p.y_tma && p.acc == nullptr && slot == nullptr &&
+                   (r_base + 32 <= row_end || row_end >= p.total_rows);
+  if (tma)
+    epilogue_tma<KIND, NCHUNK>(p, tmap_y, epi, store_count, tmem_row_base, col0, r_base, lane,
+                               rvalid, g, n0, part);
+  else
+    epilogue_rows<KIND, NCHUNK>(p, tmem_row_base, col0, r, rvalid, g, n0, y_vec, acc_vec, lane,
+                                part, slot);
+  return true;
+}
+
+// After the warp's part of a work item: a partial block is published (each
+// lane's stores made visible, then the warp's flag set); the owner clears the
+// flag it consumed, ready for the next launch.
+template <int CTAS>
+__device__ __forceinline__ void epilogue_publish(const GemmParams& p, const Work& w, int worker,
+                                                 int rank, int quarter, int lane, bool active) {
+  if (!active) return;
+  if (w.role == kRolePartial) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_gpu(p.ws_flags + (worker * CTAS + rank) * 4 + quarter, 1);
+  } else if (w.role == kRoleOwner) {
+    __syncwarp();
+    if (lane == 0) p.ws_flags[(w.contrib * CTAS + rank) * 4 + quarter] = 0;
+  }
+}
+
 // ------------------------------ 1-SM kernel --------------------------------
 
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
+                      const __grid_constant__ CUtensorMap tma_y,
                       const __grid_constant__ GemmParams p) {
   using L = SmemLayout<BN, STAGES>;
   constexpr int kTmemCols = 2 * BN;  // 256 or 512: a power of two >= 32
@@ -196,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&tma_a);
     ptx::prefetch_tmap(&tma_b);
+    if (p.y_tma) ptx::prefetch_tmap(&tma_y);
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
@@ -223,11 +505,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int64_t issued = 0;  // loads issued so far; load i used stage i % STAGES
-      for (int t = blockIdx.x; t < p.total_tiles && !aborted(abort_flag); t += gridDim.x) {
+      WorkIter it(p, blockIdx.x, gridDim.x);
+      Work w;
+      while (!aborted(abort_flag) && it.next(p, w)) {
         int g, row0, row_end, nt;
-        decode_tile<kBM>(p, t, g, row0, row_end, nt);
+        decode_tile<kBM>(p, w.tile, g, row0, row_end, nt);
         const int b_row0 = g * p.n + nt * BN;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
             record_error(p.err, kDevErrProducerTimeout, abort_flag);
             break;
@@ -259,7 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < p.total_tiles && !aborted(abort_flag); t += gridDim.x) {
+      WorkIter it(p, blockIdx.x, gridDim.x);
+      Work w;
+      while (!aborted(abort_flag) && it.next(p, w)) {
         if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
           record_error(p.err, kDevErrMmaTimeout, abort_flag);
           break;
@@ -267,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase)) {
             record_error(p.err, kDevErrMmaTimeout, abort_flag);
             ok = false;
@@ -280,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kRowBytes / kKStepBytes; ++k) {
             const uint64_t ad = ptx::desc_kmajor_sw128(a_addr + k * kKStepBytes);
             const uint64_t bd = ptx::desc_kmajor_sw128(b_addr + k * kKStepBytes);
-            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t accumulate = (kb > w.kb0 || k > 0) ? 1u : 0u;
             if (KIND == kKindI8)
               ptx::mma_i8(d_tmem, ad, bd, kIdesc, accumulate);
             else
@@ -313,24 +599,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                        (reinterpret_cast<uintptr_t>(p.y) & 15u) == 0;
     const bool acc_vec = p.acc != nullptr && (p.ldacc % 4) == 0 &&
                          (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    uint8_t* epi = smem + L::kEpiOffset + quarter * L::kEpiWarpBytes;
+    uint32_t store_count = 0;
+    WorkIter it(p, blockIdx.x, gridDim.x);
+    Work w;
+    while (it.next(p, w)) {
       int g, row0, row_end, nt;
-      decode_tile<kBM>(p, t, g, row0, row_end, nt);
+      decode_tile<kBM>(p, w.tile, g, row0, row_end, nt);
       if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
       if (aborted(abort_flag)) break;
       ptx::tc_fence_after();
-      const int r = row0 + quarter * 32 + lane;
-      epilogue_rows<KIND, BN / 32>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
-                                   static_cast<uint32_t>(acc * BN), r, r < row_end, g, nt * BN,
-                                   y_vec, acc_vec);
+      const int r_base = row0 + quarter * 32;
+      const bool ok = epilogue_work<KIND, BN / 32, 1>(
+          p, w, blockIdx.x, 0, &tma_y, epi, smem, store_count,
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
+          static_cast<uint32_t>(acc * BN), r_base, row_end, g, nt * BN, y_vec, acc_vec, quarter,
+          lane, abort_flag);
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tmem_empty[acc]);
+      if (!ok) break;
+      epilogue_publish<1>(p, w, blockIdx.x, 0, quarter, lane, r_base < row_end);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) ptx::bulk_wait_group_all();  // stores done before shared memory is released
   }
 
   ptx::tc_fence_before();
@@ -358,6 +653,7 @@ template <int KIND, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                            const __grid_constant__ CUtensorMap tma_b,
+                           const __grid_constant__ CUtensorMap tma_y,
                            const __grid_constant__ GemmParams p) {
   constexpr int kTM = 256, kTN = 256;
   using L = SmemLayout<128, STAGES>;  // per CTA: 128 A rows + 128 B rows per stage
@@ -389,6 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&tma_a);
     ptx::prefetch_tmap(&tma_b);
+    if (p.y_tma) ptx::prefetch_tmap(&tma_y);
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
@@ -417,12 +714,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int64_t issued = 0;
-      for (int t = pair; t < p.total_tiles && !aborted(abort_flag); t += npairs) {
+      WorkIter it(p, pair, npairs);
+      Work w;
+      while (!aborted(abort_flag) && it.next(p, w)) {
         int g, row0, row_end, nt;
-        decode_tile<kTM>(p, t, g, row0, row_end, nt);
+        decode_tile<kTM>(p, w.tile, g, row0, row_end, nt);
         const int a_row = row0 + static_cast<int>(rank) * 128;
         const int b_row = g * p.n + nt * kTN + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
             record_error(p.err, kDevErrProducerTimeout, abort_flag);
             break;
@@ -455,7 +754,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued_any = false;
-      for (int t = pair; t < p.total_tiles && !aborted(abort_flag); t += npairs) {
+      WorkIter it(p, pair, npairs);
+      Work w;
+      while (!aborted(abort_flag) && it.next(p, w)) {
         if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
           record_error(p.err, kDevErrMmaTimeout, abort_flag);
           break;
@@ -463,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTN);
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase)) {
             record_error(p.err, kDevErrMmaTimeout, abort_flag);
             ok = false;
@@ -476,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kRowBytes / kKStepBytes; ++k) {
             const uint64_t ad = ptx::desc_kmajor_sw128(a_addr + k * kKStepBytes);
             const uint64_t bd = ptx::desc_kmajor_sw128(b_addr + k * kKStepBytes);
-            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t accumulate = (kb > w.kb0 || k > 0) ? 1u : 0u;
             if (KIND == kKindI8)
               ptx::mma_i8_pair(d_tmem, ad, bd, kIdesc, accumulate);
             else
@@ -509,25 +810,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool acc_vec = p.acc != nullptr && (p.ldacc % 4) == 0 &&
                          (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
     const uint32_t leader_tmem_empty0 = ptx::mapa_shared(ptx::smem_u32(&tmem_empty[0]), rank & ~1u);
-    for (int t = pair; t < p.total_tiles; t += npairs) {
+    const int crank = static_cast<int>(rank & 1u);
+    uint8_t* epi = smem + L::kEpiOffset + quarter * L::kEpiWarpBytes;
+    uint32_t store_count = 0;
+    WorkIter it(p, pair, npairs);
+    Work w;
+    while (it.next(p, w)) {
       int g, row0, row_end, nt;
-      decode_tile<kTM>(p, t, g, row0, row_end, nt);
+      decode_tile<kTM>(p, w.tile, g, row0, row_end, nt);
       if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
       if (aborted(abort_flag)) break;
       ptx::tc_fence_after();
-      const int r = row0 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
-      epilogue_rows<KIND, kTN / 32>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
-                                    static_cast<uint32_t>(acc * kTN), r, r < row_end, g,
-                                    nt * kTN, y_vec, acc_vec);
+      const int r_base = row0 + crank * 128 + quarter * 32;
+      const bool ok = epilogue_work<KIND, kTN / 32, 2>(
+          p, w, pair, crank, &tma_y, epi, smem, store_count,
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
+          static_cast<uint32_t>(acc * kTN), r_base, row_end, g, nt * kTN, y_vec, acc_vec,
+          quarter, lane, abort_flag);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(leader_tmem_empty0 + static_cast<uint32_t>(acc * 8));
+      if (!ok) break;
+      epilogue_publish<2>(p, w, pair, crank, quarter, lane, r_base < row_end);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) ptx::bulk_wait_group_all();  // stores done before shared memory is released
   }
 
   ptx::tc_fence_before();
@@ -578,9 +889,28 @@ int make_operand_map(CUtensorMap* map, const void* base, CUtensorMapDataType dty
   return LEMA_OK;
 }
 
+// Output map for the TMA-store epilogue: bf16 [rows, n] with row stride ldy,
+// box = 32 columns (64 B) x 32 rows, 64-byte swizzle.
+int make_y_map(CUtensorMap* map, void* y, int64_t rows, int64_t n, int64_t ldy) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldy) * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled (y) failed (code " +
+                                        std::to_string(static_cast<int>(r)) + ")");
+  return LEMA_OK;
+}
+
 template <int KIND, int BN, int STAGES>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
-           cudaStream_t stream) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
+           const GemmParams& p, int workers, cudaStream_t stream) {
   using L = SmemLayout<BN, STAGES>;
   auto kern = gemm_sm100_kernel<KIND, BN, STAGES>;
   static bool attr_done[64] = {};
@@ -591,8 +921,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
     attr_done[dev] = true;
   }
-  const int grid = std::min(p.total_tiles, device_sm_count());
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, p);
+  kern<<<workers, kThreads, L::kTotal, stream>>>(ma, mb, my, p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }
@@ -633,25 +962,23 @@ int pair_slots() {
 }
 
 template <int KIND>
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
-                cudaStream_t stream) {
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
+                const GemmParams& p, int workers, cudaStream_t stream) {
   using L = SmemLayout<128, kPairStages>;
   auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
-  const int slots = pair_slots<KIND>();
-  if (slots <= 0) return set_error(LEMA_ERR_CUDA, "cannot size the CTA-pair grid");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * std::min(p.total_tiles, slots));
+  cfg.gridDim = dim3(2 * workers);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, p));
+  LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, p));
   return LEMA_OK;
 }
 
@@ -666,6 +993,81 @@ struct Groups {
   int num = 0;
   int64_t row_start[kMaxGroups + 1];
 };
+
+// ---- split tail: plan and per-stream workspace ----------------------------
+
+thread_local bool t_no_split = false;
+
+struct SplitWorkspace {
+  int32_t* slots = nullptr;
+  int32_t* flags = nullptr;
+  bool failed = false;
+};
+
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, SplitWorkspace> g_ws;
+
+// Partial slots for every CTA of a full grid (one per SM: 128 KB each) and
+// their publish flags, allocated once per (device, stream) so that GEMMs on
+// different streams never share them; GEMMs on one stream run in order. None
+// while this thread holds a ScopedNoGemmWorkspace, or while the stream is
+// being captured into a graph (a replay may run on another stream).
+bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags) {
+  if (t_no_split) return false;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  if (cap != cudaStreamCaptureStatusNone) return false;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  SplitWorkspace& w = g_ws[{dev, stream}];
+  if (w.failed) return false;
+  if (w.slots == nullptr) {
+    const size_t n = static_cast<size_t>(device_sm_count());
+    const size_t slot_bytes = n * kSlotElems * sizeof(int32_t);
+    const size_t flag_bytes = n * 4 * sizeof(int32_t);  // one per slot and epilogue warp
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, slot_bytes + flag_bytes) != cudaSuccess) {
+      (void)cudaGetLastError();
+      w.failed = true;
+      return false;
+    }
+    if (cudaMemset(static_cast<uint8_t*>(ptr) + slot_bytes, 0, flag_bytes) !=
+        cudaSuccess) {
+      (void)cudaGetLastError();
+      (void)cudaFree(ptr);
+      w.failed = true;
+      return false;
+    }
+    w.slots = static_cast<int32_t*>(ptr);
+    w.flags = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ptr) + slot_bytes);
+  }
+  *slots = w.slots;
+  *flags = w.flags;
+  return true;
+}
+
+// Whole tiles for floor(T / W) waves. When the remaining R tiles would occupy
+// at most half of the W workers, each is cut into two K-halves on two workers:
+// the last wave then takes half a tile-time plus the owner's fix-up (about
+// 2 us: publish, a 32 KB copy per epilogue warp, the add). Measured on B200
+// (interleaved A/B, 256 x 256 tiles): a gain from 64 K-slices of 128 B up
+// (int8 K = 11008: -6 %; bf16 K = 4096: -4 %, K = 11008: -10 %), a loss at 32
+// (int8 K = 4096: +4 %), so tiles with fewer than 64 slices run whole.
+// LEMA_GEMM_SPLIT=0 turns the split off, =1 forces it from 8 slices (tests).
+void plan_split(GemmParams& p, int workers) {
+  p.dp_tiles = p.total_tiles;
+  p.split_tiles = 0;
+  const char* env = std::getenv("LEMA_GEMM_SPLIT");
+  if (env != nullptr && std::strcmp(env, "0") == 0) return;
+  const int min_kb = (env != nullptr && std::strcmp(env, "1") == 0) ? 8 : 64;
+  const int rem = p.total_tiles % workers;
+  if (rem == 0 || 2 * rem > workers || p.num_kb < min_kb) return;
+  p.dp_tiles = p.total_tiles - rem;
+  p.split_tiles = rem;
+}
 
 enum TilePath { kPath1Sm128 = 0, kPath1Sm256 = 1, kPathPair = 2 };
 
@@ -748,6 +1150,19 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   p.total_tiles = static_cast<int32_t>(tiles);
   if (tiles == 0) return LEMA_OK;
 
+  // Workers: resident CTA pairs or SMs. Split the last wave when it pays and a
+  // workspace is available; otherwise every tile runs whole.
+  const int max_workers = path == kPathPair
+                              ? (kind == kKindI8 ? pair_slots<kKindI8>() : pair_slots<kKindBF16>())
+                              : device_sm_count();
+  if (max_workers <= 0) return set_error(LEMA_ERR_CUDA, "cannot size the GEMM grid");
+  plan_split(p, max_workers);
+  if (p.split_tiles > 0 && !split_workspace(stream, &p.ws, &p.ws_flags)) {
+    p.dp_tiles = p.total_tiles;
+    p.split_tiles = 0;
+  }
+  const int workers = p.split_tiles > 0 ? max_workers : std::min(p.total_tiles, max_workers);
+
   const CUtensorMapDataType dt =
       (kind == kKindI8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int b_box = path == kPath1Sm256 ? 256 : 128;
@@ -757,14 +1172,24 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   rc = make_operand_map(&mb, b, dt, elem, n * groups.num, k, ldb, b_box);
   if (rc) return rc;
 
-  if (kind == kKindI8) {
-    if (path == kPathPair) return launch_pair<kKindI8>(ma, mb, p, stream);
-    return path == kPath1Sm256 ? launch<kKindI8, 256, 4>(ma, mb, p, stream)
-                               : launch<kKindI8, 128, 6>(ma, mb, p, stream);
+  // y through TMA stores: 16-byte aligned rows, at least one full 32 x 32 box
+  CUtensorMap my;
+  std::memset(&my, 0, sizeof(my));
+  if (y != nullptr && aligned16(y) && (ldy * 2) % 16 == 0 && n >= 32 && rows >= 32) {
+    rc = make_y_map(&my, y, rows, n, ldy);
+    if (rc) return rc;
+    p.y_tma = 1;
   }
-  if (path == kPathPair) return launch_pair<kKindBF16>(ma, mb, p, stream);
-  return path == kPath1Sm256 ? launch<kKindBF16, 256, 4>(ma, mb, p, stream)
-                             : launch<kKindBF16, 128, 6>(ma, mb, p, stream);
+  p.total_rows = static_cast<int32_t>(rows);
+
+  if (kind == kKindI8) {
+    if (path == kPathPair) return launch_pair<kKindI8>(ma, mb, my, p, workers, stream);
+    return path == kPath1Sm256 ? launch<kKindI8, 256, 4>(ma, mb, my, p, workers, stream)
+                               : launch<kKindI8, 128, 6>(ma, mb, my, p, workers, stream);
+  }
+  if (path == kPathPair) return launch_pair<kKindBF16>(ma, mb, my, p, workers, stream);
+  return path == kPath1Sm256 ? launch<kKindBF16, 256, 4>(ma, mb, my, p, workers, stream)
+                             : launch<kKindBF16, 128, 6>(ma, mb, my, p, workers, stream);
 }
 
 // y = bias (or 0) broadcast over rows: the K == 0 case.
@@ -798,6 +1223,9 @@ int k_zero_outputs(void* y, int64_t ldy, const void* bias, int32_t* acc, int64_t
 }
 
 }  // namespace
+
+ScopedNoGemmWorkspace::ScopedNoGemmWorkspace() : prev(t_no_split) { t_no_split = true; }
+ScopedNoGemmWorkspace::~ScopedNoGemmWorkspace() { t_no_split = prev; }
 
 int gemm_read_device_error(int32_t* out) {
   int32_t v = 0, zero = 0;

@@ -35,6 +35,15 @@ enum DeviceErr : int32_t {
   kDevErrProducerTimeout = 0x101,
   kDevErrMmaTimeout = 0x102,
   kDevErrEpilogueTimeout = 0x103,
+  kDevErrSplitTimeout = 0x104,  // a split tile's partial accumulators never arrived
+};
+
+// While alive, GEMMs issued by this thread run every tile whole (no split-K
+// tail, so no workspace is allocated): the allocation-free entry point.
+struct ScopedNoGemmWorkspace {
+  ScopedNoGemmWorkspace();
+  ~ScopedNoGemmWorkspace();
+  bool prev;
 };
 
 }  // namespace lema

@@ -92,6 +92,9 @@ extern "C" int lema_w8a8_linear_fwd_noalloc(const void* x_bf16, int64_t ldx, con
   NoallocScratch s;
   int rc = noalloc_scratch(&s);
   if (rc) return rc;
+  // every GEMM tile runs whole: the split-K tail's per-stream workspace would
+  // be a device allocation
+  lema::ScopedNoGemmWorkspace no_workspace;
   return lema_w8a8_linear_fwd(x_bf16, ldx, wq, ldw, sw, bias_bf16, y_bf16, ldy, s.xq, ldq, s.sx,
                               M, N, K, stream);
 }

@@ -87,6 +87,46 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// 2-D tiled store this CTA's shared memory -> global (the tensor map clips
+// rows / columns beyond its extent), tracked in the issuing thread's bulk
+// async-group. c0 is the innermost coordinate; c0, c1 >= 0.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int32_t c0,
+                                             int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's bulk groups still read their shared
+// memory source (their buffers may then be rewritten).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until all of this thread's bulk groups have completed their writes.
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (both 16-byte aligned), waited
+// for with cp_async_wait_all by the issuing thread.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc))
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // ---- clusters (CTA pairs for cta_group::2) --------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {

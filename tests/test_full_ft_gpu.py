@@ -49,9 +49,17 @@ def test_full_ft_step_requantises_and_matches_reference_adamw(cuda_device):
         ref_w, ref_m, ref_v = adamw_step_ref(w0, g, np.zeros_like(g), np.zeros_like(g), 1,
                                              1e-3, 0.01)
         got = O.torch_bf16_to_bits(ft.true[key])
-        # the fp32 update may differ in its last bit between devices: one bf16 ulp
+        # The fp32 update may differ in its last bits between the device (fused
+        # multiply-adds in addcmul / addcdiv) and numpy: allow one bf16 ulp of the
+        # result, or, where w + update nearly cancels and the result is tiny, an
+        # absolute 2^-20 * lr (a few fp32 ulps of an update of size ~lr).
+        gf, rf = O.bf16_bits_to_f32(got), O.bf16_bits_to_f32(ref_w)
+        ulp = np.ldexp(np.float32(1.0), np.frexp(np.abs(rf))[1] - 8)
+        bound = np.maximum(ulp, np.float32(2.0 ** -20 * 1e-3))
+        excess = np.abs(gf - rf) - bound
+        assert excess.max() <= 0, (key, float(excess.max()))
         diff = np.abs(got.astype(np.int32) - ref_w.astype(np.int32))
-        assert diff.max() <= 1, (key, diff.max())
+        assert np.mean(diff == 0) > 0.99, (key, float(np.mean(diff == 0)))
         np.testing.assert_allclose(ft.m[key].numpy(), ref_m, rtol=1e-6, atol=1e-12)
         # the streamed segment now holds the quantised new weight
         layer, name = key

@@ -50,7 +50,7 @@ def test_gemm_tiny_s32_exact(cuda_device, oracle):
 
 @pytest.mark.parametrize("shape", [(512, 4096), (3, 11008), (17, 14336), (5, 20000),
                                    (64, 4104), (9, 33), (1, 8), (300, 1),
-                                   # row-pipelined kernel: several rows per CTA, 2-8 stages
+                                   # many rows (several CTA waves), long rows
                                    (2000, 4096), (700, 11008), (301, 24576), (1000, 1032)])
 def test_quantize_rows_bitexact(cuda_device, oracle, shape):
     x = rand_bf16(shape, seed=shape[0] + shape[1])
@@ -316,37 +316,53 @@ def test_bf16_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
     _dgrad_tol_check(bits(y), ref)
 
 
-# Split tail: when the last wave of tiles would leave workers idle, its tiles
-# are cut along K over all workers, the partial s32 sums published to a
-# per-stream workspace and added by the tile's owner. These shapes give few
-# tiles and long K, so each tile has several contributors.
-SPLIT_CASES = [("pair", 768, 1024, 4096),    # 12 tiles over 74 pairs: ~6 workers per tile
-               ("pair", 300, 520, 8208),     # ragged M, N and K tail
+# Split tail: when the last wave of tiles would occupy at most half of the
+# workers, each of its tiles is cut into two K-halves on two workers; the
+# second half's s32 sums are published to a per-stream workspace and added by
+# the tile's owner.
+SPLIT_CASES = [("pair", 768, 1024, 4096),     # 12 tiles halved over 24 of 74 pairs
+               ("pair", 300, 520, 8208),      # ragged M, N; 65 K-slices: halves 32 + 33
                ("1sm256", 384, 1024, 16384),  # 12 tiles over 148 CTAs
-               ("1sm128", 333, 600, 11008)]
+               ("1sm128", 333, 600, 11008),
+               ("pair", 4096, 4096, 4096)]    # 3 whole waves, then 34 tiles halved
 
 
 @pytest.mark.parametrize("path,M,N,K", SPLIT_CASES)
 def test_gemm_split_tail_bitexact(cuda_device, oracle, monkeypatch, path, M, N, K):
     monkeypatch.setenv("LEMA_GEMM_TILE", path)
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")  # split from 8 K-slices up
     dev = cuda_device
     g = torch.Generator(device=dev).manual_seed(M * 7 + K)
     a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
     b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
     sx = torch.rand(M, device=dev, generator=g) * 0.01 + 1e-4
     sw = torch.rand(N, device=dev, generator=g) * 1e-3 + 1e-5
-    for _ in range(2):  # the second launch reuses the workspace and its reset counters
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "0")
+    y_whole = ops.w8a8_gemm(a, sx, b, sw)
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")
+    for _ in range(2):  # the second launch reuses the workspace and its reset flags
         y, acc = ops.w8a8_gemm(a, sx, b, sw, want_acc=True)
-        np.testing.assert_array_equal(acc.cpu().numpy(),
-                                      oracle.c_int8_gemm(a.cpu().numpy(), b.cpu().numpy()))
+        y2 = ops.w8a8_gemm(a, sx, b, sw)  # TMA-store epilogue (no raw accumulator output)
+        assert torch.equal(y2.view(torch.int16), y_whole.view(torch.int16))
+        if M * N * K <= 2 ** 31:
+            ref = oracle.c_int8_gemm(a.cpu().numpy(), b.cpu().numpy())
+        else:  # exact row / column sums and a corner block
+            rs, cs = oracle.c_int8_gemm_checksums(a.cpu().numpy(), b.cpu().numpy())
+            np.testing.assert_array_equal(acc.long().sum(1).cpu().numpy(), rs)
+            np.testing.assert_array_equal(acc.long().sum(0).cpu().numpy(), cs)
+            ref = acc.cpu().numpy().copy()
+            ref[-200:, -300:] = oracle.c_int8_gemm(a[-200:].cpu().numpy(), b[-300:].cpu().numpy())
+        np.testing.assert_array_equal(acc.cpu().numpy(), ref)
         yref = oracle.c_epilogue(acc.cpu().numpy(), sx.cpu().numpy(), sw.cpu().numpy(), None)
         np.testing.assert_array_equal(bits(y), yref)
+        np.testing.assert_array_equal(bits(y2), yref)
 
 
 def test_bf16_gemm_split_tail_deterministic(cuda_device, oracle, monkeypatch):
     """bf16 kind: the owner adds fp32 partials in a fixed order, so a split GEMM
     is within the bf16 bar and identical from run to run."""
     monkeypatch.setenv("LEMA_GEMM_TILE", "pair")
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")
     dev = cuda_device
     a = rand_bf16((512, 8192), seed=51, outliers=False).to(dev)
     b = rand_bf16((512, 8192), seed=52, outliers=False).to(dev)
