@@ -14,6 +14,13 @@ Workloads (``--workload``):
                     attention, activations offloaded, selective full
                     fine-tuning of q/k/v/o in the last 4 layers (fp32 AdamW
                     states in pinned host RAM). Metric: tokens/s.
+  mixtral_streamed_lora
+                    one LoRA training step of a 32-layer Mixtral-8x7B-shaped
+                    MoE model (GQA 32 q / 8 kv heads, 8 experts x SwiGLU
+                    14336, top-2 softmax routing; W8A8 attention projections
+                    and grouped W8A8 experts, 1.45 GB per layer) on bs=8 x
+                    seq=512 per GPU, streamed from pinned host RAM as above.
+                    Metric: tokens/s. Needs ~47 GB of pinned host RAM per rank.
   w8a8_linear_4096  one W8A8 linear forward step (K1 quantise + K2/K3 GEMM with
                     fused epilogue) at M=N=K=4096, the per-layer shape of the
                     7B streamed model at bs=8 x seq=512. Metric: int8 TOPS.
@@ -323,6 +330,24 @@ def run_linear(args, world, rank, local) -> dict | None:
 # GPU workload: one streamed LoRA training step of the 7B-shaped model
 # ---------------------------------------------------------------------------
 
+def check_host_ram(shape, ranks_on_host: int) -> None:
+    """Refuses (before pinning anything) a streamed workload whose pinned weight
+    segments, for every rank on this host, would not fit in 80 % of the host's
+    available memory."""
+    import psutil
+    per_layer = 0
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        o, i = shape.proj_shapes()[n]
+        per_layer += o * i
+    per_layer += 3 * shape.experts * shape.intermediate * shape.hidden
+    need = per_layer * shape.layers * ranks_on_host
+    avail = psutil.virtual_memory().available
+    if need > 0.8 * avail:
+        raise RuntimeError(f"{need / 1e9:.0f} GB of pinned weight segments needed for "
+                           f"{ranks_on_host} rank(s) on this host, {avail / 1e9:.0f} GB "
+                           "available: refusing")
+
+
 def measure_h2d_gbs(dev, nbytes=1 << 30) -> float:
     """Pinned host -> device copy bandwidth of this GPU (one 1 GiB copy, best of 3)."""
     src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -339,39 +364,60 @@ def measure_h2d_gbs(dev, nbytes=1 << 30) -> float:
     return nbytes / (best / 1e3) / 1e9
 
 
-def cpu_train_sample(seq: int, threads: int) -> dict:
+def cpu_train_sample(seq: int, threads: int, moe: bool = False, reps: int = 1) -> dict:
     """CPU restatement of one streamed layer's work (no-grad forward, recompute
-    with grad, backward) on one Llama-2-7B-shaped block with the oracle's W8A8
-    linears, LoRA r16 on q/v, for `seq` tokens; scaled to the 32-layer model
-    (the embedding/head are not included)."""
+    with grad, backward) on one Llama-2-7B-shaped block (or, with ``moe``, one
+    Mixtral-8x7B-shaped block: GQA attention + 8 experts, top-2) with the
+    oracle's W8A8 linears (and W8A8 experts), LoRA r16 on q/v, for `seq` tokens;
+    scaled to the 32-layer model (the embedding/head are not included)."""
     from lema_b200.llama import LlamaBlock, LlamaShape, apply_lora, rope_cos_sin
     from oracle import oracle as O
-    from oracle.torch_ref import swap_linears
+    from oracle.torch_ref import OracleExperts, swap_linears
     torch.set_num_threads(threads)
     O.set_threads(threads)
-    shape = LlamaShape()
     g = torch.Generator().manual_seed(0)
-    blk = LlamaBlock(shape, quantized=False, device="cpu")
+    if moe:
+        from lema_b200.moe import MixtralBlock, MixtralShape
+        shape = MixtralShape()
+        blk = MixtralBlock(shape, quantized=False, device="cpu")
+        names = ("q_proj", "k_proj", "v_proj", "o_proj")
+        label = "Mixtral-8x7B-shaped"
+    else:
+        shape = LlamaShape()
+        blk = LlamaBlock(shape, quantized=False, device="cpu")
+        names = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+        label = "Llama-2-7B-shaped"
     with torch.no_grad():
         for name, p in blk.named_parameters():
-            if "layernorm" not in name:
-                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+            if "layernorm" in name:
+                continue
+            std = shape.hidden ** -0.5 if name.endswith("gate.weight") else 0.02
+            p.copy_(std * torch.randn(p.shape, generator=g))
     apply_lora(blk, 16, 32.0)
-    swap_linears(blk)
+    swap_linears(blk, names)
+    if moe:
+        ex = blk.mlp.experts
+        blk.mlp.experts = OracleExperts(ex.gate_up_proj.data, ex.down_proj.data)
+        for m in list(blk.mlp.experts.gu) + list(blk.mlp.experts.dn):
+            m.wdeq_f32()
     blk.self_attn.attn_impl = "eager"
-    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+    for name in names:
         blk.base_projection(name).wdeq_f32()  # frozen weights: dequantised once, outside timing
     x = torch.randn(1, seq, shape.hidden, generator=g).to(torch.bfloat16)
     dy = torch.randn(1, seq, shape.hidden, generator=g).to(torch.bfloat16)
     cos, sin = rope_cos_sin(shape, seq, "cpu", torch.bfloat16)
-    t0 = time.perf_counter()
-    with torch.no_grad():
-        blk(x, cos, sin)
-    xr = x.clone().requires_grad_(True)
-    blk(xr, cos, sin).backward(dy)
-    t_layer = time.perf_counter() - t0
+    times = []
+    for _ in range(max(1, reps)):  # the layer is built once; each repeat is timed alone
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            blk(x, cos, sin)
+        xr = x.clone().requires_grad_(True)
+        blk(xr, cos, sin).backward(dy)
+        times.append(time.perf_counter() - t0)
+    t_layer = statistics.median(times)
     return {"tokens_per_s": seq / (shape.layers * t_layer), "seconds_per_layer": t_layer,
-            "sample": f"1 Llama-2-7B-shaped layer, {seq} tokens, no-grad forward + recompute + "
+            "reps": times,
+            "sample": f"1 {label} layer, {seq} tokens, no-grad forward + recompute + "
                       f"backward through the oracle W8A8 linears ({t_layer:.2f} s), scaled x32 "
                       "layers (embedding / lm_head excluded)"}
 
@@ -384,7 +430,22 @@ def run_train(args, world, rank, local) -> dict | None:
     dev = torch.device("cuda", local)
     shape = LlamaShape(layers=args.layers)
     long_ft = args.workload == "llama7b_selective_ft_2048"
-    if long_ft:
+    moe = args.workload == "mixtral_streamed_lora"
+    model = "Llama-2-7B"
+    if moe:
+        from lema_b200.moe import MixtralShape
+        shape = MixtralShape(layers=args.layers)
+        model = "Mixtral-8x7B"
+        check_host_ram(shape, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+        batch, seq = 8, 512
+        tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
+                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers)
+        workload = (f"mixtral_streamed_lora: {shape.layers} x [hidden 4096, 32 q / 8 kv heads "
+                    "x 128, 8 experts x SwiGLU 14336, top-2 softmax routing], vocab 32000, LoRA "
+                    "r16 a32 on q/v, W8A8 attention projections and grouped W8A8 experts "
+                    f"streamed from pinned RAM ({tr.ws.seg_bytes / 1e9:.2f} GB per layer), "
+                    "activation checkpoints offloaded")
+    elif long_ft:
         # bs 1 x seq 2048, 512-token chunked attention, activations offloaded, selective
         # full fine-tuning of q/k/v/o in the last 4 layers (fp32 AdamW states in host RAM)
         batch, seq = 1, 2048
@@ -417,6 +478,7 @@ def run_train(args, world, rank, local) -> dict | None:
     clocks.start()
     barrier(world)
     torch.cuda.synchronize(dev)
+    launches0 = _native.kernel_launches
     ops.GemmTimer.enable(True)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -428,6 +490,7 @@ def run_train(args, world, rank, local) -> dict | None:
     torch.cuda.synchronize(dev)
     barrier(world)
     clk = clocks.stop()
+    launches = _native.kernel_launches - launches0
     gemm_ops, gemm_ms, gemm_launches = ops.GemmTimer.summary()
     ops.GemmTimer.enable(False)
     ms = t0.elapsed_time(t1)
@@ -479,24 +542,25 @@ def run_train(args, world, rank, local) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "int8 W8A8 projections (bf16 activations; bf16 attention, LoRA, lm_head)",
-        "data": "synthetic (random-init Llama-2-7B-shaped weights, token ids uniform in "
+        "data": f"synthetic (random-init {model}-shaped weights, token ids uniform in "
                 "[0, 32000), labels = inputs)",
         "config": {"workload": workload,
                    "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}",
                    "resident_layers": args.resident_layers,
-                   "l2": "per-step weight stream 12.9 GB and activations >> L2"},
-        "gpu_launches": 42 * shape.layers * args.steps,
+                   "l2": f"per-step weight stream {h2d_per_step / 1e9:.1f} GB and "
+                         "activations >> L2"},
+        "gpu_launches": launches,
         "loss_last": round(float(losses[-1]), 4),
-        "roofline": {"bound": "tensor", "kernel": "gemm_sm100 int8 (all W8A8 projection GEMMs "
-                                                  "of the timed steps)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_sm100 int8 (all W8A8 projection and "
+                                                  "grouped expert GEMMs of the timed steps)",
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                      "frac": round(achieved / int8_peak, 4),
                      "peak_source": "measured cuBLASLt int8 GEMM (torch._int_mm 8192^3, burst)",
                      "frac_of_spec_4500": round(achieved / INT8_SPEC_TOPS, 4),
                      # DRAM bytes (read + write) per launch, averaged over a layer's four
                      # int8 GEMMs, from an ncu capture of this workload (4 metrics, 8 launches)
-                     "traffic": TRAIN_GEMM_TRAFFIC_BYTES if not long_ft else None,
+                     "traffic": TRAIN_GEMM_TRAFFIC_BYTES if not (long_ft or moe) else None,
                      "gemm_launches": gemm_launches,
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
                      "algorithmic_ops_per_step": gemm_ops / args.steps},
@@ -511,7 +575,7 @@ def run_train(args, world, rank, local) -> dict | None:
     }
     if not args.skip_cpu:
         threads = os.cpu_count() or 1
-        c = cpu_train_sample(args.cpu_seq, threads)
+        c = cpu_train_sample(args.cpu_seq, threads, moe=moe)
         res["cpu_baseline"] = {"value": round(c["tokens_per_s"], 3), "unit": "tokens/s",
                                "cores": threads, "kind": "port", "sample": c["sample"]}
     return res
@@ -545,16 +609,19 @@ def run_reference(args) -> dict | None:
         return None
     threads = os.cpu_count() or 1
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048"):
-        vals = [cpu_train_sample(args.cpu_seq, threads) for _ in range(args.steps)]
-        tps = statistics.median(v["tokens_per_s"] for v in vals)
+    if args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048",
+                         "mixtral_streamed_lora"):
+        moe = args.workload == "mixtral_streamed_lora"
+        c = cpu_train_sample(args.cpu_seq, threads, moe=moe, reps=args.steps)
+        vals = [c]
+        tps = c["tokens_per_s"]
         return {
             "metric": METRIC, "impl": "reference", "value": round(tps, 3),
             "unit": "tokens/s (whole job)", "n_gpus": world, "steps": args.steps,
             "warmup": 0, "ms_per_step": round(8 * 512 / tps * 1e3, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 W8A8 projections (bf16 activations)", "data": "synthetic",
-            "config": {"workload": "llama7b_streamed_lora (per-layer CPU sample, scaled)",
+            "config": {"workload": f"{args.workload} (per-layer CPU sample, scaled)",
                        "global_batch": 8, "seq_len": 512, "parallelism": "cpu"},
             "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads,
                              "kind": "port", "sample": vals[0]["sample"]},
@@ -592,6 +659,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama7b_streamed_lora",
                     choices=["llama7b_streamed_lora", "llama7b_selective_ft_2048",
+                             "mixtral_streamed_lora",
                              "w8a8_linear_4096"])
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
@@ -603,7 +671,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--int8-peak-tops", type=float, default=0.0)
     args = ap.parse_args()
-    train = args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048")
+    train = args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048",
+                              "mixtral_streamed_lora")
     if args.steps is None:
         args.steps = (3 if args.impl == "reference" else 10) if train else 50
     if args.warmup is None:

@@ -117,11 +117,30 @@ def last_error() -> str:
     return lib().lema_last_error().decode()
 
 
+# Kernels each entry point launches (the checkpoint save launches one only in
+# its SM-store mode 1; its copy-engine mode and the restore launch none).
+KERNELS_PER_CALL = {
+    "lema_quantize_rows": 1, "lema_quantize_rows_f32": 1, "lema_quantize_per_token": 1,
+    "lema_w8a8_gemm": 1, "lema_w8a8_linear_fwd": 2, "lema_w8a8_linear_fwd_noalloc": 2,
+    "lema_dequant_transpose": 1, "lema_bf16_gemm_tn": 1, "lema_bf16_gemm_tn_f32": 1,
+    "lema_w8a8_dgrad": 2, "lema_grouped_w8a8_gemm": 1, "lema_grouped_bf16_gemm_tn": 1,
+    "lema_grouped_w8a8_dgrad": 2, "lema_rmsnorm_quant": 1, "lema_rmsnorm_bwd": 1,
+    "lema_rope": 1, "lema_rope_qkv": 1, "lema_swiglu_quant": 1, "lema_swiglu_bwd": 1,
+}
+# Running count of this library's kernel launches issued by this process.
+kernel_launches = 0
+
+
 def call(name: str, *args) -> None:
     """Invokes a status-returning entry point and raises LemaError on failure."""
+    global kernel_launches
     rc = getattr(lib(), name)(*args)
     if rc != LEMA_OK:
         raise LemaError(rc, last_error(), name)
+    if name == "lema_ckpt_save":
+        kernel_launches += 1 if args[3] == 1 else 0
+    else:
+        kernel_launches += KERNELS_PER_CALL.get(name, 0)
 
 
 def version() -> str:

@@ -198,13 +198,17 @@ class LlamaBlock(nn.Module):
     # "down" + ".wq" / ".sw"), set when the block is bound to a weight segment.
     fused_weights: dict | None = None
     use_fused = True
+    # W8A8 projections of this block type (the fused path covers all of them)
+    FUSABLE = PROJECTIONS
+    FUSED_GROUPS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
+                    ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",)))
 
     def _can_fuse(self) -> bool:
         if not (self.use_fused and self.fused_weights is not None):
             return False
         if self.gradient_checkpointing or self.self_attn.attn_impl != "sdpa":
             return False
-        for name in PROJECTIONS:
+        for name in self.FUSABLE:
             m = self.projection(name)
             if getattr(self.base_projection(name), "wgrad_acc", None) is not None:
                 return False  # trainable projections take the per-projection path
@@ -239,8 +243,7 @@ class LlamaBlock(nn.Module):
         def cat(names, what):
             return torch.cat([getattr(self.base_projection(n), what) for n in names], dim=0)
         self.fused_weights = {}
-        for group, names in (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
-                             ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",))):
+        for group, names in self.FUSED_GROUPS:
             self.fused_weights[group + ".wq"] = cat(names, "weight").contiguous()
             self.fused_weights[group + ".sw"] = cat(names, "weight_scale").contiguous()
 
@@ -250,6 +253,10 @@ class LlamaBlock(nn.Module):
         rotating q/k and laying v out contiguously, SDPA,
         o_proj, residual, RMSNorm -> quantise, stacked gate/up GEMM, SwiGLU ->
         quantise (one kernel), down GEMM, residual."""
+        return self._mlp_fused(self._attention_fused(h, cos, sin))
+
+    def _attention_fused(self, h, cos, sin):
+        """h + attention(input_layernorm(h)) through the fused producers."""
         from . import ops
         sh = self.shape
         B, S, H = h.shape
@@ -277,7 +284,15 @@ class LlamaBlock(nn.Module):
             o = F.scaled_dot_product_attention(qv, kv, vv, is_causal=True, scale=d ** -0.5,
                                                enable_gqa=gqa)
         o2d = o.transpose(1, 2).reshape(B * S, nq)
-        h2 = h + att.o_proj(o2d).view(B, S, H)
+        return h + att.o_proj(o2d).view(B, S, H)
+
+    def _mlp_fused(self, h2):
+        """h2 + mlp(post_attention_layernorm(h2)): RMSNorm -> quantise, stacked
+        gate/up GEMM, SwiGLU -> quantise, down GEMM."""
+        from . import ops
+        sh = self.shape
+        B, S, H = h2.shape
+        fw = self.fused_weights
         hn2, xq2, sx2 = ops.RMSNormQuantFn.apply(h2.reshape(-1, H),
                                                  self.post_attention_layernorm.weight, sh.eps)
         y = ops.MLPFn.apply(hn2, xq2, sx2, fw["gate_up.wq"], fw["gate_up.sw"], fw["down.wq"],

@@ -26,7 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
-from .llama import LlamaAttention, LlamaShape, RMSNorm
+from .llama import LlamaAttention, LlamaBlock, LlamaShape, RMSNorm
 
 
 @dataclass(frozen=True)
@@ -189,24 +189,30 @@ class SparseMoe(nn.Module):
         return self.experts(x2d, top_i, top_w).reshape(B, S, H)
 
 
-class MixtralBlock(nn.Module):
+class MixtralBlock(LlamaBlock):
     """Mixtral decoder layer: RMSNorm, GQA attention (W8A8 q/k/v/o), RMSNorm,
-    sparse MoE with W8A8 experts, two residual adds."""
+    sparse MoE with W8A8 experts, two residual adds. The attention half takes the
+    fused producer path of LlamaBlock (RMSNorm -> quantise, stacked q/k/v GEMM,
+    RoPE with the LoRA addends); the MoE half runs the bf16 router and the two
+    grouped W8A8 GEMMs (SparseMoe)."""
 
-    gradient_checkpointing = False
+    FUSABLE = ("q_proj", "k_proj", "v_proj", "o_proj")
+    FUSED_GROUPS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)))
 
     def __init__(self, shape: MixtralShape, quantized: bool = True, device=None,
                  dtype=torch.bfloat16):
-        super().__init__()
+        nn.Module.__init__(self)
         self.shape = shape
         self.input_layernorm = RMSNorm(shape.hidden, shape.eps, device, dtype)
         self.self_attn = LlamaAttention(shape, quantized, device, dtype)
         self.post_attention_layernorm = RMSNorm(shape.hidden, shape.eps, device, dtype)
         self.mlp = SparseMoe(shape, quantized, device, dtype)
 
-    def forward(self, h, cos, sin):
-        residual = h
-        h = self.self_attn(self.input_layernorm(h), cos, sin)
-        h = residual + h
-        residual = h
-        return residual + self.mlp(self.post_attention_layernorm(h))
+    def projection(self, name: str) -> nn.Module:
+        if name not in self.FUSABLE:
+            raise KeyError(f"{name} is not a projection of a Mixtral block (the experts are "
+                           "grouped tensors)")
+        return getattr(self.self_attn, name)
+
+    def _mlp_fused(self, h2):
+        return h2 + self.mlp(self.post_attention_layernorm(h2))

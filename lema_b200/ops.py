@@ -276,9 +276,19 @@ def grouped_w8a8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: 
     offs = (C.c_int64 * (E + 1))(*[int(o) for o in offsets])
     if bias is not None:
         bias = bias.contiguous().to(torch.bfloat16)
-    N.call("lema_grouped_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx.contiguous().float()),
-           _ptr(wq), wq.stride(1), _ptr(sw.contiguous().float()), _ptr(bias), _ptr(y), Nn,
-           offs, E, Nn, K, _stream(dev))
+    args = ("lema_grouped_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx.contiguous().float()),
+            _ptr(wq), wq.stride(1), _ptr(sw.contiguous().float()), _ptr(bias), _ptr(y), Nn,
+            offs, E, Nn, K, _stream(dev))
+    if not GemmTimer.enabled:
+        N.call(*args)
+        return y
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    N.call(*args)
+    e1.record(s)
+    GemmTimer.records.append((e0, e1, 2.0 * (int(offsets[-1]) - int(offsets[0])) * Nn * K))
     return y
 
 

@@ -16,6 +16,9 @@ norm weights as one 128-byte-aligned segment per block in pinned host memory
 213-302) and streams segments into two VRAM slots through the native memory
 manager (``lema_mm_*``), binding W8A8Linear weights as views of the slot
 instead of copying them into parameters (src/lema/adapters/_llama.py:95-100).
+A Mixtral block's segment holds its attention projections the same way plus
+the grouped expert tensors (int8 gate_up [E, 2I, H], down [E, H, I], their
+scales) and the bf16 router weight, bound into the block's experts module.
 """
 from __future__ import annotations
 
@@ -25,7 +28,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as N
-from .llama import PROJECTIONS, LlamaBlock, LlamaShape
+from .llama import LlamaBlock, LlamaShape
 
 
 def _ev_ptr(ev: torch.cuda.Event | None):
@@ -100,10 +103,12 @@ class WeightSegments:
     manager's H2D copy stream."""
 
     ALIGN = 128
-    GROUPS = (("qkv", ("q_proj", "k_proj", "v_proj")), ("o", ("o_proj",)),
-              ("gate_up", ("gate_proj", "up_proj")), ("down", ("down_proj",)))
 
     def __init__(self, shape: LlamaShape, num_blocks: int, device: torch.device):
+        from .moe import MixtralBlock, MixtralShape
+        self.moe = isinstance(shape, MixtralShape)
+        block_cls = MixtralBlock if self.moe else LlamaBlock
+        self.GROUPS = block_cls.FUSED_GROUPS
         self.shape = shape
         self.device = torch.device(device)
         self.num_blocks = num_blocks
@@ -130,10 +135,17 @@ class WeightSegments:
                 self.sub[n + ".wq"] = (group + ".wq", r0, r1)
                 self.sub[n + ".sw"] = (group + ".sw", r0, r1)
                 r0 = r1
+        if self.moe:
+            E, I, H = shape.experts, shape.intermediate, shape.hidden
+            add("experts.gate_up.wq", (E, 2 * I, H), torch.int8)
+            add("experts.gate_up.sw", (E, 2 * I), torch.float32)
+            add("experts.down.wq", (E, H, I), torch.int8)
+            add("experts.down.sw", (E, H), torch.float32)
+            add("router", (E, H), torch.bfloat16)
         add("input_layernorm", (shape.hidden,), torch.bfloat16)
         add("post_attention_layernorm", (shape.hidden,), torch.bfloat16)
         self.seg_bytes = off
-        self.ram = torch.empty(num_blocks, self.seg_bytes, dtype=torch.uint8).pin_memory()
+        self.ram = torch.empty(num_blocks, self.seg_bytes, dtype=torch.uint8, pin_memory=True)
         self.vram = [torch.empty(self.seg_bytes, dtype=torch.uint8, device=self.device)
                      for _ in range(2)]
         self.mm = C.c_void_p()
@@ -206,8 +218,15 @@ class WeightSegments:
         block the stacked group weights for its fused path."""
         block.fused_weights = {g + k: self._view(buf, g + k) for g, _ in self.GROUPS
                                for k in (".wq", ".sw")}
-        for name in PROJECTIONS:
+        for name in block.FUSABLE:
             block.base_projection(name).bind(self._view(buf, name + ".wq"),
                                              self._view(buf, name + ".sw"))
+        if self.moe:
+            ex = block.mlp.experts
+            ex.wq_gate_up = self._view(buf, "experts.gate_up.wq")
+            ex.sw_gate_up = self._view(buf, "experts.gate_up.sw")
+            ex.wq_down = self._view(buf, "experts.down.wq")
+            ex.sw_down = self._view(buf, "experts.down.sw")
+            block.mlp.gate.weight.data = self._view(buf, "router")
         block.input_layernorm.weight.data = self._view(buf, "input_layernorm")
         block.post_attention_layernorm.weight.data = self._view(buf, "post_attention_layernorm")

@@ -99,11 +99,15 @@ class StreamedLoraTrainer:
         for p in self.head.parameters():
             p.requires_grad_(False)
         # int8 segments of every block in pinned RAM (quantised once, on the device)
+        from .moe import MixtralBlock, MixtralShape
+        moe = isinstance(shape, MixtralShape)
+        block_cls = MixtralBlock if moe else LlamaBlock
         self.ws = WeightSegments(shape, self.L, dev)
         true_weights = {}
         for b in range(self.L):
             tensors = {}
-            for name, (o, i) in shape.proj_shapes().items():
+            for name in block_cls.FUSABLE:
+                o, i = shape.proj_shapes()[name]
                 w = torch.empty(o, i, device=dev, dtype=torch.bfloat16).normal_(0.0, 0.02,
                                                                                  generator=g)
                 if b in full_ft_layers and name in full_ft_modules:
@@ -115,12 +119,16 @@ class StreamedLoraTrainer:
             tensors["input_layernorm"] = ones
             tensors["post_attention_layernorm"] = ones
             self.ws.pack_block(b, tensors)
+            if moe:
+                self._pack_experts(b, g)
         torch.cuda.synchronize(dev)
         # optional HBM-resident copies of the first `resident_layers` segments
         self.resident = [self.ws.ram[b].to(dev) for b in range(min(resident_layers, self.L))]
         # two block modules, bound per layer (the reference's module pool)
-        self.blocks = [LlamaBlock(shape, quantized=True, device=dev) for _ in range(2)]
+        self.blocks = [block_cls(shape, quantized=True, device=dev) for _ in range(2)]
         for blk in self.blocks:
+            for p in blk.parameters():  # frozen base: norms, router (LoRA is added below)
+                p.requires_grad_(False)
             if targets:
                 apply_lora(blk, lora_rank, lora_alpha, targets)
             blk.gradient_checkpointing = gradient_checkpointing
@@ -156,6 +164,26 @@ class StreamedLoraTrainer:
         self.global_step = 0
 
     # ---- weights -----------------------------------------------------------
+    @torch.no_grad()
+    def _pack_experts(self, b: int, g: torch.Generator) -> None:
+        """Random-init experts of a MoE block (N(0, 0.02), as HF initialises
+        MixtralExperts), quantised per output channel one expert at a time, and a
+        router drawn N(0, 1/hidden) so that its logits on RMS-normalised inputs are
+        ~N(0, 1)."""
+        sh, dev, ws = self.shape, self.device, self.ws
+        ram = ws.ram[b]
+        for e in range(sh.experts):
+            for name, (o, i) in (("gate_up", (2 * sh.intermediate, sh.hidden)),
+                                 ("down", (sh.hidden, sh.intermediate))):
+                w = torch.empty(o, i, device=dev, dtype=torch.bfloat16).normal_(0.0, 0.02,
+                                                                                 generator=g)
+                wq, sw = ops.quantize_weight(w)
+                ws._view(ram, f"experts.{name}.wq")[e].copy_(wq)
+                ws._view(ram, f"experts.{name}.sw")[e].copy_(sw)
+        router = torch.empty(sh.experts, sh.hidden, device=dev, dtype=torch.bfloat16)
+        router.normal_(0.0, sh.hidden ** -0.5, generator=g)
+        ws._view(ram, "router").copy_(router)
+
     def _ensure(self, layer: int) -> None:
         """Starts the upload of ``layer`` into its slot unless it is already there."""
         slot = layer % 2
