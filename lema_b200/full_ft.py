@@ -15,6 +15,13 @@ re-quantised per output channel on the device (K1) and the int8 rows and
 scales are written back into the layer's pinned-RAM segment, from which the
 next forward streams them. The backward is straight-through: dx as for frozen
 projections, dW = dy^T . x with fp32 accumulation (``lema_bf16_gemm_tn_f32``).
+
+The reference clips and steps the selected layers after the whole backward;
+each layer's clip and step read only that layer's accumulators, final once its
+own backward is done, so ``step_layer_async`` runs them right then on a side
+stream (device-side clip, non-blocking pinned copies both ways), overlapping
+the optimizer's PCIe round trips with the backward of the remaining layers.
+``finish`` waits for that stream before the pinned weights are read again.
 """
 from __future__ import annotations
 
@@ -44,6 +51,7 @@ class SelectiveFullFT:
             self.v[key] = torch.zeros(w.shape, dtype=torch.float32).pin_memory()
             self.acc[key] = torch.zeros(w.shape, dtype=torch.float32, device=self.device)
         self.layer_steps: dict[int, int] = {}
+        self.stream = torch.cuda.Stream(self.device)
 
     def attach(self, layer: int, block) -> None:
         """Makes the selected projections of ``block`` (bound to ``layer``) trainable."""
@@ -54,13 +62,21 @@ class SelectiveFullFT:
     def layer_grads(self, layer: int) -> list[torch.Tensor]:
         return [self.acc[(layer, n)] for n in self.modules if (layer, n) in self.acc]
 
-    def clip_layer_(self, layer: int, max_norm: float = 1.0) -> float:
+    def clip_layer_(self, layer: int, max_norm: float = 1.0) -> torch.Tensor:
+        """Scales the layer's accumulators by max_norm / norm when their joint
+        norm exceeds max_norm (reference :194-202), on the device: the per-tensor
+        fp32 sums of squares are added in fp64 as the reference's Python floats are,
+        and the fp32 multiply by 1.0 when no clipping is due leaves them unchanged.
+        Returns the norm (device tensor)."""
         accs = self.layer_grads(layer)
-        total = sum(float(a.pow(2).sum()) for a in accs)
-        norm = math.sqrt(total)
-        if norm > max_norm and norm > 0:
-            for a in accs:
-                a.mul_(max_norm / norm)
+        total = torch.zeros((), dtype=torch.float64, device=self.device)
+        for a in accs:
+            total = total + a.pow(2).sum().double()
+        norm = total.sqrt()
+        coeff = torch.where(norm > max_norm, max_norm / norm, torch.ones_like(norm))
+        coeff = coeff.float()
+        for a in accs:
+            a.mul_(coeff)
         return norm
 
     @torch.no_grad()
@@ -88,14 +104,34 @@ class SelectiveFullFT:
             # re-quantise the new weight into the layer's streamed int8 segment
             wq, sw = ops.quantize_weight(wb)
             ram = self.ws.ram[layer]
-            self.ws._view(ram, name + ".wq").copy_(wq)
-            self.ws._view(ram, name + ".sw").copy_(sw)
-            self.true[key].copy_(wb)
-            self.m[key].copy_(m)
-            self.v[key].copy_(v)
+            # pinned destinations, copies ordered on this stream (the device
+            # temporaries are freed only after them, stream-ordered)
+            self.ws._view(ram, name + ".wq").copy_(wq, non_blocking=True)
+            self.ws._view(ram, name + ".sw").copy_(sw, non_blocking=True)
+            self.true[key].copy_(wb, non_blocking=True)
+            self.m[key].copy_(m, non_blocking=True)
+            self.v[key].copy_(v, non_blocking=True)
             g.zero_()
+
+    def step_layer_async(self, layer: int, reduce_entry=None, reducer=None) -> None:
+        """Clips and steps ``layer`` on the side stream once the current stream's
+        work so far (the layer's backward) is done; with data parallelism the
+        layer's gradient bucket is first averaged over the ranks (the side stream
+        waits for its all-reduce)."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            if reduce_entry is not None:
+                reducer.finish(reduce_entry)
+            self.clip_layer_(layer, 1.0)
+            self.step_layer(layer)
+
+    def finish(self) -> None:
+        """Waits (host) for every pending layer step: the pinned weights, moments
+        and int8 segments are then current."""
+        self.stream.synchronize()
 
     def step(self) -> None:
         for layer in self.layers:
             self.clip_layer_(layer, 1.0)
             self.step_layer(layer)
+        torch.cuda.current_stream(self.device).synchronize()

@@ -17,7 +17,10 @@
   finished layer's LoRA gradients start their data-parallel all-reduce
   (NCCL) while the next layer computes;
 * selective full fine-tuning (reference :169-181, src/lema/_full_ft.py) of
-  chosen projections of chosen layers, see ``full_ft.SelectiveFullFT``;
+  chosen projections of chosen layers, see ``full_ft.SelectiveFullFT``: each
+  selected layer is clipped and stepped on a side stream as soon as its own
+  backward is done (the reference does the same per-layer arithmetic after
+  the whole backward);
 * optimizer (reference :183-187): every ``grad_accum`` micro-steps (the loss
   is divided by ``grad_accum`` as at reference :156), clip_grad_norm_(1.0) and
   AdamW over the LoRA parameters; with data parallelism the LoRA gradients
@@ -52,24 +55,35 @@ class LoraGradReducer:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self._pending: list[tuple[object, torch.Tensor, list[torch.Tensor]]] = []
 
-    def launch(self, grads: list[torch.Tensor]) -> None:
+    def launch(self, grads: list[torch.Tensor]):
+        """Starts the all-reduce of one bucket; returns its entry (None when there
+        is nothing to reduce)."""
         if self.world == 1 or not grads:
-            return
+            return None
         flat = torch.cat([g.reshape(-1).float() for g in grads])
         work = self.dist.all_reduce(flat, op=self.dist.ReduceOp.SUM, group=self.group,
                                     async_op=True)
-        self._pending.append((work, flat, grads))
+        entry = (work, flat, grads)
+        self._pending.append(entry)
+        return entry
 
-    def finish(self) -> None:
-        for work, flat, grads in self._pending:
+    def finish(self, entry=None) -> None:
+        """Makes the current stream wait for the bucket(s) and writes the averages
+        back into the gradients: one entry, or every pending one."""
+        entries = list(self._pending) if entry is None else [entry]
+        cur = torch.cuda.current_stream() if torch.cuda.is_available() else None
+        for e in entries:
+            work, flat, grads = e
             work.wait()
+            if cur is not None and flat.is_cuda:
+                flat.record_stream(cur)
             flat.div_(self.world)
             off = 0
             for g in grads:
                 n = g.numel()
                 g.copy_(flat[off:off + n].view_as(g))
                 off += n
-        self._pending.clear()
+            self._pending.remove(e)
 
 
 class StreamedLoraTrainer:
@@ -259,10 +273,10 @@ class StreamedLoraTrainer:
             del out, x
             self._release(i)
             if stepping:
-                grads = [p.grad for ab in self.lora[i].values() for p in ab]
-                if self.full_ft is not None:
-                    grads += self.full_ft.layer_grads(i)
-                self.reducer.launch(grads)
+                self.reducer.launch([p.grad for ab in self.lora[i].values() for p in ab])
+                if self.full_ft is not None and i in self.full_ft.layers:
+                    entry = self.reducer.launch(self.full_ft.layer_grads(i))
+                    self.full_ft.step_layer_async(i, entry, self.reducer)
         if stepping:
             self.reducer.finish()
             if self.opt is not None:
@@ -270,7 +284,7 @@ class StreamedLoraTrainer:
                 self.opt.step()
                 self.opt.zero_grad(set_to_none=False)
             if self.full_ft is not None:
-                self.full_ft.step()
+                self.full_ft.finish()
                 # the selected layers' int8 segments changed: drop stale copies
                 for s in (0, 1):
                     if self.slot_layer[s] in self.full_ft.layers:
