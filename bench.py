@@ -432,14 +432,20 @@ def run_train(args, world, rank, local) -> dict | None:
     long_ft = args.workload == "llama7b_selective_ft_2048"
     moe = args.workload == "mixtral_streamed_lora"
     model = "Llama-2-7B"
+    shard = args.weight_stream == "sharded"
+    if shard and world < 2:
+        raise SystemExit("--weight-stream sharded needs --gpus >= 2")
+    if args.vram_slots is None:
+        args.vram_slots = 3 if shard else 2
     if moe:
         from lema_b200.moe import MixtralShape
         shape = MixtralShape(layers=args.layers)
         model = "Mixtral-8x7B"
-        check_host_ram(shape, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+        check_host_ram(shape, 1 if shard else int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
         batch, seq = 8, 512
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
-                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers)
+                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
+                                 weight_shard=shard, vram_slots=args.vram_slots)
         workload = (f"mixtral_streamed_lora: {shape.layers} x [hidden 4096, 32 q / 8 kv heads "
                     "x 128, 8 experts x SwiGLU 14336, top-2 softmax routing], vocab 32000, LoRA "
                     "r16 a32 on q/v, W8A8 attention projections and grouped W8A8 experts "
@@ -461,7 +467,8 @@ def run_train(args, world, rank, local) -> dict | None:
     else:
         batch, seq = 8, 512
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
-                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers)
+                                 lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
+                                 weight_shard=shard, vram_slots=args.vram_slots)
         workload = (f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 heads, MLP "
                     "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections streamed "
                     "from pinned RAM, activation checkpoints offloaded")
@@ -513,9 +520,9 @@ def run_train(args, world, rank, local) -> dict | None:
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
     h2d_gbs = measure_h2d_gbs(dev)
-    seg_bytes = tr.ws.seg_bytes
+    seg_bytes = tr.ws.chunk  # per rank: the whole segment, or (sharded) its chunk
     streamed = shape.layers - args.resident_layers
-    h2d_per_step = (2 * streamed - min(2, streamed)) * seg_bytes + \
+    h2d_per_step = (2 * streamed - min(tr.nslots, streamed)) * seg_bytes + \
         tr.ckpt.nbytes * shape.layers
     d2h_per_step = tr.ckpt.nbytes * shape.layers
     if tr.full_ft is not None:  # bf16 weight + fp32 m, v in; the same + int8 rows out
@@ -548,6 +555,10 @@ def run_train(args, world, rank, local) -> dict | None:
                    "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}",
                    "resident_layers": args.resident_layers,
+                   "vram_slots": args.vram_slots,
+                   "weight_stream": ("sharded: 1/N of each segment per rank over PCIe, NCCL "
+                                     "all-gather over NVLink" if shard else
+                                     "own: every rank streams its own full segments"),
                    "l2": f"per-step weight stream {h2d_per_step / 1e9:.1f} GB and "
                          "activations >> L2"},
         "gpu_launches": launches,
@@ -661,6 +672,13 @@ def main():
                     choices=["llama7b_streamed_lora", "llama7b_selective_ft_2048",
                              "mixtral_streamed_lora",
                              "w8a8_linear_4096"])
+    ap.add_argument("--weight-stream", choices=["own", "sharded"], default="own",
+                    help="own (default): every rank streams its own segments; sharded: each "
+                         "rank uploads 1/N of every segment and the rest is all-gathered over "
+                         "NVLink (opt-in; adds a weight collective)")
+    ap.add_argument("--vram-slots", type=int, default=None,
+                    help="VRAM slots of the weight stream (uploads run slots-1 layers ahead); "
+                         "default 2 (the reference's double buffering), 3 when sharded")
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)

@@ -98,13 +98,29 @@ class _Seg:
     dtype: torch.dtype
 
 
+def shard_layout(seg_bytes: int, world: int, align: int = 128) -> tuple[int, int]:
+    """(padded segment bytes, bytes per rank) when a segment is split into
+    ``world`` equal, ``align``-aligned chunks for sharded streaming."""
+    chunk = -(-seg_bytes // (world * align)) * align
+    return chunk * world, chunk
+
+
 class WeightSegments:
-    """All blocks' int8 segments in pinned RAM + two VRAM slots fed by the native
-    manager's H2D copy stream."""
+    """All blocks' int8 segments in pinned RAM + ``num_slots`` (default two) VRAM
+    slots fed by the native manager's H2D copy stream.
+
+    Sharded streaming (``shard_group`` given, opt-in): rank r of W keeps only
+    chunk r of every (padded) segment in pinned RAM and uploads it into its
+    place in the slot; an in-place NCCL all-gather over NVLink, issued on a side
+    stream behind the upload, fills in the other W-1 chunks. Each rank then moves
+    1/W of the segment bytes over PCIe (the host's memory and PCIe root are
+    shared by the ranks) and ~(W-1)/W of them over NVLink. The default is the
+    unsharded form: every rank streams its own full copy of each segment."""
 
     ALIGN = 128
 
-    def __init__(self, shape: LlamaShape, num_blocks: int, device: torch.device):
+    def __init__(self, shape: LlamaShape, num_blocks: int, device: torch.device,
+                 shard_group=None, num_slots: int = 2):
         from .moe import MixtralBlock, MixtralShape
         self.moe = isinstance(shape, MixtralShape)
         block_cls = MixtralBlock if self.moe else LlamaBlock
@@ -145,22 +161,41 @@ class WeightSegments:
         add("input_layernorm", (shape.hidden,), torch.bfloat16)
         add("post_attention_layernorm", (shape.hidden,), torch.bfloat16)
         self.seg_bytes = off
-        self.ram = torch.empty(num_blocks, self.seg_bytes, dtype=torch.uint8, pin_memory=True)
-        self.vram = [torch.empty(self.seg_bytes, dtype=torch.uint8, device=self.device)
-                     for _ in range(2)]
+        self.group = shard_group
+        if shard_group is not None:
+            import torch.distributed as dist
+            self._dist = dist
+            self.rank = dist.get_rank(shard_group)
+            self.world = dist.get_world_size(shard_group)
+            self.slot_bytes, self.chunk = shard_layout(self.seg_bytes, self.world, self.ALIGN)
+            self.gather_stream = torch.cuda.Stream(self.device)
+        else:
+            self.rank, self.world = 0, 1
+            self.slot_bytes = self.chunk = self.seg_bytes
+        # pinned RAM: every block's full segment, or this rank's chunk of it
+        self.ram = torch.empty(num_blocks, self.chunk, dtype=torch.uint8, pin_memory=True)
+        self.num_slots = max(2, int(num_slots))
+        self.vram = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
+                     for _ in range(self.num_slots)]
+        self._staging: torch.Tensor | None = None
         self.mm = C.c_void_p()
         dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        N.call("lema_mm_create", num_blocks + 2, self.seg_bytes, dev_index, C.byref(self.mm))
+        N.call("lema_mm_create", num_blocks + 2, self.chunk, dev_index, C.byref(self.mm))
         for b in range(num_blocks):
             N.call("lema_mm_register_ram_buffer", self.mm, b, self.ram[b].data_ptr(),
-                   self.seg_bytes)
-        for s in range(2):
-            N.call("lema_mm_register_vram_slot", self.mm, s, self.vram[s].data_ptr(),
-                   self.seg_bytes)
+                   self.chunk)
+        for s in range(self.num_slots):  # the upload lands at this rank's chunk of the slot
+            N.call("lema_mm_register_vram_slot", self.mm, s,
+                   self.vram[s].data_ptr() + self.rank * self.chunk, self.chunk)
         sp = C.c_void_p()
         N.call("lema_mm_copy_stream", self.mm, C.byref(sp))
         self.h2d_stream = torch.cuda.ExternalStream(sp.value, device=self.device)
         self._pending: dict[int, int] = {}
+        self._gathers: dict[int, object] = {}
+
+    @property
+    def sharded(self) -> bool:
+        return self.group is not None
 
     def close(self) -> None:
         if self.mm:
@@ -182,24 +217,58 @@ class WeightSegments:
         raw = buf[seg.offset: seg.offset + seg.nbytes]
         return raw.view(seg.dtype).view(seg.shape)
 
-    def pack_block(self, b: int, tensors: dict[str, torch.Tensor]) -> None:
-        """Writes one block's quantised tensors (device or host) into RAM segment b."""
-        ram = self.ram[b]
+    def staging(self, b: int) -> torch.Tensor:
+        """A full-segment buffer to write block b into: the pinned segment itself,
+        or (sharded) a device buffer whose chunk ``commit`` keeps."""
+        if not self.sharded:
+            return self.ram[b]
+        if self._staging is None:
+            self._staging = torch.zeros(self.slot_bytes, dtype=torch.uint8, device=self.device)
+        return self._staging
+
+    def commit(self, b: int) -> None:
+        """Sharded: copies this rank's chunk of the staging buffer into RAM."""
+        if self.sharded:
+            c0 = self.rank * self.chunk
+            self.ram[b].copy_(self._staging[c0:c0 + self.chunk])
+
+    def pack_block(self, b: int, tensors: dict[str, torch.Tensor], commit: bool = True) -> None:
+        """Writes one block's quantised tensors (device or host) into its segment."""
+        buf = self.staging(b)
         for name, t in tensors.items():
-            v = self._view(ram, name)
+            v = self._view(buf, name)
             v.copy_(t.detach().reshape(v.shape))
+        if commit:
+            self.commit(b)
 
     # ---- streaming -----------------------------------------------------------
     def upload(self, b: int, slot: int) -> None:
-        """Starts the H2D of block b's segment into VRAM slot ``slot`` (the copy
-        stream first waits until compute released that slot)."""
+        """Starts the H2D of block b's segment (or this rank's chunk of it) into
+        VRAM slot ``slot`` (the copy stream first waits until compute released
+        that slot); sharded, the slot's all-gather follows on the gather stream."""
         ev = C.c_int64(-1)
         N.call("lema_mm_async_transfer_to_vram", self.mm, b, slot, 0, C.byref(ev))
-        self._pending[slot] = ev.value
+        if not self.sharded:
+            self._pending[slot] = ev.value
+            return
+        gs = self.gather_stream
+        N.call("lema_mm_stream_wait_transfer", self.mm, ev.value, gs.cuda_stream)
+        with torch.cuda.stream(gs):
+            full = self.vram[slot]
+            mine = full[self.rank * self.chunk:(self.rank + 1) * self.chunk]
+            self._gathers[slot] = self._dist.all_gather_into_tensor(full, mine, group=self.group,
+                                                                    async_op=True)
 
     def acquire(self, slot: int, stream: torch.cuda.Stream | None = None) -> None:
-        """Makes the compute stream wait (on the device) for slot's upload."""
+        """Makes the compute stream wait (on the device) for slot's upload (and,
+        sharded, its all-gather)."""
         s = stream or torch.cuda.current_stream(self.device)
+        if self.sharded:
+            work = self._gathers.pop(slot, None)
+            if work is not None:
+                with torch.cuda.stream(s):
+                    work.wait()
+            return
         ev = self._pending.pop(slot, -1)
         if ev >= 0:
             N.call("lema_mm_stream_wait_transfer", self.mm, ev, s.cuda_stream)

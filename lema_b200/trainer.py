@@ -94,7 +94,7 @@ class StreamedLoraTrainer:
                  gradient_checkpointing: bool = False, attn_chunk: int = 0,
                  full_ft_layers: tuple[int, ...] = (),
                  full_ft_modules: tuple[str, ...] = ("q_proj", "k_proj", "v_proj", "o_proj"),
-                 group=None):
+                 group=None, weight_shard: bool = False, vram_slots: int = 2):
         self.shape = shape
         self.device = torch.device(device)
         self.batch, self.seq = batch, seq
@@ -116,7 +116,20 @@ class StreamedLoraTrainer:
         from .moe import MixtralBlock, MixtralShape
         moe = isinstance(shape, MixtralShape)
         block_cls = MixtralBlock if moe else LlamaBlock
-        self.ws = WeightSegments(shape, self.L, dev)
+        shard_group = None
+        if weight_shard:
+            # opt-in: each rank uploads 1/world of every segment, NCCL all-gathers
+            # the rest over NVLink (beyond the gradient-all-reduce-only default)
+            import torch.distributed as dist
+            if not dist.is_initialized() or dist.get_world_size(group) < 2:
+                raise ValueError("weight_shard needs an initialised process group of >= 2 ranks")
+            if full_ft_layers or resident_layers:
+                raise ValueError("weight_shard streams every layer and keeps no full segment "
+                                 "in RAM: no resident layers, no selective full fine-tuning")
+            shard_group = group if group is not None else dist.group.WORLD
+        self.ws = WeightSegments(shape, self.L, dev, shard_group=shard_group,
+                                 num_slots=vram_slots)
+        self.nslots = self.ws.num_slots
         true_weights = {}
         for b in range(self.L):
             tensors = {}
@@ -132,12 +145,14 @@ class StreamedLoraTrainer:
             ones = torch.ones(shape.hidden, device=dev, dtype=torch.bfloat16)
             tensors["input_layernorm"] = ones
             tensors["post_attention_layernorm"] = ones
-            self.ws.pack_block(b, tensors)
+            self.ws.pack_block(b, tensors, commit=False)
             if moe:
                 self._pack_experts(b, g)
+            self.ws.commit(b)
         torch.cuda.synchronize(dev)
         # optional HBM-resident copies of the first `resident_layers` segments
         self.resident = [self.ws.ram[b].to(dev) for b in range(min(resident_layers, self.L))]
+        self.weight_shard = weight_shard
         # two block modules, bound per layer (the reference's module pool)
         self.blocks = [block_cls(shape, quantized=True, device=dev) for _ in range(2)]
         for blk in self.blocks:
@@ -172,7 +187,7 @@ class StreamedLoraTrainer:
                                               mode=ckpt_mode, h2d_stream=self.ws.h2d_stream)
         self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
         self.reducer = LoraGradReducer(group)
-        self.slot_layer = [-1, -1]
+        self.slot_layer = [-1] * self.nslots
         self.grad_accum = max(1, int(grad_accum))
         self.micro_step = 0
         self.global_step = 0
@@ -185,7 +200,7 @@ class StreamedLoraTrainer:
         router drawn N(0, 1/hidden) so that its logits on RMS-normalised inputs are
         ~N(0, 1)."""
         sh, dev, ws = self.shape, self.device, self.ws
-        ram = ws.ram[b]
+        ram = ws.staging(b)
         for e in range(sh.experts):
             for name, (o, i) in (("gate_up", (2 * sh.intermediate, sh.hidden)),
                                  ("down", (sh.hidden, sh.intermediate))):
@@ -200,15 +215,15 @@ class StreamedLoraTrainer:
 
     def _ensure(self, layer: int) -> None:
         """Starts the upload of ``layer`` into its slot unless it is already there."""
-        slot = layer % 2
+        slot = layer % self.nslots
         if layer < len(self.resident) or self.slot_layer[slot] == layer:
             return
         self.ws.upload(layer, slot)
         self.slot_layer[slot] = layer
 
     def _bind(self, layer: int) -> LlamaBlock:
-        slot = layer % 2
-        blk = self.blocks[slot]
+        slot = layer % self.nslots
+        blk = self.blocks[layer % 2]
         if layer < len(self.resident):
             self._bind_resident(blk, layer)
         else:
@@ -227,7 +242,7 @@ class StreamedLoraTrainer:
 
     def _release(self, layer: int) -> None:
         if layer >= len(self.resident):
-            self.ws.release(layer % 2)
+            self.ws.release(layer % self.nslots)
 
     # ---- one step ------------------------------------------------------------
     def train_step(self, ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
@@ -238,12 +253,14 @@ class StreamedLoraTrainer:
         labels = ids if labels is None else labels.to(dev, non_blocking=True)
         L = self.L
         # forward (no grad), saving each block's input to pinned host
+        ahead = self.nslots - 1  # uploads run this many layers ahead of compute
         with torch.no_grad():
             h = self.embed(ids)
-            self._ensure(0)
+            for k in range(min(ahead, L)):
+                self._ensure(k)
             for i in range(L):
-                if i + 1 < L:
-                    self._ensure(i + 1)
+                if i + ahead < L:
+                    self._ensure(i + ahead)
                 blk = self._bind(i)
                 self.ckpt.save(i, h)
                 h = blk(h, self.cos, self.sin)
@@ -261,9 +278,13 @@ class StreamedLoraTrainer:
         del logits, h
         # backward in reverse: restore, re-forward with grad, backward
         self.ckpt.restore_async(L - 1)
+        for k in range(1, ahead):
+            if L - 1 - k >= 0:
+                self._ensure(L - 1 - k)
         for i in range(L - 1, -1, -1):
+            if i - ahead >= 0:
+                self._ensure(i - ahead)
             if i - 1 >= 0:
-                self._ensure(i - 1)
                 self.ckpt.restore_async(i - 1)
             blk = self._bind(i)
             x = self.ckpt.wait(i).requires_grad_(True)
@@ -286,7 +307,7 @@ class StreamedLoraTrainer:
             if self.full_ft is not None:
                 self.full_ft.finish()
                 # the selected layers' int8 segments changed: drop stale copies
-                for s in (0, 1):
+                for s in range(self.nslots):
                     if self.slot_layer[s] in self.full_ft.layers:
                         self.slot_layer[s] = -1
                 for b in self.full_ft.layers:

@@ -149,3 +149,12 @@ def test_missing_rank_fails_fast_on_the_host(tmp_path):
                        start_method="spawn")
     assert (tmp_path / "lonely.txt").read_text().startswith("error")
     assert time.time() - t0 < 60
+
+
+def test_shard_layout_covers_the_segment():
+    from lema_b200.tensorstore import shard_layout
+    for seg in (1, 127, 128, 202_375_168 + 65_536, 1_451_229_312):
+        for world in (1, 2, 3, 4, 8):
+            padded, chunk = shard_layout(seg, world)
+            assert chunk % 128 == 0 and padded == chunk * world
+            assert padded >= seg and padded - seg < world * 128

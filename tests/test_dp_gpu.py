@@ -43,3 +43,21 @@ def test_two_rank_step_equals_accumulation(cuda_device, tmp_path):
         mismatched += int((d > 2e-4).sum())
     tr.close()
     assert mismatched <= 0.01 * total, (mismatched, total)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_weight_stream_equals_own_segments(cuda_device, tmp_path):
+    """Sharded streaming (half of every segment over each rank's PCIe link, the
+    other half all-gathered over NVLink) gives the same 2-rank steps, bit for
+    bit, as every rank streaming its own segments — dense and MoE blocks."""
+    out = tmp_path / "shard.pt"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29563",
+           os.path.join(HERE, "shard_gpu_worker.py"), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    rep = torch.load(out)
+    for name, v in rep.items():
+        assert v["same"], (name, v)
+        assert v["chunk_bytes"] * 2 >= v["segment_bytes"] > v["chunk_bytes"], (name, v)

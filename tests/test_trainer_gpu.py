@@ -175,3 +175,21 @@ def test_fused_step_close_to_unfused_step(cuda_device):
     for a, b in zip(g0, g1):
         rms = b.pow(2).mean().sqrt().item() + 1e-30
         assert (a - b).pow(2).mean().sqrt().item() / rms <= 5e-2
+
+
+def test_more_vram_slots_give_the_same_step(cuda_device):
+    """Three or four slots (uploads running two or three layers ahead) stream the
+    same bytes into the same kernels as two: identical LoRA parameters."""
+    ids = _ids(23, 2, 64, SMALL.vocab, cuda_device)
+    out = []
+    for slots in (2, 3, 4):
+        tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=1e-3, seed=12,
+                                 vram_slots=slots)
+        with sdpa_kernel(SDPBackend.MATH):
+            losses = [float(tr.train_step(ids)) for _ in range(2)]
+        out.append((losses, [p.detach().clone() for p in tr.params]))
+        tr.close()
+    for losses, params in out[1:]:
+        assert losses == out[0][0]
+        for a, b in zip(params, out[0][1]):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
