@@ -498,6 +498,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the set-up above overlaps the previous kernel's tail (programmatic launch);
+  // operands, scales and the split workspace are read only after this
+  ptx::griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -707,6 +710,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::cluster_sync();  // barriers of both CTAs initialised before any remote use
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the set-up above overlaps the previous kernel's tail (programmatic launch);
+  // operands, scales and the split workspace are read only after this
+  ptx::griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -921,8 +927,17 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
     attr_done[dev] = true;
   }
-  kern<<<workers, kThreads, L::kTotal, stream>>>(ma, mb, my, p);
-  LEMA_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(workers);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, p));
   return LEMA_OK;
 }
 
@@ -967,17 +982,19 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   using L = SmemLayout<128, kPairStages>;
   auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * workers);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, p));
   return LEMA_OK;
 }

@@ -127,6 +127,17 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+// ---- programmatic dependent launch --------------------------------------
+
+// Waits until the grids this one depends on (the previous kernel on the stream,
+// when this grid was launched with programmatic stream serialisation) have
+// completed and their memory is visible. Without that launch attribute it
+// returns at once. Every kernel launched with the attribute calls it before
+// reading anything an earlier kernel wrote.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- clusters (CTA pairs for cta_group::2) --------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
