@@ -1,23 +1,30 @@
 // gemm_sm100.cu — K2/K3 (int8 tcgen05 GEMM + fused dequant/bias/bf16 epilogue),
 // the bf16 tcgen05 GEMM used by K4 (dgrad), and K6 (grouped int8 GEMM for MoE
-// experts). One persistent, warp-specialised kernel template serves all three:
+// experts). Two persistent, warp-specialised kernel templates serve all three:
+// a 1-SM kernel (128 x BN tiles) and a CTA-pair kernel (cluster of 2, 256 x 256
+// tiles, cta_group::2 MMAs), with the same roles:
 //
 //   warp 0      TMA producer: one thread streams 128-byte-wide K slices of the
 //               A tile (128 rows) and B tile (BN rows) into a STAGES-deep ring
 //               of 128B-swizzled shared-memory buffers (plain TMA, no multicast).
 //   warp 1      allocates TMEM (2 x BN columns: double-buffered accumulators);
-//               one thread issues tcgen05.mma (M=128, N=BN, K=32 bytes per
-//               instruction) and tcgen05.commit to free smem stages / publish
-//               finished accumulators.
+//               one thread issues tcgen05.mma (K=32 bytes per instruction) and
+//               tcgen05.commit to free smem stages / publish finished
+//               accumulators.
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, then
 //               y = bf16((float(acc) * sx[m]) * sw[n] + bias[n]) (int8 kind) or
-//               y = bf16(acc) (bf16 kind), stored straight to global memory,
-//               while the MMA warp already accumulates the next tile into the
-//               other TMEM buffer.
+//               y = bf16(acc) (bf16 kind), staged in 64-byte-swizzled shared
+//               memory and written by TMA stores (direct stores for raw
+//               accumulator outputs and unaligned y), while the MMA warp already
+//               accumulates the next tile into the other TMEM buffer.
 //
 // Tiles are ordered m-fastest inside each group so concurrently running CTAs
 // share the B (weight) tile through L2. A "group" is a contiguous row range of
 // A that multiplies its own B matrix (MoE experts); the dense GEMM is one group.
+// When the last wave would fill at most half of the workers, its tiles are cut
+// into two K-halves (plan_split, WorkIter). Kernels are launched with
+// programmatic stream serialisation: their set-up overlaps the previous
+// kernel's tail and griddepcontrol.wait precedes every data read.
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
