@@ -318,7 +318,7 @@ def run_linear(args, world, rank, local) -> dict | None:
                 "path": "lema_b200.ops.w8a8_linear with pinned host x / y"},
     }
     if not args.skip_cpu:
-        threads = os.cpu_count() or 1
+        threads = len(os.sched_getaffinity(0))
         c = cpu_linear_sample(M, N, K, rows=args.cpu_rows, reps=3, threads=threads)
         res["cpu_baseline"] = {"value": round(c["tops"], 4), "unit": "TOPS", "cores": threads,
                                "kind": "port", "sample": c["sample"]}
@@ -428,6 +428,11 @@ def run_train(args, world, rank, local) -> dict | None:
     from lema_b200.trainer import StreamedLoraTrainer
 
     dev = torch.device("cuda", local)
+    # run next to the GPU before pinning gigabytes of host memory (restored for the
+    # CPU baseline, which uses every host thread)
+    from lema_b200.topology import bind_to_gpu_cpus
+    all_cpus = os.sched_getaffinity(0)
+    local_cpus = bind_to_gpu_cpus(dev)
     shape = LlamaShape(layers=args.layers)
     long_ft = args.workload == "llama7b_selective_ft_2048"
     moe = args.workload == "mixtral_streamed_lora"
@@ -584,8 +589,11 @@ def run_train(args, world, rank, local) -> dict | None:
                 "h2d_bytes_per_step": batch * seq * 8, "d2h_bytes_per_step": 4,
                 "path": "StreamedLoraTrainer.train_step(ids in pinned host memory) + loss.item()"},
     }
+    res["config"]["host_cpus"] = (f"{len(local_cpus)} GPU-local CPUs" if local_cpus
+                                  else "unbound")
     if not args.skip_cpu:
-        threads = os.cpu_count() or 1
+        os.sched_setaffinity(0, all_cpus)
+        threads = len(all_cpus)
         c = cpu_train_sample(args.cpu_seq, threads, moe=moe)
         res["cpu_baseline"] = {"value": round(c["tokens_per_s"], 3), "unit": "tokens/s",
                                "cores": threads, "kind": "port", "sample": c["sample"]}
@@ -618,7 +626,7 @@ def run_reference(args) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.workload in ("llama7b_streamed_lora", "llama7b_selective_ft_2048",
                          "mixtral_streamed_lora"):
