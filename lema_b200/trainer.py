@@ -94,7 +94,8 @@ class StreamedLoraTrainer:
                  gradient_checkpointing: bool = False, attn_chunk: int = 0,
                  full_ft_layers: tuple[int, ...] = (),
                  full_ft_modules: tuple[str, ...] = ("q_proj", "k_proj", "v_proj", "o_proj"),
-                 group=None, weight_shard: bool = False, vram_slots: int = 2):
+                 group=None, weight_shard: bool = False, vram_slots: int = 2,
+                 weights: str | None = None):
         self.shape = shape
         self.device = torch.device(device)
         self.batch, self.seq = batch, seq
@@ -131,7 +132,10 @@ class StreamedLoraTrainer:
                                  num_slots=vram_slots)
         self.nslots = self.ws.num_slots
         true_weights = {}
-        for b in range(self.L):
+        if weights is not None:
+            self._load_weights(weights, block_cls, full_ft_layers, full_ft_modules,
+                               true_weights)
+        for b in range(self.L if weights is None else 0):
             tensors = {}
             for name in block_cls.FUSABLE:
                 o, i = shape.proj_shapes()[name]
@@ -193,6 +197,39 @@ class StreamedLoraTrainer:
         self.global_step = 0
 
     # ---- weights -----------------------------------------------------------
+    @torch.no_grad()
+    def _load_weights(self, path: str, block_cls, full_ft_layers, full_ft_modules,
+                      true_weights: dict) -> None:
+        """Fills the segments, embedding and head from a checkpoint: an int8
+        segment file (straight copy) or a Hugging Face safetensors checkpoint
+        (quantised block by block on the device)."""
+        from . import checkpoint as ckp
+        dev = self.device
+        if ckp.is_segment_file(path):
+            if full_ft_layers:
+                raise ValueError("selective full fine-tuning needs the bf16 weights: load a "
+                                 "Hugging Face checkpoint, not an int8 segment file")
+            ck = ckp.load_segments(path, self.ws)
+        else:
+            ck = ckp.HFCheckpoint(path)
+            for b in range(self.L):
+                keep = tuple(full_ft_modules) if b in full_ft_layers else ()
+                kept = ckp.pack_block_from_hf(self.ws, b, ck, block_cls.FUSABLE, dev, keep)
+                for name, w in kept.items():
+                    true_weights[(b, name)] = w
+        self.embed.weight.copy_(ck.get("model.embed_tokens.weight").to(dev, torch.bfloat16))
+        self.head.norm.weight.copy_(ck.get("model.norm.weight").to(dev, torch.bfloat16))
+        lm = "lm_head.weight" if "lm_head.weight" in ck else "model.embed_tokens.weight"
+        self.head.lm_head.weight.copy_(ck.get(lm).to(dev, torch.bfloat16))
+
+    def save_segments(self, path: str) -> None:
+        """Writes the quantised segments, embedding and head as an int8 segment
+        file that ``weights=path`` loads without re-quantising."""
+        from . import checkpoint as ckp
+        torch.cuda.synchronize(self.device)
+        ckp.save_segments(path, self.ws, self.embed.weight, self.head.norm.weight,
+                          self.head.lm_head.weight)
+
     @torch.no_grad()
     def _pack_experts(self, b: int, g: torch.Generator) -> None:
         """Random-init experts of a MoE block (N(0, 0.02), as HF initialises
