@@ -61,3 +61,39 @@ def test_sharded_weight_stream_equals_own_segments(cuda_device, tmp_path):
     for name, v in rep.items():
         assert v["same"], (name, v)
         assert v["chunk_bytes"] * 2 >= v["segment_bytes"] > v["chunk_bytes"], (name, v)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_full_ft_step_equals_accumulation(cuda_device, tmp_path):
+    """Selective full fine-tuning under data parallelism (each selected layer's
+    accumulators all-reduced as their own bucket, then clipped and stepped on the
+    side stream) moves the true weights as one rank accumulating both
+    micro-batches does."""
+    out = tmp_path / "dpft.pt"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29565",
+           os.path.join(HERE, "dp_ft_gpu_worker.py"), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    dp = torch.load(out)
+    sys.path.insert(0, HERE)
+    from dp_ft_gpu_worker import FT_LAYERS
+    from dp_gpu_worker import SMALL, micro_batch
+    from lema_b200.trainer import StreamedLoraTrainer
+    tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, targets=(), lr=1e-3,
+                             seed=31, full_ft_layers=FT_LAYERS, grad_accum=2)
+    with sdpa_kernel(SDPBackend.MATH):
+        tr.train_step(micro_batch(0, cuda_device))
+        tr.train_step(micro_batch(1, cuda_device))
+    total = moved = mismatched = 0
+    for key, w in tr.full_ft.true.items():
+        a, b = dp[key].float(), w.float()
+        total += a.numel()
+        mismatched += int(((a - b).abs() > 1e-6 + 2 ** -7 * b.abs()).sum())
+        moved += int((a != 0).sum())
+    tr.close()
+    assert moved > 0
+    # the first AdamW step moves each weight by about lr * sign(grad): a few
+    # elements whose gradient is ~0 may go the other way
+    assert mismatched <= 0.01 * total, (mismatched, total)
