@@ -1030,6 +1030,7 @@ struct SplitWorkspace {
 
 std::mutex g_ws_mu;
 std::map<std::pair<int, cudaStream_t>, SplitWorkspace> g_ws;
+constexpr size_t kMaxSplitWorkspaces = 8;  // (device, stream) pairs, 19 MB each on B200
 
 // Partial slots for every CTA of a full grid (one per SM: 128 KB each) and
 // their publish flags, allocated once per (device, stream) so that GEMMs on
@@ -1046,6 +1047,8 @@ bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags) {
   if (cap != cudaStreamCaptureStatusNone) return false;
   const int dev = current_device();
   std::lock_guard<std::mutex> lock(g_ws_mu);
+  if (g_ws.size() >= kMaxSplitWorkspaces && g_ws.find({dev, stream}) == g_ws.end())
+    return false;  // bounded: GEMMs on further streams run whole tiles
   SplitWorkspace& w = g_ws[{dev, stream}];
   if (w.failed) return false;
   if (w.slots == nullptr) {

@@ -226,6 +226,10 @@ class WeightSegments:
             self._staging = torch.zeros(self.slot_bytes, dtype=torch.uint8, device=self.device)
         return self._staging
 
+    def drop_staging(self) -> None:
+        """Frees the device staging buffer once every block is packed."""
+        self._staging = None
+
     def commit(self, b: int) -> None:
         """Sharded: copies this rank's chunk of the staging buffer into RAM."""
         if self.sharded:

@@ -154,6 +154,7 @@ class StreamedLoraTrainer:
                 self._pack_experts(b, g)
             self.ws.commit(b)
         torch.cuda.synchronize(dev)
+        self.ws.drop_staging()
         # optional HBM-resident copies of the first `resident_layers` segments
         self.resident = [self.ws.ram[b].to(dev) for b in range(min(resident_layers, self.L))]
         self.weight_shard = weight_shard
