@@ -442,6 +442,8 @@ def run_train(args, world, rank, local) -> dict | None:
         raise SystemExit("--weight-stream sharded needs --gpus >= 2")
     if args.vram_slots is None:
         args.vram_slots = 3 if shard else 2
+    from lema_b200 import ops
+    ops.set_dgrad_mode(args.dgrad)
     if moe:
         from lema_b200.moe import MixtralShape
         shape = MixtralShape(layers=args.layers)
@@ -561,6 +563,7 @@ def run_train(args, world, rank, local) -> dict | None:
                    "parallelism": f"dp{world}",
                    "resident_layers": args.resident_layers,
                    "vram_slots": args.vram_slots,
+                   "dgrad": args.dgrad,
                    "weight_stream": ("sharded: 1/N of each segment per rank over PCIe, NCCL "
                                      "all-gather over NVLink" if shard else
                                      "own: every rank streams its own full segments"),
@@ -689,6 +692,9 @@ def main():
     ap.add_argument("--vram-slots", type=int, default=None,
                     help="VRAM slots of the weight stream (uploads run slots-1 layers ahead); "
                          "default 2 (the reference's double buffering), 3 when sharded")
+    ap.add_argument("--dgrad", choices=["bf16", "int8"], default="bf16",
+                    help="straight-through dgrad of the frozen projections: bf16 (the "
+                         "operator contract, default) or the opt-in int8-dy variant")
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)

@@ -86,7 +86,7 @@ LEMA_API int lema_quantize_per_token(const void* x_bf16, int64_t M, int64_t K, i
 
 /* ---- K2+K3: int8 tcgen05 GEMM with fused dequant/bias/bf16 epilogue ----- */
 /* y[M,N] (bf16, row stride ldy) from xq[M,K] (ld ldx), wq[N,K] (ld ldw),
- * sx[M], sw[N], bias[N] (bf16, may be NULL = zero). acc_dbg (may be NULL)
+ * sx[M], sw[N] (may be NULL = all ones), bias[N] (bf16, may be NULL = zero). acc_dbg (may be NULL)
  * receives the raw s32 accumulators [M,N] (row stride ldacc) for bit-exact
  * checks; y may be NULL when only acc_dbg is wanted.
  * Constraints: ldx % 16 == 0, ldw % 16 == 0, xq/wq 16-byte aligned,
@@ -151,6 +151,28 @@ LEMA_API int lema_w8a8_dgrad(const void* dy_bf16, int64_t lddy,
                     const int8_t* wq, int64_t ldw, const float* sw,
                     void* dx_bf16, int64_t lddx, void* wdT_ws, int64_t ldt,
                     int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Per-row int8 quantisation of x[r,c] * cs[c] (bf16 x, fp32 column scales cs,
+ * the product rounded to fp32), same contract as lema_quantize_rows on the
+ * products: the activation side of the int8-dy backward. */
+LEMA_API int lema_quantize_rows_colscaled(const void* x_bf16, const float* cs, int64_t rows,
+                                          int64_t cols, int64_t ldx, int8_t* q, int64_t ldq,
+                                          float* scale, void* stream);
+
+/* wqT[k,n] = wq[n,k] (int8 transpose; ldt >= N, ldt % 16 == 0). */
+LEMA_API int lema_transpose_i8(const int8_t* wq, int64_t ldw, int64_t N, int64_t K,
+                               int8_t* wqT, int64_t ldt, void* stream);
+
+/* The int8-dy variant of the straight-through dgrad (opt-in; it has no
+ * counterpart in the reference and a looser tolerance than lema_w8a8_dgrad):
+ * dq, sd = quantise_rows(dy * sw), wqT = wq^T, dx = bf16(sd[m] * (dq . wqT^T)),
+ * i.e. dx ~ dy . (wq * sw) with dy carried as int8 per row. Workspaces:
+ * wqT_ws int8 [K, ldt] (ldt >= N, multiple of 16), dq_ws int8 [M, ldq]
+ * (ldq >= N, multiple of 16), sd_ws fp32 [M]. */
+LEMA_API int lema_w8a8_dgrad_int8(const void* dy_bf16, int64_t lddy, const int8_t* wq,
+                                  int64_t ldw, const float* sw, void* dx_bf16, int64_t lddx,
+                                  int8_t* wqT_ws, int64_t ldt, int8_t* dq_ws, int64_t ldq,
+                                  float* sd_ws, int64_t M, int64_t N, int64_t K, void* stream);
 
 /* ---- Fused producers of the W8A8 GEMM inputs (and their backward) ------ */
 /* RMSNorm of HF LlamaRMSNorm as adapters/_llama.py:238,248 apply it, in bf16:

@@ -38,6 +38,10 @@ _SIGNATURES: dict[str, list] = {
     "lema_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp],
     "lema_bf16_gemm_tn_f32": [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp],
     "lema_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i64, i64, vp],
+    "lema_quantize_rows_colscaled": [vp, vp, i64, i64, i64, vp, i64, vp, vp],
+    "lema_transpose_i8": [vp, i64, i64, i64, vp, i64, vp],
+    "lema_w8a8_dgrad_int8": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, i64, i64,
+                             vp],
     "lema_grouped_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, i64, i64, vp],
@@ -124,6 +128,7 @@ KERNELS_PER_CALL = {
     "lema_w8a8_gemm": 1, "lema_w8a8_linear_fwd": 2, "lema_w8a8_linear_fwd_noalloc": 2,
     "lema_dequant_transpose": 1, "lema_bf16_gemm_tn": 1, "lema_bf16_gemm_tn_f32": 1,
     "lema_w8a8_dgrad": 2, "lema_grouped_w8a8_gemm": 1, "lema_grouped_bf16_gemm_tn": 1,
+    "lema_quantize_rows_colscaled": 1, "lema_transpose_i8": 1, "lema_w8a8_dgrad_int8": 3,
     "lema_grouped_w8a8_dgrad": 2, "lema_rmsnorm_quant": 1, "lema_rmsnorm_bwd": 1,
     "lema_rope": 1, "lema_rope_qkv": 1, "lema_swiglu_quant": 1, "lema_swiglu_bwd": 1,
 }

@@ -231,7 +231,9 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
                                               const int32_t* part, int32_t* slot) {
   float sxr = 0.f;
   if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
-  const float* swg = (KIND == kKindI8) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
+  // no column scales (sw null): every column scale is 1
+  const float* swg =
+      (KIND == kKindI8 && p.sw != nullptr) ? p.sw + static_cast<int64_t>(g) * p.n : nullptr;
   const __nv_bfloat16* bg = p.bias != nullptr ? p.bias + static_cast<int64_t>(g) * p.n : nullptr;
 #pragma unroll 1
   for (int c = 0; c < NCHUNK; ++c) {
@@ -266,14 +268,14 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
-                              __ldg(swg + n + j));
+                              swg != nullptr ? __ldg(swg + n + j) : 1.f);
           if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
           out[j] = __float2bfloat16_rn(f);
         }
       } else {
         for (int j = 0; j < 32 && n + j < p.n; ++j) {
           float f = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sxr),
-                              swg[n + j]);
+                              swg != nullptr ? swg[n + j] : 1.f);
           if (bg != nullptr) f = __fadd_rn(f, __bfloat162float(bg[n + j]));
           out[j] = __float2bfloat16_rn(f);
         }
@@ -322,7 +324,8 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
     const int c = lane * 8 + j;
     const int n = n0 + c;
     const bool in = n < p.n && c < NCHUNK * 32;
-    if (KIND == kKindI8) sw_s[c] = in ? __ldg(p.sw + static_cast<int64_t>(g) * p.n + n) : 0.f;
+    if (KIND == kKindI8)
+      sw_s[c] = !in ? 0.f : p.sw != nullptr ? __ldg(p.sw + static_cast<int64_t>(g) * p.n + n) : 1.f;
     if (has_bias)
       bias_s[c] = in ? p.bias[static_cast<int64_t>(g) * p.n + n] : __float2bfloat16_rn(0.f);
   }
@@ -1132,8 +1135,8 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   if (a == nullptr || b == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null operand");
   if (y == nullptr && acc == nullptr)
     return set_error(LEMA_ERR_INVALID_ARGUMENT, "no output (y and acc_dbg both null)");
-  if (kind == kKindI8 && (sx == nullptr || sw == nullptr))
-    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null scale pointer");
+  if (kind == kKindI8 && sx == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null row scale pointer");
   if (rows > INT32_MAX || n > INT32_MAX || k > INT32_MAX ||
       n * static_cast<int64_t>(groups.num) > INT32_MAX)
     return set_error(LEMA_ERR_UNSUPPORTED, "dimension exceeds int32");

@@ -1,7 +1,9 @@
 // quantize.cu — K1: per-row dynamic symmetric int8 quantisation (per token for
 // activations, per output channel for weights), the int8 -> bf16 dequant +
 // transpose that feeds the dgrad GEMM, and the C-ABI front ends that chain
-// K1 -> K2/K3 (forward) and dequant -> bf16 GEMM (dgrad).
+// K1 -> K2/K3 (forward) and dequant -> bf16 GEMM (dgrad). The opt-in int8-dy
+// dgrad chains a column-scaled quantiser (rows of dy * sw), an int8 transpose
+// of wq and the int8 GEMM with unit column scales.
 //
 // K1 is HBM-bound: one CTA of 128 threads owns one row, reads it once with
 // 128-bit loads into registers (up to 16 vectors per thread = 16384 bf16),
@@ -125,6 +127,115 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __re
           qr + static_cast<int64_t>(idx) * E) = Vec<T>::quant(v[i], s, inv_s);
   }
   if (threadIdx.x == 0) scale[row] = s;
+}
+
+// Rows of x[r, c] * cs[c] (bf16 x, fp32 column scales; each product rounded to
+// fp32) quantised by the contract: the row is held as bf16 vectors and the
+// products are formed twice (for |max| and for the quantiser), the scales read
+// through L1.
+template <int VPT>
+__global__ void __launch_bounds__(kQThreads) quant_rows_colscaled_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ cs, int cols,
+    int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  const float4* cs4 = reinterpret_cast<const float4*>(cs);
+  const int nvec = cols / 8;
+  uint4 v[VPT];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kQThreads;
+    if (idx < nvec) {
+      v[i] = ld_stream(xr + idx);
+      const float4 c0 = __ldg(cs4 + 2 * idx), c1 = __ldg(cs4 + 2 * idx + 1);
+      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        amax = fmaxf(amax, fabsf(__fmul_rn(bf16_lo(w[j]), c[2 * j])));
+        amax = fmaxf(amax, fabsf(__fmul_rn(bf16_hi(w[j]), c[2 * j + 1])));
+      }
+    }
+  }
+  amax = block_max(amax, red);
+  const float s = quant_row_scale(amax);
+  const float inv_s = quant_row_inv_scale(s);
+  int8_t* qr = q + row * ldq;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kQThreads;
+    if (idx < nvec) {
+      const float4 c0 = __ldg(cs4 + 2 * idx), c1 = __ldg(cs4 + 2 * idx + 1);
+      const float f[8] = {__fmul_rn(bf16_lo(v[i].x), c0.x), __fmul_rn(bf16_hi(v[i].x), c0.y),
+                          __fmul_rn(bf16_lo(v[i].y), c0.z), __fmul_rn(bf16_hi(v[i].y), c0.w),
+                          __fmul_rn(bf16_lo(v[i].z), c1.x), __fmul_rn(bf16_hi(v[i].z), c1.y),
+                          __fmul_rn(bf16_lo(v[i].w), c1.z), __fmul_rn(bf16_hi(v[i].w), c1.w)};
+      *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(idx) * 8) = quant8(f, s, inv_s);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+// Any alignment / length: two passes over the row, exact division.
+__global__ void __launch_bounds__(kQThreads) quant_rows_colscaled_generic_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ cs,
+    int64_t cols, int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
+  __shared__ float red[4];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float amax = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += kQThreads)
+    amax = fmaxf(amax, fabsf(__fmul_rn(__bfloat162float(xr[c]), cs[c])));
+  amax = block_max(amax, red);
+  const float s = quant_row_scale(amax);
+  int8_t* qr = q + row * ldq;
+  for (int64_t c = threadIdx.x; c < cols; c += kQThreads)
+    qr[c] = static_cast<int8_t>(quant_exact(__fmul_rn(__bfloat162float(xr[c]), cs[c]), s));
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+// wqT[k, n] = wq[n, k]: 64 (n) x 128 (k) tiles through shared memory, 16-byte
+// loads along k, 16-byte stores along n.
+constexpr int kTTN = 64;
+constexpr int kTTK = 128;
+__global__ void __launch_bounds__(256) transpose_i8_kernel(const int8_t* __restrict__ wq,
+                                                           int64_t ldw, int64_t n_rows,
+                                                           int64_t k_cols,
+                                                           int8_t* __restrict__ out, int64_t ldt,
+                                                           bool vec_in, bool vec_out) {
+  __shared__ __align__(16) int8_t tile[kTTK][kTTN + 16];
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTTN;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kTTK;
+  for (int c = threadIdx.x; c < kTTN * (kTTK / 16); c += 256) {
+    const int r = c % kTTN, qd = c / kTTN;
+    const int64_t n = n0 + r;
+    const int64_t kb = k0 + qd * 16;
+    __align__(16) int8_t v[16];
+    if (vec_in && n < n_rows && kb + 16 <= k_cols) {
+      *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(wq + n * ldw + kb));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        v[j] = (n < n_rows && kb + j < k_cols) ? wq[n * ldw + kb + j] : static_cast<int8_t>(0);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) tile[qd * 16 + j][r] = v[j];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < kTTK * (kTTN / 16); c += 256) {
+    const int r = c / (kTTN / 16), qd = c % (kTTN / 16);
+    const int64_t k = k0 + r;
+    const int64_t n = n0 + qd * 16;
+    if (k >= k_cols || n >= n_rows) continue;
+    int8_t* dst = out + k * ldt + n;
+    if (vec_out && n + 16 <= n_rows) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[r][qd * 16]);
+    } else {
+      for (int j = 0; j < 16 && n + j < n_rows; ++j) dst[j] = tile[r][qd * 16 + j];
+    }
+  }
 }
 
 // General path: any alignment / length; reads the row twice.
@@ -321,4 +432,75 @@ extern "C" int lema_grouped_w8a8_dgrad(const void* dy_bf16, int64_t lddy, const 
   // rows of expert e: dx = dy . wdT_e^T, wdT_e = ws[e] ([K, ldt])
   return lema_grouped_bf16_gemm_tn(dy_bf16, lddy, wdT_ws, ldt, dx_bf16, lddx, offsets_host, E,
                                    K, N, stream);
+}
+
+extern "C" int lema_quantize_rows_colscaled(const void* x_bf16, const float* cs, int64_t rows,
+                                            int64_t cols, int64_t ldx, int8_t* q, int64_t ldq,
+                                            float* scale, void* stream) {
+  clear_error();
+  if (rows < 0 || cols < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0) return LEMA_OK;
+  if (x_bf16 == nullptr || cs == nullptr || q == nullptr || scale == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldx < cols || ldq < cols) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld < cols");
+  if (rows > INT32_MAX) return set_error(LEMA_ERR_UNSUPPORTED, "rows exceed 2^31-1");
+  const auto* x = static_cast<const __nv_bfloat16*>(x_bf16);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec_ok = cols > 0 && cols % 8 == 0 && aligned16(x) && (ldx * 2) % 16 == 0 &&
+                      aligned16(cs) && (reinterpret_cast<uintptr_t>(q) % 8) == 0 && ldq % 8 == 0;
+  const int64_t per_thread = (cols / 8 + kQThreads - 1) / kQThreads;
+  const dim3 grid(static_cast<unsigned>(rows));
+  const int c = static_cast<int>(cols);
+  if (vec_ok && per_thread <= 16) {
+    if (per_thread <= 2)
+      quant_rows_colscaled_kernel<2><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+    else if (per_thread <= 4)
+      quant_rows_colscaled_kernel<4><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+    else if (per_thread <= 8)
+      quant_rows_colscaled_kernel<8><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+    else
+      quant_rows_colscaled_kernel<16><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  } else {
+    quant_rows_colscaled_generic_kernel<<<grid, kQThreads, 0, s>>>(x, ldx, cs, cols, q, ldq,
+                                                                    scale);
+  }
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_transpose_i8(const int8_t* wq, int64_t ldw, int64_t N, int64_t K,
+                                 int8_t* wqT, int64_t ldt, void* stream) {
+  clear_error();
+  if (N < 0 || K < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
+  if (N == 0 || K == 0) return LEMA_OK;
+  if (wq == nullptr || wqT == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldw < K || ldt < N) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld too small");
+  if ((K + kTTK - 1) / kTTK > INT32_MAX || (N + kTTN - 1) / kTTN > 65535)
+    return set_error(LEMA_ERR_UNSUPPORTED, "matrix too large for the transpose grid");
+  dim3 grid(static_cast<unsigned>((K + kTTK - 1) / kTTK),
+            static_cast<unsigned>((N + kTTN - 1) / kTTN));
+  const bool vec_in = aligned16(wq) && ldw % 16 == 0;
+  const bool vec_out = aligned16(wqT) && ldt % 16 == 0;
+  transpose_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(wq, ldw, N, K, wqT,
+                                                                           ldt, vec_in, vec_out);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_w8a8_dgrad_int8(const void* dy_bf16, int64_t lddy, const int8_t* wq,
+                                    int64_t ldw, const float* sw, void* dx_bf16, int64_t lddx,
+                                    int8_t* wqT_ws, int64_t ldt, int8_t* dq_ws, int64_t ldq,
+                                    float* sd_ws, int64_t M, int64_t N, int64_t K,
+                                    void* stream) {
+  clear_error();
+  if (ldt < N || ldt % 16 != 0 || ldq < N || ldq % 16 != 0)
+    return set_error(LEMA_ERR_MISALIGNED, "workspace lds must be >= N and multiples of 16");
+  if (sw == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null weight scales");
+  int rc = lema_quantize_rows_colscaled(dy_bf16, sw, M, N, lddy, dq_ws, ldq, sd_ws, stream);
+  if (rc) return rc;
+  rc = lema_transpose_i8(wq, ldw, N, K, wqT_ws, ldt, stream);
+  if (rc) return rc;
+  // dx[M, K] = bf16(sd[m] * sum_n dq[m, n] * wqT[k, n]) (no column scales)
+  return lema_w8a8_gemm(dq_ws, ldq, sd_ws, wqT_ws, ldt, nullptr, nullptr, dx_bf16, lddx, nullptr,
+                        0, M, K, N, stream);
 }

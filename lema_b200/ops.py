@@ -220,6 +220,36 @@ def dequant_transpose(wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
     return wdT[:, :Nn]
 
 
+def quantize_rows_colscaled(x: torch.Tensor, cs: torch.Tensor
+                            ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rows of fp32(x[r, c]) * cs[c] (bf16 x, fp32 cs) quantised per row:
+    (q int8 [R, C] view of an [R, ldq] buffer, scale fp32 [R])."""
+    dev = _require_cuda(x, cs)
+    x = _rows_view(x).to(torch.bfloat16)
+    rows, cols = x.shape
+    ldq = pad_to(max(cols, 1), 16)
+    buf = torch.empty(rows, ldq, dtype=torch.int8, device=dev)
+    if ldq > cols:
+        buf[:, cols:].zero_()
+    scale = torch.empty(rows, dtype=torch.float32, device=dev)
+    N.call("lema_quantize_rows_colscaled", _ptr(x), _ptr(cs.contiguous().float()), rows, cols,
+           _ld(x), _ptr(buf), ldq, _ptr(scale), _stream(dev))
+    return buf[:, :cols], scale
+
+
+def transpose_i8(wq: torch.Tensor) -> torch.Tensor:
+    """wqT[K, N] = wq[N, K] for int8 (a view of a [K, round_up(N, 16)] buffer)."""
+    dev = _require_cuda(wq)
+    wq = _rows_view(wq)
+    if wq.dtype != torch.int8:
+        raise TypeError("transpose_i8 takes int8")
+    Nn, K = wq.shape
+    ldt = pad_to(max(Nn, 1), 16)
+    out = torch.zeros(K, ldt, dtype=torch.int8, device=dev)
+    N.call("lema_transpose_i8", _ptr(wq), _ld(wq), Nn, K, _ptr(out), ldt, _stream(dev))
+    return out[:, :Nn]
+
+
 def bf16_gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """y = bf16(a . b^T) with fp32 accumulation (tcgen05 kind::f16)."""
     dev = _require_cuda(a, b)
@@ -235,8 +265,49 @@ def bf16_gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return y
 
 
+# Straight-through dgrad of the frozen W8A8 projections: "bf16" (the contract:
+# dy . bf16(wq * sw) with fp32 accumulation) or the opt-in "int8" variant
+# (dy * sw quantised per row, int8 GEMM with wq^T; looser tolerance).
+_DGRAD_MODE = "bf16"
+
+
+def set_dgrad_mode(mode: str) -> None:
+    global _DGRAD_MODE
+    if mode not in ("bf16", "int8"):
+        raise ValueError(f"dgrad mode must be 'bf16' or 'int8', not {mode!r}")
+    _DGRAD_MODE = mode
+
+
+def dgrad_mode() -> str:
+    return _DGRAD_MODE
+
+
+def w8a8_dgrad_int8(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """dx[M, K] ~ dy[M, N] . (wq * sw): dy * sw quantised per row to int8, int8
+    GEMM with the transposed int8 weight, dx = bf16(sd[m] * acc)."""
+    dev = _require_cuda(dy, wq, sw)
+    dy = _rows_view(dy).to(torch.bfloat16)
+    M, Nn = dy.shape
+    K = wq.shape[1]
+    ld = pad_to(max(Nn, 1), 16)
+    wqT = torch.empty(K, ld, dtype=torch.int8, device=dev)
+    dq = torch.empty(M, ld, dtype=torch.int8, device=dev)
+    if ld > Nn:
+        wqT[:, Nn:].zero_()
+        dq[:, Nn:].zero_()
+    sd = torch.empty(M, dtype=torch.float32, device=dev)
+    dx = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    N.call("lema_w8a8_dgrad_int8", _ptr(dy), _ld(dy), _ptr(wq), _ld(wq),
+           _ptr(sw.contiguous().float()), _ptr(dx), K, _ptr(wqT), ld, _ptr(dq), ld, _ptr(sd),
+           M, Nn, K, _stream(dev))
+    return dx
+
+
 def w8a8_dgrad(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
-    """dx[M, K] = bf16(dy[M, N] . wdeq[N, K]), wdeq = bf16(wq * sw) (straight-through)."""
+    """dx[M, K] = bf16(dy[M, N] . wdeq[N, K]), wdeq = bf16(wq * sw) (straight-through);
+    the int8 variant when ``set_dgrad_mode("int8")`` is in effect."""
+    if _DGRAD_MODE == "int8":
+        return w8a8_dgrad_int8(dy, wq, sw)
     dev = _require_cuda(dy, wq, sw)
     dy = _rows_view(dy)
     if dy.dtype != torch.bfloat16:

@@ -226,6 +226,20 @@ def w8a8_linear_ref(x_bits: np.ndarray, w_bits: np.ndarray, bias_bits: np.ndarra
     return {"xq": xq, "sx": sx, "wq": wq, "sw": sw, "acc": acc, "y": y}
 
 
+def dgrad_int8_ref(dy_bits: np.ndarray, wq: np.ndarray, sw: np.ndarray):
+    """The optional int8-dy variant of the frozen-base backward (straight-through
+    estimator of src/lema/adapters/_llama.py:245-250 through both quantisers):
+    g[m, n] = fp32(dy[m, n]) * sw[n] (one fp32 rounding), g quantised per row by
+    the contract (dq, sd), acc = dq . wq in s32, dx = bf16(acc * sd[m]). Returns
+    dict with g, dq, sd, acc, dx (bf16 bits)."""
+    sw = np.ascontiguousarray(sw, dtype=np.float32)
+    g = (bf16_bits_to_f32(np.asarray(dy_bits, dtype=np.uint16)) * sw[None, :]).astype(np.float32)
+    dq, sd = c_quantize_rows_f32(g)
+    acc = c_int8_gemm(dq, np.ascontiguousarray(np.asarray(wq, dtype=np.int8).T))
+    dx = c_epilogue(acc, sd, np.ones(acc.shape[1], np.float32), None)
+    return {"g": g, "dq": dq, "sd": sd, "acc": acc, "dx": dx}
+
+
 def cfg1_inputs(seed: int = 0, M: int = 512, K: int = 4096, N: int = 4096,
                 outlier_frac: float = 0.01):
     """Seeded single-linear workload: X ~ N(0,1) bf16 [M,K] with 1% of channels

@@ -202,6 +202,65 @@ def test_dequant_transpose_and_dgrad(cuda_device, oracle, M, N, K):
     _dgrad_tol_check(bits(dx), ref)
 
 
+@pytest.mark.parametrize("shape", [(64, 4096), (7, 4100), (3, 11008), (5, 24576), (1, 8),
+                                   (300, 16), (0, 64)])
+def test_quantize_rows_colscaled_bitexact(cuda_device, oracle, shape):
+    """Rows of fp32(x) * cs quantised: vector path (cols % 8 == 0, <= 16K), the
+    generic path (ragged or longer rows) and the empty case, all bit-exact."""
+    x = rand_bf16(shape, seed=shape[0] * 3 + shape[1], outliers=False)
+    g = torch.Generator().manual_seed(shape[1])
+    cs = torch.rand(shape[1], generator=g) * 0.01 + 1e-4
+    if shape[0] > 2:
+        x[1] = 0.0
+    q, s = ops.quantize_rows_colscaled(x.to(cuda_device), cs.to(cuda_device))
+    f = (x.float().numpy() * cs.numpy()[None, :]).astype(np.float32)
+    qr, sr = oracle.c_quantize_rows_f32(f)
+    np.testing.assert_array_equal(q.cpu().numpy(), qr)
+    np.testing.assert_array_equal(s.cpu().numpy(), sr)
+
+
+@pytest.mark.parametrize("N,K", [(4096, 4096), (11008, 4096), (4096, 11008), (37, 129),
+                                 (64, 128), (1, 5)])
+def test_transpose_i8_exact(cuda_device, N, K):
+    g = torch.Generator(device=cuda_device).manual_seed(N + K)
+    wq = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=cuda_device, generator=g)
+    t = ops.transpose_i8(wq)
+    assert torch.equal(t, wq.t())
+    # strided source (a column window of a wider matrix) takes the scalar loads
+    if K > 3:
+        t2 = ops.transpose_i8(wq[:, 1:K - 1])
+        assert torch.equal(t2, wq[:, 1:K - 1].t())
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (100, 300, 200), (64, 11008, 4096),
+                                   (1024, 4096, 11008)])
+def test_w8a8_dgrad_int8(cuda_device, oracle, M, N, K):
+    """The optional int8-dy dgrad: bit-exact against its own restatement (scaled
+    quantiser, s32 GEMM, epilogue with unit column scales), and within a 2e-2
+    relative RMS of the bf16 straight-through dgrad it approximates."""
+    dev = cuda_device
+    w = rand_bf16((N, K), seed=N * 3 + K, scale=0.02, outliers=False)
+    wq, sw = ops.quantize_weight(w.to(dev))
+    dy = rand_bf16((M, N), seed=M + 5, outliers=False)
+    dx = ops.w8a8_dgrad_int8(dy.to(dev), wq, sw)
+    ref = oracle.dgrad_int8_ref(bits(dy), wq.cpu().numpy(), sw.cpu().numpy())
+    np.testing.assert_array_equal(bits(dx), ref["dx"])
+    # against the contract's bf16 dgrad (double-accumulated)
+    ref_wdT = oracle.c_dequant_transpose(wq.cpu().numpy(), sw.cpu().numpy())
+    _, exact = oracle.c_bf16_gemm_tn(bits(dy), ref_wdT)
+    got = torch.from_numpy(bits(dx).view(np.int16)).view(torch.bfloat16).float().numpy()
+    rms = float(np.sqrt(np.mean(exact.astype(np.float64) ** 2)))
+    rel = float(np.sqrt(np.mean((got.astype(np.float64) - exact) ** 2))) / rms
+    assert rel <= 2e-2, rel
+    # the mode switch routes the straight-through dgrad through the same entry point
+    prev = ops.dgrad_mode()
+    ops.set_dgrad_mode("int8")
+    try:
+        assert torch.equal(ops.w8a8_dgrad(dy.to(dev), wq, sw), dx)
+    finally:
+        ops.set_dgrad_mode(prev)
+
+
 def test_bf16_gemm_tn(cuda_device, oracle):
     dev = cuda_device
     a = rand_bf16((300, 520), seed=1, outliers=False)

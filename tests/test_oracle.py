@@ -98,6 +98,29 @@ def test_gemm_epilogue_dequant_agree(oracle):
                                   oracle.np_dequant_transpose(b, sw))
 
 
+def test_int8_dgrad_restatement(oracle):
+    """The int8-dy dgrad chain (C) agrees with the same chain in numpy, and with
+    unit scales it is the exact integer product."""
+    rng = np.random.default_rng(4)
+    dy = oracle.f32_to_bf16_bits(rng.standard_normal((21, 90)).astype(np.float32))
+    wq = rng.integers(-127, 128, size=(90, 33), dtype=np.int8)
+    sw = rng.random(90, dtype=np.float32) * 1e-3 + 1e-5
+    out = oracle.dgrad_int8_ref(dy, wq, sw)
+    g = (oracle.bf16_bits_to_f32(dy) * sw[None, :]).astype(np.float32)
+    dq, sd = oracle.np_quantize_rows_f32(g)
+    np.testing.assert_array_equal(out["dq"], dq)
+    np.testing.assert_array_equal(out["sd"], sd)
+    acc = oracle.np_int8_gemm(dq, np.ascontiguousarray(wq.T))
+    np.testing.assert_array_equal(out["acc"], acc)
+    np.testing.assert_array_equal(out["dx"],
+                                  oracle.np_epilogue(acc, sd, np.ones(33, np.float32), None))
+    # dx approximates dy . (wq * sw) to the quantiser's resolution
+    exact = oracle.bf16_bits_to_f32(dy).astype(np.float64) @ (wq * sw[:, None]).astype(np.float64)
+    got = oracle.bf16_bits_to_f32(out["dx"]).astype(np.float64)
+    rel = np.sqrt(np.mean((got - exact) ** 2) / np.mean(exact ** 2))
+    assert rel < 2e-2, rel
+
+
 def test_bf16_gemm_reference_close_to_torch(oracle):
     g = torch.Generator().manual_seed(3)
     a = torch.randn(19, 70, generator=g).to(torch.bfloat16)

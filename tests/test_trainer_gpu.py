@@ -193,3 +193,39 @@ def test_more_vram_slots_give_the_same_step(cuda_device):
         assert losses == out[0][0]
         for a, b in zip(params, out[0][1]):
             assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_int8_dgrad_step_close_to_bf16_dgrad(cuda_device):
+    """The opt-in int8-dy dgrad leaves the forward (and loss) untouched and gives
+    LoRA gradients within 5e-2 relative RMS of the bf16 straight-through dgrad."""
+    from lema_b200 import ops
+    ids = _ids(29, 2, 64, SMALL.vocab, cuda_device)
+    grads = []
+    prev = ops.dgrad_mode()
+    try:
+        for mode in ("bf16", "int8"):
+            ops.set_dgrad_mode(mode)
+            tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=0.0, seed=8)
+            with torch.no_grad():
+                g = torch.Generator(device=cuda_device).manual_seed(9)
+                for layer in tr.lora:
+                    for a, b in layer.values():
+                        b.copy_(torch.randn(b.shape, device=cuda_device, generator=g) * 0.02)
+            captured = []
+            orig = tr.opt.step
+
+            def grab(orig=orig, captured=captured, tr=tr):
+                captured.extend(p.grad.detach().float().clone() for p in tr.params)
+                return orig()
+            tr.opt.step = grab
+            with sdpa_kernel(SDPBackend.MATH):
+                loss = float(tr.train_step(ids))
+            grads.append((loss, captured))
+            tr.close()
+    finally:
+        ops.set_dgrad_mode(prev)
+    (l0, g0), (l1, g1) = grads
+    assert l0 == l1
+    for a, b in zip(g1, g0):
+        rms = b.pow(2).mean().sqrt().item() + 1e-30
+        assert (a - b).pow(2).mean().sqrt().item() / rms <= 5e-2
