@@ -571,8 +571,9 @@ def run_train(args, world, rank, local) -> dict | None:
                          "activations >> L2"},
         "gpu_launches": launches,
         "loss_last": round(float(losses[-1]), 4),
-        "roofline": {"bound": "tensor", "kernel": "gemm_sm100 int8 (all W8A8 projection and "
-                                                  "grouped expert GEMMs of the timed steps)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_sm100 int8 (every int8 GEMM launch of "
+                                                  "the timed steps: W8A8 projections, grouped "
+                                                  "experts, int8-dy dgrads when selected)",
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                      "frac": round(achieved / int8_peak, 4),
                      "peak_source": "measured cuBLASLt int8 GEMM (torch._int_mm 8192^3, burst)",
@@ -581,6 +582,7 @@ def run_train(args, world, rank, local) -> dict | None:
                      # int8 GEMMs, from an ncu capture of this workload (4 metrics, 8 launches)
                      "traffic": TRAIN_GEMM_TRAFFIC_BYTES if not (long_ft or moe) else None,
                      "gemm_launches": gemm_launches,
+                     "gemm_launches_untimed": ops.GemmTimer.dropped,
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
                      "algorithmic_ops_per_step": gemm_ops / args.steps},
         "pcie": {"h2d_gbs_measured": round(h2d_gbs, 1),

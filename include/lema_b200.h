@@ -174,6 +174,17 @@ LEMA_API int lema_w8a8_dgrad_int8(const void* dy_bf16, int64_t lddy, const int8_
                                   int8_t* wqT_ws, int64_t ldt, int8_t* dq_ws, int64_t ldq,
                                   float* sd_ws, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* ---- Timing of the int8 GEMM launches ---------------------------------- */
+/* Starts recording a CUDA event pair around every int8 GEMM launch (dense and
+ * grouped, on the current device, streams not being captured) up to
+ * max_records launches; events are created here, not in the timed region. */
+LEMA_API int lema_gemm_timer_start(int64_t max_records);
+/* Stops recording, waits for the recorded launches and returns the summed
+ * 2*M*N*K ops, the summed launch durations in ms, the launches recorded and
+ * the launches not recorded (pool full, capturing stream, other device). */
+LEMA_API int lema_gemm_timer_stop(double* total_ops, double* total_ms, int64_t* launches,
+                                  int64_t* dropped);
+
 /* ---- Fused producers of the W8A8 GEMM inputs (and their backward) ------ */
 /* RMSNorm of HF LlamaRMSNorm as adapters/_llama.py:238,248 apply it, in bf16:
  * hn = bf16(g * bf16(x * rsqrt(mean(x^2) + eps))) per row; rstd[r] (fp32) for

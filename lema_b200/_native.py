@@ -42,6 +42,9 @@ _SIGNATURES: dict[str, list] = {
     "lema_transpose_i8": [vp, i64, i64, i64, vp, i64, vp],
     "lema_w8a8_dgrad_int8": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, i64, i64,
                              vp],
+    "lema_gemm_timer_start": [i64],
+    "lema_gemm_timer_stop": [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i64),
+                             C.POINTER(i64)],
     "lema_grouped_w8a8_gemm": [vp, i64, vp, vp, i64, vp, vp, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_bf16_gemm_tn": [vp, i64, vp, i64, vp, i64, vp, i32, i64, i64, vp],
     "lema_grouped_w8a8_dgrad": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, i64, i64, vp],

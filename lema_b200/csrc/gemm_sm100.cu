@@ -31,6 +31,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include <cudaTypedefs.h>
 
@@ -1099,6 +1100,56 @@ void plan_split(GemmParams& p, int workers) {
   p.split_tiles = rem;
 }
 
+// Optional timing of the int8 GEMM launches (the bench's tensor roofline):
+// a pre-created pool of CUDA event pairs recorded on the launching stream
+// around each launch, so an instrumented step keeps the fused entry points
+// and pays one event record on either side of each GEMM. Launches on a
+// capturing stream, on another device or past the pool are not recorded
+// (counted as dropped).
+struct GemmTimer {
+  std::mutex mu;
+  bool on = false;
+  int device = -1;
+  std::vector<cudaEvent_t> events;  // 2 per record
+  std::vector<double> ops;
+  int64_t used = 0;
+  int64_t dropped = 0;
+};
+
+GemmTimer& gemm_timer() {
+  static GemmTimer t;
+  return t;
+}
+
+// Reserves a record slot for a launch on `stream`; -1 when not timing it.
+int64_t timer_begin(cudaStream_t stream, double ops) {
+  GemmTimer& t = gemm_timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (!t.on) return -1;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    (void)cudaGetLastError();
+    ++t.dropped;
+    return -1;
+  }
+  if (cap != cudaStreamCaptureStatusNone || current_device() != t.device ||
+      2 * (t.used + 1) > static_cast<int64_t>(t.events.size())) {
+    ++t.dropped;
+    return -1;
+  }
+  const int64_t i = t.used++;
+  t.ops[i] = ops;
+  if (cudaEventRecord(t.events[2 * i], stream) != cudaSuccess) (void)cudaGetLastError();
+  return i;
+}
+
+void timer_end(int64_t i, cudaStream_t stream) {
+  if (i < 0) return;
+  GemmTimer& t = gemm_timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (cudaEventRecord(t.events[2 * i + 1], stream) != cudaSuccess) (void)cudaGetLastError();
+}
+
 enum TilePath { kPath1Sm128 = 0, kPath1Sm256 = 1, kPathPair = 2 };
 
 // Tile path: LEMA_GEMM_TILE=1sm128|1sm256|pair forces one (tests, tuning);
@@ -1213,9 +1264,15 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   p.total_rows = static_cast<int32_t>(rows);
 
   if (kind == kKindI8) {
-    if (path == kPathPair) return launch_pair<kKindI8>(ma, mb, my, p, workers, stream);
-    return path == kPath1Sm256 ? launch<kKindI8, 256, 4>(ma, mb, my, p, workers, stream)
+    const int64_t rec = timer_begin(stream, 2.0 * static_cast<double>(rows) *
+                                                static_cast<double>(n) * static_cast<double>(k));
+    if (path == kPathPair)
+      rc = launch_pair<kKindI8>(ma, mb, my, p, workers, stream);
+    else
+      rc = path == kPath1Sm256 ? launch<kKindI8, 256, 4>(ma, mb, my, p, workers, stream)
                                : launch<kKindI8, 128, 6>(ma, mb, my, p, workers, stream);
+    timer_end(rec, stream);
+    return rc;
   }
   if (path == kPathPair) return launch_pair<kKindBF16>(ma, mb, my, p, workers, stream);
   return path == kPath1Sm256 ? launch<kKindBF16, 256, 4>(ma, mb, my, p, workers, stream)
@@ -1376,4 +1433,50 @@ extern "C" int lema_bf16_gemm_tn_f32(const void* a_bf16, int64_t lda, const void
   g.row_start[1] = M;
   return run_gemm(kKindBF16, a_bf16, lda, b_bf16, ldb, g, N, K, nullptr, nullptr, nullptr,
                   nullptr, 0, reinterpret_cast<int32_t*>(y_f32), ldy, s);
+}
+
+extern "C" int lema_gemm_timer_start(int64_t max_records) {
+  clear_error();
+  if (max_records <= 0 || max_records > (int64_t{1} << 20))
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "max_records must be in [1, 2^20]");
+  GemmTimer& t = gemm_timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  const int dev = current_device();
+  if (dev != t.device) {
+    for (cudaEvent_t e : t.events) (void)cudaEventDestroy(e);
+    t.events.clear();
+    t.device = dev;
+  }
+  while (static_cast<int64_t>(t.events.size()) < 2 * max_records) {
+    cudaEvent_t e = nullptr;
+    LEMA_CUDA_TRY(cudaEventCreate(&e));
+    t.events.push_back(e);
+  }
+  t.ops.assign(static_cast<size_t>(max_records), 0.0);
+  t.used = 0;
+  t.dropped = 0;
+  t.on = true;
+  return LEMA_OK;
+}
+
+extern "C" int lema_gemm_timer_stop(double* total_ops, double* total_ms, int64_t* launches,
+                                    int64_t* dropped) {
+  clear_error();
+  GemmTimer& t = gemm_timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  t.on = false;
+  double ops = 0.0, ms = 0.0;
+  for (int64_t i = 0; i < t.used; ++i) {
+    LEMA_CUDA_TRY(cudaEventSynchronize(t.events[2 * i + 1]));
+    float e = 0.f;
+    LEMA_CUDA_TRY(cudaEventElapsedTime(&e, t.events[2 * i], t.events[2 * i + 1]));
+    ms += e;
+    ops += t.ops[i];
+  }
+  if (total_ops) *total_ops = ops;
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = t.used;
+  if (dropped) *dropped = t.dropped;
+  t.used = 0;
+  return LEMA_OK;
 }

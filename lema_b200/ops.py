@@ -25,26 +25,33 @@ from . import _native as N
 
 
 class GemmTimer:
-    """Optional CUDA-event bracketing of every int8 GEMM launch (for the bench):
-    records (start, end, ops) on the launching stream. Off unless ``enable()``."""
+    """Optional timing of every int8 GEMM launch (for the bench's roofline): the
+    library records a pre-created CUDA event pair around each launch on its
+    stream (``lema_gemm_timer_start`` / ``lema_gemm_timer_stop``), so a timed
+    step runs the same fused entry points as an untimed one."""
 
     enabled = False
-    records: list = []
+    max_records = 1 << 16
+    dropped = 0
 
     @classmethod
     def enable(cls, on: bool = True) -> None:
+        if on:
+            N.call("lema_gemm_timer_start", cls.max_records)
+        elif cls.enabled:
+            cls.summary()
         cls.enabled = on
-        cls.records = []
 
     @classmethod
     def summary(cls) -> tuple[float, float, int]:
-        """(total ops, total ms, launches) over the recorded GEMMs (synchronises)."""
-        ops_, ms = 0.0, 0.0
-        for e0, e1, n in cls.records:
-            e1.synchronize()
-            ms += e0.elapsed_time(e1)
-            ops_ += n
-        return ops_, ms, len(cls.records)
+        """(total ops, total ms, launches) over the recorded GEMMs since
+        ``enable()`` (synchronises; recording stops)."""
+        ops_, ms = C.c_double(0.0), C.c_double(0.0)
+        n, dropped = C.c_int64(0), C.c_int64(0)
+        N.call("lema_gemm_timer_stop", C.byref(ops_), C.byref(ms), C.byref(n), C.byref(dropped))
+        cls.enabled = False
+        cls.dropped = dropped.value
+        return ops_.value, ms.value, n.value
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -188,20 +195,8 @@ def w8a8_linear_forward(x2d: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
     y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
     if bias is not None:
         bias = bias.contiguous().to(torch.bfloat16)
-    stream = _stream(dev)
-    if not GemmTimer.enabled:
-        N.call("lema_w8a8_linear_fwd", _ptr(x2d), _ld(x2d), _ptr(wq), _ld(wq), _ptr(sw),
-               _ptr(bias), _ptr(y), Nn, _ptr(xq), ldq, _ptr(sx), M, Nn, K, stream)
-        return y
-    N.call("lema_quantize_rows", _ptr(x2d), M, K, _ld(x2d), _ptr(xq), ldq, _ptr(sx), stream)
-    s = torch.cuda.current_stream(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    N.call("lema_w8a8_gemm", _ptr(xq), ldq, _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), _ptr(bias),
-           _ptr(y), Nn, None, Nn, M, Nn, K, stream)
-    e1.record(s)
-    GemmTimer.records.append((e0, e1, 2.0 * M * Nn * K))
+    N.call("lema_w8a8_linear_fwd", _ptr(x2d), _ld(x2d), _ptr(wq), _ld(wq), _ptr(sw),
+           _ptr(bias), _ptr(y), Nn, _ptr(xq), ldq, _ptr(sx), M, Nn, K, _stream(dev))
     return y
 
 
@@ -350,16 +345,7 @@ def grouped_w8a8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: 
     args = ("lema_grouped_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx.contiguous().float()),
             _ptr(wq), wq.stride(1), _ptr(sw.contiguous().float()), _ptr(bias), _ptr(y), Nn,
             offs, E, Nn, K, _stream(dev))
-    if not GemmTimer.enabled:
-        N.call(*args)
-        return y
-    s = torch.cuda.current_stream(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s)
     N.call(*args)
-    e1.record(s)
-    GemmTimer.records.append((e0, e1, 2.0 * (int(offsets[-1]) - int(offsets[0])) * Nn * K))
     return y
 
 
@@ -573,19 +559,8 @@ def gemm_from_quant(xq, sx, wq, sw) -> torch.Tensor:
     M, K = xq.shape
     Nn = wq.shape[0]
     y = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
-    stream = _stream(dev)
-    if not GemmTimer.enabled:
-        N.call("lema_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), None,
-               _ptr(y), Nn, None, Nn, M, Nn, K, stream)
-        return y
-    s = torch.cuda.current_stream(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s)
     N.call("lema_w8a8_gemm", _ptr(xq), _ld(xq), _ptr(sx), _ptr(wq), _ld(wq), _ptr(sw), None,
-           _ptr(y), Nn, None, Nn, M, Nn, K, stream)
-    e1.record(s)
-    GemmTimer.records.append((e0, e1, 2.0 * M * Nn * K))
+           _ptr(y), Nn, None, Nn, M, Nn, K, _stream(dev))
     return y
 
 

@@ -492,3 +492,26 @@ def test_wgrad_fp32_accumulators(cuda_device, oracle, M, N, K):
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     err = np.abs(dw - ref)
     assert np.all(err <= 2e-5 * np.abs(ref) + 1e-5 * rms + 1e-30), err.max()
+
+
+def test_gemm_timer_records_int8_launches(cuda_device):
+    """The library's GEMM timer records one event pair per int8 GEMM launch
+    (dense, grouped, inside the fused forward) and none for bf16 GEMMs."""
+    dev = cuda_device
+    x = rand_bf16((512, 1024), seed=3).to(dev)
+    wq, sw = ops.quantize_weight(rand_bf16((768, 1024), seed=4, scale=0.02).to(dev))
+    ops.GemmTimer.enable(True)
+    ops.w8a8_linear_forward(x, wq, sw)
+    xq, sx = ops.quantize_rows(x)
+    ops.w8a8_gemm(xq, sx, wq, sw)
+    ops.bf16_gemm_tn(x, x[:256])
+    wg = wq.view(1, 768, 1024)
+    ops.grouped_w8a8_gemm(xq, sx, wg, sw.view(1, 768), [0, 300])
+    total_ops, ms, n = ops.GemmTimer.summary()
+    assert n == 3 and ops.GemmTimer.dropped == 0
+    assert total_ops == 2.0 * 1024 * 768 * (512 + 512 + 300)
+    assert 0.0 < ms < 1000.0
+    # stopped: nothing more is recorded
+    ops.w8a8_gemm(xq, sx, wq, sw)
+    ops.GemmTimer.enable(True)
+    assert ops.GemmTimer.summary()[2] == 0
