@@ -452,7 +452,8 @@ def run_train(args, world, rank, local) -> dict | None:
         batch, seq = 8, 512
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
-                                 weight_shard=shard, vram_slots=args.vram_slots)
+                                 weight_shard=shard, vram_slots=args.vram_slots,
+                                 ckpt_mode=CKPT_MODES[args.ckpt])
         workload = (f"mixtral_streamed_lora: {shape.layers} x [hidden 4096, 32 q / 8 kv heads "
                     "x 128, 8 experts x SwiGLU 14336, top-2 softmax routing], vocab 32000, LoRA "
                     "r16 a32 on q/v, W8A8 attention projections and grouped W8A8 experts "
@@ -465,7 +466,7 @@ def run_train(args, world, rank, local) -> dict | None:
         last4 = tuple(range(max(0, shape.layers - 4), shape.layers))
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, targets=(), seed=0,
                                  resident_layers=args.resident_layers, attn_chunk=512,
-                                 full_ft_layers=last4)
+                                 full_ft_layers=last4, ckpt_mode=CKPT_MODES[args.ckpt])
         workload = (f"llama7b_selective_ft_2048: {shape.layers} x [hidden 4096, 32x128 heads, "
                     "MLP 11008], vocab 32000, bs 1 x seq 2048, 512-token chunked causal "
                     "attention, W8A8 projections streamed from pinned RAM, activation "
@@ -475,7 +476,8 @@ def run_train(args, world, rank, local) -> dict | None:
         batch, seq = 8, 512
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
-                                 weight_shard=shard, vram_slots=args.vram_slots)
+                                 weight_shard=shard, vram_slots=args.vram_slots,
+                                 ckpt_mode=CKPT_MODES[args.ckpt])
         workload = (f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 heads, MLP "
                     "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections streamed "
                     "from pinned RAM, activation checkpoints offloaded")
@@ -493,7 +495,6 @@ def run_train(args, world, rank, local) -> dict | None:
     barrier(world)
     torch.cuda.synchronize(dev)
     launches0 = _native.kernel_launches
-    ops.GemmTimer.enable(True)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -505,10 +506,24 @@ def run_train(args, world, rank, local) -> dict | None:
     barrier(world)
     clk = clocks.stop()
     launches = _native.kernel_launches - launches0
-    gemm_ops, gemm_ms, gemm_launches = ops.GemmTimer.summary()
-    ops.GemmTimer.enable(False)
     ms = t0.elapsed_time(t1)
     ms_max = max_over_ranks(ms, world)
+    # The same K steps again with an event pair around every int8 GEMM launch
+    # (the tensor roofline). Kept out of the region above: an event record
+    # between two kernels ends the programmatic overlap of the GEMM's set-up
+    # with its producer, which costs a compute-bound step a few percent.
+    barrier(world)
+    ops.GemmTimer.enable(True)
+    r0 = torch.cuda.Event(enable_timing=True)
+    r1 = torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    for i in range(args.steps):
+        tr.train_step(ids_dev[i % n_batches])
+    r1.record(stream)
+    torch.cuda.synchronize(dev)
+    gemm_ops, gemm_ms, gemm_launches = ops.GemmTimer.summary()
+    timed_step_ms = max_over_ranks(r0.elapsed_time(r1), world) / args.steps
+    barrier(world)
     dev_err = _native.device_error()
     if dev_err:
         raise RuntimeError(f"kernel device error word {dev_err:#x}")
@@ -564,6 +579,7 @@ def run_train(args, world, rank, local) -> dict | None:
                    "resident_layers": args.resident_layers,
                    "vram_slots": args.vram_slots,
                    "dgrad": args.dgrad,
+                   "checkpoints": args.ckpt,
                    "weight_stream": ("sharded: 1/N of each segment per rank over PCIe, NCCL "
                                      "all-gather over NVLink" if shard else
                                      "own: every rank streams its own full segments"),
@@ -581,6 +597,9 @@ def run_train(args, world, rank, local) -> dict | None:
                      # DRAM bytes (read + write) per launch, averaged over a layer's four
                      # int8 GEMMs, from an ncu capture of this workload (4 metrics, 8 launches)
                      "traffic": TRAIN_GEMM_TRAFFIC_BYTES if not (long_ft or moe) else None,
+                     "measured_over": f"a second run of the {args.steps} timed steps with "
+                                      "an event pair around each int8 GEMM launch",
+                     "instrumented_ms_per_step": round(timed_step_ms, 3),
                      "gemm_launches": gemm_launches,
                      "gemm_launches_untimed": ops.GemmTimer.dropped,
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
@@ -677,6 +696,9 @@ def run_reference(args) -> dict | None:
     }
 
 
+CKPT_MODES = {"host": 0, "host-kernel": 1, "device": 2}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -697,6 +719,10 @@ def main():
     ap.add_argument("--dgrad", choices=["bf16", "int8"], default="bf16",
                     help="straight-through dgrad of the frozen projections: bf16 (the "
                          "operator contract, default) or the opt-in int8-dy variant")
+    ap.add_argument("--ckpt", choices=list(CKPT_MODES), default="host",
+                    help="boundary activations: host (offloaded to pinned host by the copy "
+                         "engine, default), host-kernel (offloaded by the SM store kernel) or "
+                         "device (kept in HBM, no offload: for measuring what the offload costs)")
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)

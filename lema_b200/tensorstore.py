@@ -36,15 +36,30 @@ def _ev_ptr(ev: torch.cuda.Event | None):
 
 
 class ActivationCheckpointStore:
-    """``num`` pinned host slots of ``shape`` (bf16 by default)."""
+    """``num`` pinned host slots of ``shape`` (bf16 by default).
+
+    ``mode`` 0 saves through the copy engine, 1 through the SM store kernel
+    (``lema_ckpt_save``); mode 2 keeps the boundary tensors in device memory
+    instead (the reference's ``boundary_activations`` list,
+    src/lema/_trainer.py:109-111): no host slots, no copies."""
+
+    DEVICE = 2
 
     def __init__(self, num: int, shape: tuple[int, ...], device: torch.device,
                  dtype: torch.dtype = torch.bfloat16, mode: int = 0,
                  h2d_stream: torch.cuda.Stream | None = None):
+        if mode not in (0, 1, self.DEVICE):
+            raise ValueError(f"checkpoint mode must be 0, 1 or 2, not {mode}")
         self.device = torch.device(device)
         self.shape = tuple(shape)
         self.dtype = dtype
         self.mode = mode
+        self._kept: dict[int, torch.Tensor] = {}
+        if mode == self.DEVICE:
+            self.host = None
+            self.nbytes = 0  # bytes moved per slot and direction
+            self._dev_buf: dict[int, torch.Tensor] = {}
+            return
         self.host = torch.empty((num, *shape), dtype=dtype).pin_memory()
         self.nbytes = self.host[0].numel() * self.host.element_size()
         self.d2h = torch.cuda.Stream(device=self.device)
@@ -59,6 +74,9 @@ class ActivationCheckpointStore:
             raise ValueError(f"checkpoint slot holds {self.shape} {self.dtype}, got "
                              f"{tuple(t.shape)} {t.dtype}")
         t = t.detach()
+        if self.mode == self.DEVICE:
+            self._kept[i] = t
+            return
         if not t.is_contiguous():
             t = t.contiguous()
         ready = torch.cuda.Event()
@@ -70,6 +88,9 @@ class ActivationCheckpointStore:
     def restore_async(self, i: int) -> torch.Tensor:
         """Starts the H2D copy of slot i into a device buffer and returns the buffer;
         call ``wait(i)`` on the consuming stream before reading it."""
+        if self.mode == self.DEVICE:
+            self._dev_buf[i] = self._kept.pop(i)
+            return self._dev_buf[i]
         buf = torch.empty(self.shape, dtype=self.dtype, device=self.device)
         # buf's memory may still be read by earlier work on the allocating stream:
         # the copy stream starts only after that point.
@@ -81,6 +102,8 @@ class ActivationCheckpointStore:
         return buf
 
     def wait(self, i: int, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        if self.mode == self.DEVICE:
+            return self._dev_buf.pop(i)
         s = stream or torch.cuda.current_stream(self.device)
         s.wait_event(self.restored[i])
         return self._dev_buf.pop(i)

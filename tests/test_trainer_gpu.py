@@ -112,19 +112,21 @@ def test_streamed_equals_hbm_resident(cuda_device):
 
 def test_trainer_kernel_mode_checkpoint(cuda_device):
     """Boundary activations saved by the SM store kernel (mode 1) instead of the
-    copy engine give the same step."""
+    copy engine, or kept in device memory (mode 2, no offload), give the same
+    step."""
     ids = _ids(13, 2, 64, SMALL.vocab, cuda_device)
     out = []
-    for mode in (0, 1):
+    for mode in (0, 1, 2):
         tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=1e-3, seed=2,
                                  ckpt_mode=mode)
         with sdpa_kernel(SDPBackend.MATH):
             out.append(float(tr.train_step(ids)))
         out.append([p.detach().clone() for p in tr.params])
         tr.close()
-    assert out[0] == out[2]
-    for a, b in zip(out[1], out[3]):
+    assert out[0] == out[2] == out[4]
+    for a, b, c in zip(out[1], out[3], out[5]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+        assert torch.equal(a.view(torch.int16), c.view(torch.int16))
 
 
 def test_attention_checkpointing_gives_the_same_step(cuda_device):
