@@ -129,26 +129,45 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __re
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// Max over a CTA of W warps (called once per CTA); every thread gets the result.
+template <int W>
+__device__ __forceinline__ float block_max_w(float v, float* red) {
+  v = warp_max(v);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) r = fmaxf(r, red[w]);
+  return r;
+}
+
 // Rows of x[r, c] * cs[c] (bf16 x, fp32 column scales; each product rounded to
-// fp32) quantised by the contract: the row is held as bf16 vectors and the
-// products are formed twice (for |max| and for the quantiser), the scales read
-// through L1.
-template <int VPT>
-__global__ void __launch_bounds__(kQThreads) quant_rows_colscaled_kernel(
+// fp32) quantised by the contract: one CTA of THREADS threads per row, the row
+// held as bf16 vectors (VPT 16-byte vectors per thread, loads issued before
+// use), the products formed twice (for |max| and for the quantiser), the
+// scales read through L1. THREADS grows with the row so that VPT stays <= 6
+// (rows up to 24576 columns at 512 threads).
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) quant_rows_colscaled_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, const float* __restrict__ cs, int cols,
     int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
-  __shared__ float red[4];
+  __shared__ float red[THREADS / 32];
   const int64_t row = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
   const float4* cs4 = reinterpret_cast<const float4*>(cs);
   const int nvec = cols / 8;
   uint4 v[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * THREADS;
+    if (idx < nvec) v[i] = ld_stream(xr + idx);
+  }
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int idx = threadIdx.x + i * kQThreads;
+    const int idx = threadIdx.x + i * THREADS;
     if (idx < nvec) {
-      v[i] = ld_stream(xr + idx);
       const float4 c0 = __ldg(cs4 + 2 * idx), c1 = __ldg(cs4 + 2 * idx + 1);
       const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
@@ -159,13 +178,13 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_colscaled_kernel(
       }
     }
   }
-  amax = block_max(amax, red);
+  amax = block_max_w<THREADS / 32>(amax, red);
   const float s = quant_row_scale(amax);
   const float inv_s = quant_row_inv_scale(s);
   int8_t* qr = q + row * ldq;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int idx = threadIdx.x + i * kQThreads;
+    const int idx = threadIdx.x + i * THREADS;
     if (idx < nvec) {
       const float4 c0 = __ldg(cs4 + 2 * idx), c1 = __ldg(cs4 + 2 * idx + 1);
       const float f[8] = {__fmul_rn(bf16_lo(v[i].x), c0.x), __fmul_rn(bf16_hi(v[i].x), c0.y),
@@ -196,44 +215,71 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_colscaled_generic_kernel
   if (threadIdx.x == 0) scale[row] = s;
 }
 
-// wqT[k, n] = wq[n, k]: 64 (n) x 128 (k) tiles through shared memory, 16-byte
-// loads along k, 16-byte stores along n.
-constexpr int kTTN = 64;
-constexpr int kTTK = 128;
+// wqT[k, n] = wq[n, k] in 128 (n) x 128 (k) tiles, 256 threads. Each thread
+// loads 16 bytes along k from four consecutive rows (4 x 16 bytes), transposes
+// the 4 x 16 block in registers with byte permutes into 16 words of four
+// n-values, and stores them as 32-bit words to tile[k][n / 4] (a warp covers
+// one k row: 32 distinct banks). Then each quarter-warp copies one 128-byte
+// k row of the tile to wqT with 16-byte loads and stores.
+constexpr int kTT = 128;
 __global__ void __launch_bounds__(256) transpose_i8_kernel(const int8_t* __restrict__ wq,
                                                            int64_t ldw, int64_t n_rows,
                                                            int64_t k_cols,
                                                            int8_t* __restrict__ out, int64_t ldt,
                                                            bool vec_in, bool vec_out) {
-  __shared__ __align__(16) int8_t tile[kTTK][kTTN + 16];
-  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTTN;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kTTK;
-  for (int c = threadIdx.x; c < kTTN * (kTTK / 16); c += 256) {
-    const int r = c % kTTN, qd = c / kTTN;
-    const int64_t n = n0 + r;
-    const int64_t kb = k0 + qd * 16;
-    __align__(16) int8_t v[16];
+  __shared__ __align__(16) uint32_t tile[kTT][kTT / 4];
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTT;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kTT;
+  const int g = threadIdx.x & 31, b = threadIdx.x >> 5;  // rows 4g..4g+3, k 16b..16b+15
+  const int64_t kb = k0 + 16 * b;
+  uint32_t w[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t n = n0 + 4 * g + r;
     if (vec_in && n < n_rows && kb + 16 <= k_cols) {
-      *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(wq + n * ldw + kb));
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(wq + n * ldw + kb));
+      w[r][0] = v.x;
+      w[r][1] = v.y;
+      w[r][2] = v.z;
+      w[r][3] = v.w;
     } else {
-#pragma unroll
+      uint32_t t[4] = {0u, 0u, 0u, 0u};
       for (int j = 0; j < 16; ++j)
-        v[j] = (n < n_rows && kb + j < k_cols) ? wq[n * ldw + kb + j] : static_cast<int8_t>(0);
-    }
+        if (n < n_rows && kb + j < k_cols)
+          t[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(wq[n * ldw + kb + j]))
+                       << (8 * (j & 3));
 #pragma unroll
-    for (int j = 0; j < 16; ++j) tile[qd * 16 + j][r] = v[j];
+      for (int m = 0; m < 4; ++m) w[r][m] = t[m];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    // bytes e of rows 0..3 -> word (a_e, b_e, c_e, d_e), little-endian
+    const uint32_t ab_lo = __byte_perm(w[0][m], w[1][m], 0x5140);
+    const uint32_t ab_hi = __byte_perm(w[0][m], w[1][m], 0x7362);
+    const uint32_t cd_lo = __byte_perm(w[2][m], w[3][m], 0x5140);
+    const uint32_t cd_hi = __byte_perm(w[2][m], w[3][m], 0x7362);
+    const int row = 16 * b + 4 * m;
+    tile[row + 0][g] = __byte_perm(ab_lo, cd_lo, 0x5410);
+    tile[row + 1][g] = __byte_perm(ab_lo, cd_lo, 0x7632);
+    tile[row + 2][g] = __byte_perm(ab_hi, cd_hi, 0x5410);
+    tile[row + 3][g] = __byte_perm(ab_hi, cd_hi, 0x7632);
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < kTTK * (kTTN / 16); c += 256) {
-    const int r = c / (kTTN / 16), qd = c % (kTTN / 16);
-    const int64_t k = k0 + r;
-    const int64_t n = n0 + qd * 16;
+  const int c = threadIdx.x & 7;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int kl = (threadIdx.x >> 3) + 32 * i;
+    const int64_t k = k0 + kl;
+    const int64_t n = n0 + 16 * c;
     if (k >= k_cols || n >= n_rows) continue;
     int8_t* dst = out + k * ldt + n;
+    const uint4 v = *reinterpret_cast<const uint4*>(&tile[kl][4 * c]);
     if (vec_out && n + 16 <= n_rows) {
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[r][qd * 16]);
+      *reinterpret_cast<uint4*>(dst) = v;
     } else {
-      for (int j = 0; j < 16 && n + j < n_rows; ++j) dst[j] = tile[r][qd * 16 + j];
+      const uint8_t* bytes = reinterpret_cast<const uint8_t*>(&v);
+      for (int j = 0; j < 16 && n + j < n_rows; ++j) dst[j] = static_cast<int8_t>(bytes[j]);
     }
   }
 }
@@ -448,18 +494,19 @@ extern "C" int lema_quantize_rows_colscaled(const void* x_bf16, const float* cs,
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec_ok = cols > 0 && cols % 8 == 0 && aligned16(x) && (ldx * 2) % 16 == 0 &&
                       aligned16(cs) && (reinterpret_cast<uintptr_t>(q) % 8) == 0 && ldq % 8 == 0;
-  const int64_t per_thread = (cols / 8 + kQThreads - 1) / kQThreads;
+  const int64_t nvec = cols / 8;
   const dim3 grid(static_cast<unsigned>(rows));
   const int c = static_cast<int>(cols);
-  if (vec_ok && per_thread <= 16) {
-    if (per_thread <= 2)
-      quant_rows_colscaled_kernel<2><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
-    else if (per_thread <= 4)
-      quant_rows_colscaled_kernel<4><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
-    else if (per_thread <= 8)
-      quant_rows_colscaled_kernel<8><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
-    else
-      quant_rows_colscaled_kernel<16><<<grid, kQThreads, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  if (vec_ok && nvec <= 128 * 2) {
+    quant_rows_colscaled_kernel<128, 2><<<grid, 128, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  } else if (vec_ok && nvec <= 128 * 4) {
+    quant_rows_colscaled_kernel<128, 4><<<grid, 128, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  } else if (vec_ok && nvec <= 256 * 4) {
+    quant_rows_colscaled_kernel<256, 4><<<grid, 256, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  } else if (vec_ok && nvec <= 256 * 6) {
+    quant_rows_colscaled_kernel<256, 6><<<grid, 256, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
+  } else if (vec_ok && nvec <= 512 * 6) {
+    quant_rows_colscaled_kernel<512, 6><<<grid, 512, 0, s>>>(x, ldx, cs, c, q, ldq, scale);
   } else {
     quant_rows_colscaled_generic_kernel<<<grid, kQThreads, 0, s>>>(x, ldx, cs, cols, q, ldq,
                                                                     scale);
@@ -475,10 +522,9 @@ extern "C" int lema_transpose_i8(const int8_t* wq, int64_t ldw, int64_t N, int64
   if (N == 0 || K == 0) return LEMA_OK;
   if (wq == nullptr || wqT == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null pointer");
   if (ldw < K || ldt < N) return set_error(LEMA_ERR_INVALID_ARGUMENT, "ld too small");
-  if ((K + kTTK - 1) / kTTK > INT32_MAX || (N + kTTN - 1) / kTTN > 65535)
+  if ((K + kTT - 1) / kTT > INT32_MAX || (N + kTT - 1) / kTT > 65535)
     return set_error(LEMA_ERR_UNSUPPORTED, "matrix too large for the transpose grid");
-  dim3 grid(static_cast<unsigned>((K + kTTK - 1) / kTTK),
-            static_cast<unsigned>((N + kTTN - 1) / kTTN));
+  dim3 grid(static_cast<unsigned>((K + kTT - 1) / kTT), static_cast<unsigned>((N + kTT - 1) / kTT));
   const bool vec_in = aligned16(wq) && ldw % 16 == 0;
   const bool vec_out = aligned16(wqT) && ldt % 16 == 0;
   transpose_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(wq, ldw, N, K, wqT,

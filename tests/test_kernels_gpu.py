@@ -203,10 +203,12 @@ def test_dequant_transpose_and_dgrad(cuda_device, oracle, M, N, K):
 
 
 @pytest.mark.parametrize("shape", [(64, 4096), (7, 4100), (3, 11008), (5, 24576), (1, 8),
-                                   (300, 16), (0, 64)])
+                                   (300, 16), (0, 64), (9, 8192), (40, 22016), (2, 24584),
+                                   (600, 2048)])
 def test_quantize_rows_colscaled_bitexact(cuda_device, oracle, shape):
-    """Rows of fp32(x) * cs quantised: vector path (cols % 8 == 0, <= 16K), the
-    generic path (ragged or longer rows) and the empty case, all bit-exact."""
+    """Rows of fp32(x) * cs quantised: the vector paths (cols % 8 == 0, 128 to
+    512 threads per row up to 24576 columns), the generic path (ragged or longer
+    rows) and the empty case, all bit-exact."""
     x = rand_bf16(shape, seed=shape[0] * 3 + shape[1], outliers=False)
     g = torch.Generator().manual_seed(shape[1])
     cs = torch.rand(shape[1], generator=g) * 0.01 + 1e-4
@@ -220,7 +222,7 @@ def test_quantize_rows_colscaled_bitexact(cuda_device, oracle, shape):
 
 
 @pytest.mark.parametrize("N,K", [(4096, 4096), (11008, 4096), (4096, 11008), (37, 129),
-                                 (64, 128), (1, 5)])
+                                 (64, 128), (1, 5), (22016, 4096), (130, 260), (200, 33)])
 def test_transpose_i8_exact(cuda_device, N, K):
     g = torch.Generator(device=cuda_device).manual_seed(N + K)
     wq = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=cuda_device, generator=g)
