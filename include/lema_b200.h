@@ -174,6 +174,23 @@ LEMA_API int lema_w8a8_dgrad_int8(const void* dy_bf16, int64_t lddy, const int8_
                                   int8_t* wqT_ws, int64_t ldt, int8_t* dq_ws, int64_t ldq,
                                   float* sd_ws, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* ---- Selective full fine-tuning: fused optimizer step + re-quantisation ---- */
+/* One AdamW step of a trainable projection, in place (the reference's per-layer
+ * step, src/lema/_full_ft.py:204-229, each fp32 operation rounded once):
+ *   w = f32(w) * decay;  m = m * beta1 + g * c1;  v = v * beta2 + (g * g) * c2;
+ *   w = bf16_rne(w + step_size * (m / (sqrt(v) / sqrt_bc2 + eps)))
+ * with decay = 1 - lr*wd, c1 = 1 - beta1, c2 = 1 - beta2, sqrt_bc2 =
+ * sqrt(1 - beta2^t), step_size = -lr / (1 - beta1^t) (fp32 of the double
+ * values); then each row of the new bf16 weight is quantised by the
+ * lema_quantize_rows rule into q [rows, ldq] / scale [rows]; g is cleared when
+ * zero_grad. w bf16 [rows, ldw], g fp32 [rows, ldg], m and v fp32 [rows, ldmv]. */
+LEMA_API int lema_adamw_requant_rows(void* w_bf16, int64_t ldw, float* g, int64_t ldg, float* m,
+                                     float* v, int64_t ldmv, int64_t rows, int64_t cols,
+                                     float decay, float beta1, float c1, float beta2, float c2,
+                                     float sqrt_bc2, float step_size, float eps,
+                                     int32_t zero_grad, int8_t* q, int64_t ldq, float* scale,
+                                     void* stream);
+
 /* ---- Timing of the int8 GEMM launches ---------------------------------- */
 /* Starts recording a CUDA event pair around every int8 GEMM launch (dense and
  * grouped, on the current device, streams not being captured) up to

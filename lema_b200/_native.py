@@ -42,6 +42,9 @@ _SIGNATURES: dict[str, list] = {
     "lema_transpose_i8": [vp, i64, i64, i64, vp, i64, vp],
     "lema_w8a8_dgrad_int8": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, i64, i64,
                              vp],
+    "lema_adamw_requant_rows": [vp, i64, vp, i64, vp, vp, i64, i64, i64, C.c_float, C.c_float,
+                                C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
+                                C.c_float, i32, vp, i64, vp, vp],
     "lema_gemm_timer_start": [i64],
     "lema_gemm_timer_stop": [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i64),
                              C.POINTER(i64)],
@@ -134,6 +137,7 @@ KERNELS_PER_CALL = {
     "lema_quantize_rows_colscaled": 1, "lema_transpose_i8": 1, "lema_w8a8_dgrad_int8": 3,
     "lema_grouped_w8a8_dgrad": 2, "lema_rmsnorm_quant": 1, "lema_rmsnorm_bwd": 1,
     "lema_rope": 1, "lema_rope_qkv": 1, "lema_swiglu_quant": 1, "lema_swiglu_bwd": 1,
+    "lema_adamw_requant_rows": 1,
 }
 # Running count of this library's kernel launches issued by this process.
 kernel_launches = 0

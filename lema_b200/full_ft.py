@@ -25,8 +25,6 @@ the optimizer's PCIe round trips with the backward of the remaining layers.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 
 from . import ops
@@ -81,37 +79,29 @@ class SelectiveFullFT:
 
     @torch.no_grad()
     def step_layer(self, layer: int) -> None:
-        beta1, beta2, eps = 0.9, 0.999, 1e-8
+        """The reference's AdamW step (src/lema/_full_ft.py:204-229) of every
+        selected projection of ``layer``: weight and moments in from pinned RAM,
+        one fused kernel (``lema_adamw_requant_rows``: the AdamW arithmetic, the
+        per-output-channel int8 re-quantisation of the new weight, the cleared
+        accumulator), weight, moments and the int8 rows back to pinned RAM."""
         step = self.layer_steps.get(layer, 0) + 1
         self.layer_steps[layer] = step
-        b1 = 1 - beta1 ** step
-        b2 = 1 - beta2 ** step
         for name in self.modules:
             key = (layer, name)
             if key not in self.true:
                 continue
-            w = self.true[key].to(self.device, non_blocking=True).float()
-            g = self.acc[key]
+            w = self.true[key].to(self.device, non_blocking=True)
             m = self.m[key].to(self.device, non_blocking=True)
             v = self.v[key].to(self.device, non_blocking=True)
-            if self.wd:
-                w.mul_(1 - self.lr * self.wd)
-            m.mul_(beta1).add_(g, alpha=1 - beta1)
-            v.mul_(beta2).addcmul_(g, g, value=1 - beta2)
-            denom = v.sqrt().div_(math.sqrt(b2)).add_(eps)
-            w.addcdiv_(m, denom, value=-(self.lr / b1))
-            wb = w.to(torch.bfloat16)
-            # re-quantise the new weight into the layer's streamed int8 segment
-            wq, sw = ops.quantize_weight(wb)
+            wq, sw = ops.adamw_requant_rows(w, self.acc[key], m, v, step, self.lr, self.wd)
             ram = self.ws.ram[layer]
             # pinned destinations, copies ordered on this stream (the device
             # temporaries are freed only after them, stream-ordered)
             self.ws._view(ram, name + ".wq").copy_(wq, non_blocking=True)
             self.ws._view(ram, name + ".sw").copy_(sw, non_blocking=True)
-            self.true[key].copy_(wb, non_blocking=True)
+            self.true[key].copy_(w, non_blocking=True)
             self.m[key].copy_(m, non_blocking=True)
             self.v[key].copy_(v, non_blocking=True)
-            g.zero_()
 
     def step_layer_async(self, layer: int, reduce_entry=None, reducer=None) -> None:
         """Clips and steps ``layer`` on the side stream once the current stream's

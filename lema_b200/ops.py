@@ -18,6 +18,7 @@ on the current torch stream of the tensors' device.
 from __future__ import annotations
 
 import ctypes as C
+import math
 
 import torch
 
@@ -541,6 +542,52 @@ def swiglu_quant(gu: torch.Tensor, want_m: bool = False):
     N.call("lema_swiglu_quant", _ptr(gu), gu.stride(0), M, I, _ptr(mq), mq.stride(0), _ptr(sm),
            _ptr(m), I, _stream(dev))
     return mq, sm, m
+
+
+# ---------------------------------------------------------------------------
+# Selective full fine-tuning: fused AdamW step + re-quantisation
+# ---------------------------------------------------------------------------
+
+def adamw_coefficients(step: int, lr: float, wd: float, beta1: float = 0.9,
+                       beta2: float = 0.999, eps: float = 1e-8) -> tuple[float, ...]:
+    """The fp32 scalars of one AdamW step as the reference forms them
+    (src/lema/_full_ft.py:204-229; Python doubles rounded once to fp32):
+    (decay, beta1, c1, beta2, c2, sqrt_bc2, step_size, eps)."""
+    import numpy as np
+    b1 = 1 - beta1 ** step
+    b2 = 1 - beta2 ** step
+    f = np.float32
+    decay = f(1 - lr * wd) if wd else f(1.0)
+    return tuple(float(x) for x in (decay, f(beta1), f(1 - beta1), f(beta2), f(1 - beta2),
+                                    f(math.sqrt(b2)), f(-(lr / b1)), f(eps)))
+
+
+def adamw_requant_rows(w: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
+                       step: int, lr: float, wd: float, zero_grad: bool = True
+                       ) -> tuple[torch.Tensor, torch.Tensor]:
+    """One AdamW step of a [N, K] weight in place (w bf16, g / m / v fp32 on the
+    device; g cleared when ``zero_grad``) fused with the per-output-channel int8
+    quantisation of the new weight: returns (wq [N, K] view of [N, round_up(K, 16)],
+    sw [N])."""
+    dev = _require_cuda(w, g, m, v)
+    if w.dtype != torch.bfloat16 or g.dtype != torch.float32 or m.dtype != torch.float32 \
+            or v.dtype != torch.float32:
+        raise TypeError("adamw_requant_rows takes bf16 w and fp32 g, m, v")
+    for t in (w, g, m, v):
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError("2-D tensors with unit column stride required")
+    if m.stride(0) != v.stride(0) or not (w.shape == g.shape == m.shape == v.shape):
+        raise ValueError("w, g, m, v must have one shape (m and v one row stride)")
+    rows, cols = w.shape
+    ldq = pad_to(max(cols, 1), 16)
+    q = torch.empty(rows, ldq, dtype=torch.int8, device=dev)
+    if ldq > cols:
+        q[:, cols:].zero_()
+    sw = torch.empty(rows, dtype=torch.float32, device=dev)
+    N.call("lema_adamw_requant_rows", _ptr(w), _ld(w), _ptr(g), _ld(g), _ptr(m), _ptr(v),
+           _ld(m), rows, cols, *adamw_coefficients(step, lr, wd), int(zero_grad), _ptr(q), ldq,
+           _ptr(sw), _stream(dev))
+    return q[:, :cols], sw
 
 
 def swiglu_bwd(gu: torch.Tensor, dm: torch.Tensor) -> torch.Tensor:

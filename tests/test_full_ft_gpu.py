@@ -100,3 +100,35 @@ def test_full_ft_weight_gradient_is_dy_t_x(cuda_device):
     rel = (got - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt()
     assert rel < 1e-5, float(rel)
     tr.close()
+
+
+@pytest.mark.parametrize("shape,step,wd", [((64, 4096), 3, 0.01), ((37, 11008), 1, 0.01),
+                                           ((5, 100), 7, 0.0), ((3, 4104), 2, 0.1),
+                                           ((0, 64), 1, 0.01)])
+def test_fused_adamw_requant_bitexact(cuda_device, shape, step, wd):
+    """lema_adamw_requant_rows against the numpy restatement of the reference's
+    AdamW step (bit for bit: each fp32 operation rounded once in the same
+    order), the int8 rows against the quantisation contract of the new weight,
+    and the accumulator cleared. Vector path (cols % 8 == 0) and scalar path."""
+    from oracle import oracle as O
+    from oracle.torch_ref import adamw_step_ref
+    from lema_b200 import ops
+    g0 = torch.Generator().manual_seed(shape[1] + step)
+    w = (torch.randn(*shape, generator=g0) * 0.02).to(torch.bfloat16)
+    g = torch.randn(*shape, generator=g0) * 1e-3
+    m = torch.randn(*shape, generator=g0) * 1e-4
+    v = torch.rand(*shape, generator=g0) * 1e-6
+    lr = 1e-3
+    ref_w, ref_m, ref_v = adamw_step_ref(O.torch_bf16_to_bits(w), g.numpy(), m.numpy(),
+                                         v.numpy(), step, lr, wd)
+    dev = cuda_device
+    wd_, gd, md, vd = w.to(dev), g.to(dev), m.to(dev), v.to(dev)
+    wq, sw = ops.adamw_requant_rows(wd_, gd, md, vd, step, lr, wd)
+    np.testing.assert_array_equal(O.torch_bf16_to_bits(wd_.cpu()), ref_w)
+    np.testing.assert_array_equal(md.cpu().numpy(), ref_m)
+    np.testing.assert_array_equal(vd.cpu().numpy(), ref_v)
+    assert not gd.any()
+    if shape[0]:
+        wq_ref, sw_ref = O.c_quantize_rows(ref_w)
+        np.testing.assert_array_equal(wq.cpu().numpy(), wq_ref)
+        np.testing.assert_array_equal(sw.cpu().numpy(), sw_ref)
