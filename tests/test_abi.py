@@ -57,6 +57,39 @@ def test_argument_errors_do_not_touch_the_gpu():
     assert rc == N.LEMA_ERR_MISALIGNED
 
 
+def test_argument_errors_of_the_dgrad_optimizer_and_timer_entries():
+    """The int8-dy dgrad pieces, the fused AdamW step and the GEMM timer reject
+    bad arguments (and accept empty problems) before any CUDA call."""
+    lib = N.lib()
+    fake = 4096  # a non-null address that is never dereferenced
+    assert lib.lema_quantize_rows_colscaled(None, None, 4, 8, 8, None, 16, None,
+                                            None) == N.LEMA_ERR_INVALID_ARGUMENT
+    assert lib.lema_quantize_rows_colscaled(None, None, 0, 8, 8, None, 16, None, None) == 0
+    assert lib.lema_quantize_rows_colscaled(fake, fake, 4, 8, 4, fake, 16, fake,
+                                            None) == N.LEMA_ERR_INVALID_ARGUMENT  # ldx < cols
+    assert lib.lema_transpose_i8(None, 16, 4, 8, None, 16, None) == N.LEMA_ERR_INVALID_ARGUMENT
+    assert lib.lema_transpose_i8(None, 16, 0, 8, None, 16, None) == 0
+    assert lib.lema_transpose_i8(fake, 16, 40, 8, fake, 16, None) == N.LEMA_ERR_INVALID_ARGUMENT
+    rc = lib.lema_w8a8_dgrad_int8(None, 8, None, 16, None, None, 16, None, 8, None, 16, None,
+                                  4, 8, 16, None)
+    assert rc == N.LEMA_ERR_MISALIGNED  # ldt must be a multiple of 16
+    rc = lib.lema_w8a8_dgrad_int8(fake, 8, fake, 16, None, fake, 16, fake, 16, fake, 16, fake,
+                                  4, 8, 16, None)
+    assert rc == N.LEMA_ERR_INVALID_ARGUMENT and "scales" in N.last_error()
+    coef = (1.0, 0.9, 0.1, 0.999, 0.001, 0.03, -0.01, 1e-8)
+    assert lib.lema_adamw_requant_rows(None, 8, None, 8, None, None, 8, 0, 8, *coef, 1, None,
+                                       16, None, None) == 0
+    assert lib.lema_adamw_requant_rows(None, 8, None, 8, None, None, 8, 2, 8, *coef, 1, None,
+                                       16, None, None) == N.LEMA_ERR_INVALID_ARGUMENT
+    assert lib.lema_adamw_requant_rows(fake, 4, fake, 8, fake, fake, 8, 2, 8, *coef, 1, fake,
+                                       16, fake, None) == N.LEMA_ERR_INVALID_ARGUMENT
+    assert lib.lema_gemm_timer_start(0) == N.LEMA_ERR_INVALID_ARGUMENT
+    ops_, ms = C.c_double(-1.0), C.c_double(-1.0)
+    n, dropped = C.c_int64(-1), C.c_int64(-1)
+    assert lib.lema_gemm_timer_stop(C.byref(ops_), C.byref(ms), C.byref(n), C.byref(dropped)) == 0
+    assert (ops_.value, ms.value, n.value) == (0.0, 0.0, 0)
+
+
 class HostManager:
     """A host-only (device = -1) native manager: packing and the job pool."""
 
