@@ -427,7 +427,10 @@ def _offsets_array(offsets) -> tuple[C.Array, int]:
 def grouped_w8a8_dgrad(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
                        offsets: list[int]) -> torch.Tensor:
     """Per-expert straight-through dgrad: rows of expert e get dy . bf16(wq[e] * sw[e]).
-    dy [T, N] bf16 sorted by expert, wq [E, N, K] int8, sw [E, N]."""
+    dy [T, N] bf16 sorted by expert, wq [E, N, K] int8, sw [E, N]. The int8-dy
+    variant when ``set_dgrad_mode("int8")`` is in effect."""
+    if _DGRAD_MODE == "int8":
+        return grouped_w8a8_dgrad_int8(dy, wq, sw, offsets)
     dev = _require_cuda(dy, wq, sw)
     dy = _rows_view(dy.to(torch.bfloat16))
     E, Nn, K = wq.shape
@@ -443,6 +446,47 @@ def grouped_w8a8_dgrad(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
     N.call("lema_grouped_w8a8_dgrad", _ptr(dy), _ld(dy), _ptr(wq), wq.stride(1),
            _ptr(sw.contiguous().float()), _ptr(dx), K, _ptr(ws), ldt, offs, E, Nn, K,
            _stream(dev))
+    return dx
+
+
+def grouped_w8a8_dgrad_int8(dy: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                            offsets: list[int]) -> torch.Tensor:
+    """Per-expert int8-dy dgrad: the rows of expert e, dy * sw[e], quantised per
+    row (column-scaled quantiser), wq[e] transposed in int8, then one grouped int8
+    GEMM with unit column scales: dx ~ dy . (wq[e] * sw[e]). Experts without rows
+    are skipped."""
+    dev = _require_cuda(dy, wq, sw)
+    dy = _rows_view(dy.to(torch.bfloat16))
+    E, Nn, K = wq.shape
+    if wq.stride(2) != 1 or wq.stride(0) != Nn * wq.stride(1):
+        raise ValueError("expert weights must be stacked contiguously: [E, N, ldw]")
+    offs, E2 = _offsets_array(offsets)
+    if E2 != E:
+        raise ValueError("offsets must have E+1 entries")
+    bounds = [int(o) for o in offsets]
+    T = dy.shape[0]
+    ld = pad_to(max(Nn, 1), 16)
+    dq = torch.empty(T, ld, dtype=torch.int8, device=dev)
+    wqT = torch.empty(E, K, ld, dtype=torch.int8, device=dev)
+    if ld > Nn:
+        dq[:, Nn:].zero_()
+        wqT[:, :, Nn:].zero_()
+    sd = torch.empty(T, dtype=torch.float32, device=dev)
+    swc = sw.contiguous().float()
+    stream = _stream(dev)
+    lddy = _ld(dy)
+    for e in range(E):
+        r0, r1 = bounds[e], bounds[e + 1]
+        if r1 <= r0:
+            continue
+        N.call("lema_quantize_rows_colscaled", dy.data_ptr() + r0 * lddy * 2,
+               swc[e].data_ptr(), r1 - r0, Nn, lddy, dq.data_ptr() + r0 * ld, ld,
+               sd.data_ptr() + r0 * 4, stream)
+        N.call("lema_transpose_i8", wq[e].data_ptr(), wq.stride(1), Nn, K, wqT[e].data_ptr(), ld,
+               stream)
+    dx = torch.empty(T, K, dtype=torch.bfloat16, device=dev)
+    N.call("lema_grouped_w8a8_gemm", _ptr(dq), ld, _ptr(sd), _ptr(wqT), ld, None, None,
+           _ptr(dx), K, offs, E, K, Nn, stream)
     return dx
 
 

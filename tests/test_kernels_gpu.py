@@ -482,6 +482,35 @@ def test_grouped_dgrad_matches_oracle(cuda_device, oracle, monkeypatch, path):
         _dgrad_tol_check(bits(dx[r0:r1].contiguous()), ref)
 
 
+@pytest.mark.parametrize("E,N,K,counts", [(5, 640, 384, [300, 0, 129, 1, 200]),
+                                          (8, 4096, 1024, [512, 384, 0, 640, 128, 256, 64, 33])])
+def test_grouped_dgrad_int8_bitexact(cuda_device, oracle, E, N, K, counts):
+    """The int8-dy grouped dgrad: each expert's rows bit-exact against the oracle's
+    int8-dy chain with that expert's weight (empty and ragged experts included),
+    and through the mode switch of ``grouped_w8a8_dgrad``."""
+    dev = cuda_device
+    offsets = np.concatenate([[0], np.cumsum(counts)]).tolist()
+    T = offsets[-1]
+    w = rand_bf16((E * N, K), seed=61 + N, scale=0.02, outliers=False)
+    wq, sw = ops.quantize_rows(w.to(dev))
+    dy = rand_bf16((T, N), seed=62 + N, outliers=False)
+    wq3, sw2 = wq.reshape(E, N, K), sw.reshape(E, N)
+    dx = ops.grouped_w8a8_dgrad_int8(dy.to(dev), wq3, sw2, offsets)
+    wqn, swn = wq.cpu().numpy().reshape(E, N, K), sw.cpu().numpy().reshape(E, N)
+    for e in range(E):
+        r0, r1 = offsets[e], offsets[e + 1]
+        if r1 == r0:
+            continue
+        ref = oracle.dgrad_int8_ref(bits(dy[r0:r1].contiguous()), wqn[e], swn[e])
+        np.testing.assert_array_equal(bits(dx[r0:r1].contiguous()), ref["dx"], err_msg=str(e))
+    prev = ops.dgrad_mode()
+    ops.set_dgrad_mode("int8")
+    try:
+        assert torch.equal(ops.grouped_w8a8_dgrad(dy.to(dev), wq3, sw2, offsets), dx)
+    finally:
+        ops.set_dgrad_mode(prev)
+
+
 @pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (77, 300, 200)])
 def test_wgrad_fp32_accumulators(cuda_device, oracle, M, N, K):
     """dW = dy^T . x with fp32 output against a double-accumulated reference; the
