@@ -8,7 +8,7 @@
   stream while block i-1 computes; the block's W8A8 projections are bound to
   views of the slot (no parameter copy, unlike src/lema/adapters/_llama.py:
   95-100); the block's input is saved to a pinned host slot on a D2H stream
-  (reference keeps it in VRAM, :109-111);
+  (the reference keeps it in VRAM, :109-111, which ``ckpt_mode=2`` selects);
 * head + loss (reference :151-162): final RMSNorm, bf16 lm_head, shifted
   cross entropy, backward to the last hidden state;
 * backward in reverse (reference :125-173): the saved input is restored on the
@@ -40,7 +40,6 @@ import torch.nn.functional as F
 
 from . import ops
 from .llama import LlamaBlock, LlamaHead, LlamaShape, apply_lora, rope_cos_sin
-from .modules import LoRALinear
 from .tensorstore import ActivationCheckpointStore, WeightSegments
 
 
