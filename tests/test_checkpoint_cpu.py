@@ -96,3 +96,23 @@ def test_segment_file_round_trip_and_checks(tmp_path):
     save_file({"w": torch.ones(2)}, str(tmp_path / "plain.safetensors"))
     assert not ckp.is_segment_file(str(tmp_path / "plain.safetensors"))
     assert not ckp.is_segment_file(str(tmp_path))
+
+
+def test_corrupted_or_truncated_files_raise(tmp_path):
+    """A corrupted safetensors header and a truncated segment file surface as
+    Python exceptions (host-side fault injection); neither is taken for a
+    segment file."""
+    bad = tmp_path / "bad.safetensors"
+    bad.write_bytes(b"\xff" * 64)
+    assert not ckp.is_segment_file(str(bad))
+    with pytest.raises(Exception):
+        ckp.HFCheckpoint(str(bad))
+    shape = LlamaShape(hidden=64, heads=2, kv_heads=2, intermediate=96, vocab=32, layers=3)
+    good = str(tmp_path / "w8a8.safetensors")
+    ckp.save_segments(good, _fake_segments(1, shape), torch.zeros(32, 64), torch.ones(64),
+                      torch.zeros(32, 64))
+    data = open(good, "rb").read()
+    cut = tmp_path / "cut.safetensors"
+    cut.write_bytes(data[: len(data) // 2])
+    with pytest.raises(Exception):
+        ckp.load_segments(str(cut), _fake_segments(2, shape))
