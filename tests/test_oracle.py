@@ -147,3 +147,38 @@ def test_cfg1_inputs_seeded():
     assert torch.equal(x1.view(torch.int16), x2.view(torch.int16))
     assert torch.equal(w1.view(torch.int16), w2.view(torch.int16))
     assert x1.dtype == torch.bfloat16 and w1.shape == (16, 64) and not b1.any()
+
+
+def test_adamw_restatement_pinned_to_reference(oracle):
+    """tests/golden/full_ft_adamw.npz was written by tests/golden/make_golden_adamw.py
+    from the reference's own clip and AdamW step (src/lema/_full_ft.py:194-229).
+    The oracle's numpy restatement (which the fused kernel matches bit for bit)
+    reproduces each step from the reference's state: the clip norm to 1e-6, the
+    moments to 1e-6 relative (1e-10 absolute near zero), the bf16 weights to one
+    ulp, >= 99 % of them exactly (the reference's CPU torch ops may fuse a
+    multiply-add)."""
+    from oracle.torch_ref import adamw_step_ref
+    d = np.load(GOLDEN / "full_ft_adamw.npz")
+    names = sorted({k.split("/")[1] for k in d.files if k.startswith("w0/")})
+    w = {n: d[f"w0/{n}"] for n in names}
+    m = {n: np.zeros(d[f"g1/{n}"].shape, np.float32) for n in names}
+    v = {n: np.zeros(d[f"g1/{n}"].shape, np.float32) for n in names}
+    for step in (1, 2, 3):
+        g = {n: d[f"g{step}/{n}"].astype(np.float32) for n in names}
+        total = sum(float(np.sum(g[n].astype(np.float32) ** 2, dtype=np.float32)) for n in names)
+        ref_norm = float(d[f"norm{step}"])
+        assert abs(np.sqrt(total) - ref_norm) <= 1e-6 * ref_norm
+        if ref_norm > 1.0:
+            g = {n: (g[n] * np.float32(1.0 / ref_norm)).astype(np.float32) for n in names}
+        for n in names:
+            nw, nm, nv = adamw_step_ref(w[n], g[n], m[n], v[n], step, 1e-3, 0.01)
+            # one rounding apart where the reference's multiply-add is fused
+            np.testing.assert_allclose(nm, d[f"m{step}/{n}"], rtol=1e-6, atol=1e-10)
+            np.testing.assert_allclose(nv, d[f"v{step}/{n}"], rtol=1e-6, atol=1e-14)
+            ref_w = d[f"w{step}/{n}"]
+            gf, rf = oracle.bf16_bits_to_f32(nw), oracle.bf16_bits_to_f32(ref_w)
+            ulp = np.ldexp(np.float32(1.0), np.frexp(np.abs(rf))[1] - 8)
+            assert np.all(np.abs(gf - rf) <= ulp), n
+            assert np.mean(nw == ref_w) >= 0.99, (n, float(np.mean(nw == ref_w)))
+            # the next step starts from the reference's state
+            w[n], m[n], v[n] = ref_w, d[f"m{step}/{n}"], d[f"v{step}/{n}"]
