@@ -75,3 +75,57 @@ def test_chunked_attention_equals_full_attention():
     blk.self_attn.attn_chunk = 32
     chunked = blk(x, cos, sin)
     assert torch.allclose(full, chunked, atol=1e-6, rtol=1e-5)
+
+
+def test_oracle_model_reproduces_reference_trainer_step():
+    """tests/golden/llama_model_w8a8.npz was written by tests/golden/make_golden_model.py
+    from one LemaTrainer.train_step of the reference (2 Llama blocks with the oracle's
+    W8A8 linears, LoRA r4 on q/v, bf16, CPU). This build's embedding, blocks and head
+    with the same weights give the same logits, loss and LoRA gradients."""
+    import numpy as np
+    import torch.nn.functional as F
+    from pathlib import Path
+
+    from lema_b200.llama import LlamaHead, apply_lora
+    d = np.load(Path(__file__).parent / "golden" / "llama_model_w8a8.npz")
+    hidden, heads, inter, layers, vocab, seq, batch, rank, alpha = (int(v) for v in d["meta"])
+    shape = LlamaShape(hidden=hidden, heads=heads, kv_heads=heads, intermediate=inter,
+                       vocab=vocab, layers=layers)
+    ck = {k[len("ckpt/"):]: bf16(d[k]) for k in d.files if k.startswith("ckpt/")}
+    embed = torch.nn.Embedding(vocab, hidden, dtype=torch.bfloat16)
+    embed.weight.data.copy_(ck["model.embed_tokens.weight"])
+    head = LlamaHead(shape)
+    head.norm.weight.data.copy_(ck["model.norm.weight"])
+    head.lm_head.weight.data.copy_(ck["lm_head.weight"])
+    blocks, loras = [], []
+    for i in range(layers):
+        blk = LlamaBlock(shape, quantized=False)
+        p = f"model.layers.{i}."
+        blk.input_layernorm.weight.data.copy_(ck[p + "input_layernorm.weight"])
+        blk.post_attention_layernorm.weight.data.copy_(ck[p + "post_attention_layernorm.weight"])
+        for part, names in (("self_attn", ("q_proj", "k_proj", "v_proj", "o_proj")),
+                            ("mlp", ("gate_proj", "up_proj", "down_proj"))):
+            for n in names:
+                blk.base_projection(n).weight.data.copy_(ck[f"{p}{part}.{n}.weight"])
+        blk.self_attn.attn_impl = "eager"
+        swap_linears(blk)
+        params = {n: (torch.nn.Parameter(bf16(d[f"lora/{i + 1}.self_attn.{n}/A"]).clone()),
+                      torch.nn.Parameter(bf16(d[f"lora/{i + 1}.self_attn.{n}/B"]).clone()))
+                  for n in ("q_proj", "v_proj")}
+        apply_lora(blk, rank, alpha, targets=("q_proj", "v_proj"), params=params)
+        blocks.append(blk)
+        loras.append(params)
+    ids = torch.from_numpy(d["ids"])
+    cos, sin = rope_cos_sin(shape, seq, "cpu", torch.bfloat16)
+    h = embed(ids)
+    for blk in blocks:
+        h = blk(h, cos, sin)
+    logits = head(h)
+    loss = F.cross_entropy(logits[:, :-1].reshape(-1, vocab), ids[:, 1:].reshape(-1))
+    loss.backward()
+    assert (torch_bf16_to_bits(logits.detach()) == d["logits"]).all()
+    assert float(loss) == float(d["loss"])
+    for i, params in enumerate(loras):
+        for n, (a, b) in params.items():
+            assert (torch_bf16_to_bits(a.grad) == d[f"grad/{i + 1}.self_attn.{n}/A"]).all(), (i, n)
+            assert (torch_bf16_to_bits(b.grad) == d[f"grad/{i + 1}.self_attn.{n}/B"]).all(), (i, n)
