@@ -61,6 +61,16 @@ LEMA_API const char* lema_version(void);
  * error word (0 = no kernel recorded a failure). */
 LEMA_API int lema_device_error(int32_t* code_out);
 
+/* Enqueues on `stream` a one-thread kernel that moves the current device's
+ * error word into *host_word when it is nonzero, and clears it. host_word must
+ * be page-locked host memory mapped into the device (cudaHostAlloc, torch's
+ * pin_memory()). The host reads *host_word whenever it likes, with no sync: a
+ * trainer enqueues this at the end of each step and checks the word before
+ * each step, so a bounded wait that ran out stops training at the first step
+ * that starts after the failing step's kernels have run. (Replaces no
+ * reference interface: the reference has no device code.) */
+LEMA_API int lema_device_error_async(int32_t* host_word, void* stream);
+
 /* Number of SMs the kernels size their persistent grids for (current device). */
 LEMA_API int lema_num_sms(int32_t* out);
 
@@ -201,6 +211,20 @@ LEMA_API int lema_gemm_timer_start(int64_t max_records);
  * the launches not recorded (pool full, capturing stream, other device). */
 LEMA_API int lema_gemm_timer_stop(double* total_ops, double* total_ms, int64_t* launches,
                                   int64_t* dropped);
+
+/* ---- Stream-K workspace and test hooks --------------------------------- */
+/* Number of (device, stream) stream-K workspaces the library holds (each is
+ * one cudaMalloc of partial-accumulator slots and flags, made on the first
+ * GEMM on that stream whose plan splits a tile). */
+LEMA_API int lema_gemm_workspace_count(int64_t* count);
+/* Test hooks of the GEMMs' bounded waits; the defaults are what every other
+ * caller runs with. skip_publish != 0: split tiles' partial ranges are not
+ * published, so the owners' waits for them run out and record 0x104 in the
+ * device error word. wait_budget_cycles: clock64 cycles each bounded wait in
+ * the GEMM kernels may spin before it records its error and the kernel drains
+ * and returns; 0 restores the default (about 2 s). Applies to launches issued
+ * after the call, from any thread. */
+LEMA_API int lema_gemm_set_test_hooks(int32_t skip_publish, int64_t wait_budget_cycles);
 
 /* ---- Fused producers of the W8A8 GEMM inputs (and their backward) ------ */
 /* RMSNorm of HF LlamaRMSNorm as adapters/_llama.py:238,248 apply it, in bf16:

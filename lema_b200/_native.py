@@ -27,6 +27,9 @@ _SIGNATURES: dict[str, list] = {
     "lema_last_error": [],
     "lema_version": [],
     "lema_device_error": [C.POINTER(i32)],
+    "lema_device_error_async": [vp, vp],
+    "lema_gemm_workspace_count": [C.POINTER(i64)],
+    "lema_gemm_set_test_hooks": [i32, i64],
     "lema_num_sms": [C.POINTER(i32)],
     "lema_quantize_rows": [vp, i64, i64, i64, vp, i64, vp, vp],
     "lema_quantize_rows_f32": [vp, i64, i64, i64, vp, i64, vp, vp],
@@ -137,7 +140,7 @@ KERNELS_PER_CALL = {
     "lema_quantize_rows_colscaled": 1, "lema_transpose_i8": 1, "lema_w8a8_dgrad_int8": 3,
     "lema_grouped_w8a8_dgrad": 2, "lema_rmsnorm_quant": 1, "lema_rmsnorm_bwd": 1,
     "lema_rope": 1, "lema_rope_qkv": 1, "lema_swiglu_quant": 1, "lema_swiglu_bwd": 1,
-    "lema_adamw_requant_rows": 1,
+    "lema_adamw_requant_rows": 1, "lema_device_error_async": 1,
 }
 # Running count of this library's kernel launches issued by this process.
 kernel_launches = 0
@@ -174,3 +177,48 @@ def num_sms() -> int:
 
 def exported_symbols() -> list[str]:
     return list(_SIGNATURES)
+
+
+def gemm_workspace_count() -> int:
+    """(device, stream) stream-K workspaces the library has allocated."""
+    out = i64(0)
+    call("lema_gemm_workspace_count", C.byref(out))
+    return out.value
+
+
+def gemm_set_test_hooks(skip_publish: bool = False, wait_budget_cycles: int = 0) -> None:
+    """Test hooks of the GEMMs' bounded waits (0 cycles = the default budget)."""
+    call("lema_gemm_set_test_hooks", int(bool(skip_publish)), int(wait_budget_cycles))
+
+
+DEVICE_ERROR_NAMES = {
+    0x101: "a GEMM's TMA producer timed out waiting for a free stage",
+    0x102: "a GEMM's MMA issuer timed out waiting for operands or accumulators",
+    0x103: "a GEMM's epilogue timed out waiting for accumulators",
+    0x104: "a split GEMM tile's partial accumulators never arrived",
+}
+
+
+class DeviceErrorWatch:
+    """Watches the library's device error word across training steps without a
+    host synchronisation: ``arm(stream)`` enqueues a one-thread kernel that
+    moves a nonzero word into a pinned host int (``lema_device_error_async``);
+    ``check()`` reads that int on the host and raises ``LemaError`` when a
+    kernel recorded a failure (a bounded wait that ran out leaves a wrong
+    tile behind, so the step's results must not be used)."""
+
+    def __init__(self, host=None):
+        import torch
+        self.host = host if host is not None else torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def arm(self, stream) -> None:
+        call("lema_device_error_async", self.host.data_ptr(), stream)
+
+    def check(self) -> None:
+        code = int(self.host[0])
+        if code:
+            self.host[0] = 0
+            what = DEVICE_ERROR_NAMES.get(code, "a kernel recorded a device-side failure")
+            raise LemaError(LEMA_ERR_DEVICE,
+                            f"device error 0x{code:x}: {what}; the last step's results are "
+                            "invalid", "train_step")

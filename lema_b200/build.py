@@ -67,8 +67,6 @@ def _compile(src: Path, verbose: bool) -> Path:
     cmd = [_nvcc(), *ARCH_FLAGS, *COMMON_FLAGS]
     if verbose:
         cmd += ["-Xptxas", "-v"]
-    if src.suffix == ".cpp":
-        cmd += ["-x", "cu"] if False else []
     cmd += ["-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -18,14 +18,18 @@
 //               accumulator outputs and unaligned y), while the MMA warp already
 //               accumulates the next tile into the other TMEM buffer.
 //
-// Tiles are ordered m-fastest inside each group so concurrently running CTAs
-// share the B (weight) tile through L2. A "group" is a contiguous row range of
-// A that multiplies its own B matrix (MoE experts); the dense GEMM is one group.
-// When the last wave would fill at most half of the workers, its tiles are cut
-// into two K-halves (plan_split, WorkIter). Kernels are launched with
-// programmatic stream serialisation: their set-up overlaps the previous
-// kernel's tail and griddepcontrol.wait precedes every data read.
+// Tiles are ordered in panels of column tiles inside each group (decode_tile)
+// so concurrently running CTAs share A rows and B columns through L2. A
+// "group" is a contiguous row range of A that multiplies its own B matrix (MoE
+// experts); the dense GEMM is one group. When the tile count leaves the last
+// wave part-empty, a stream-K schedule gives every worker an equal range of
+// K-slices instead (plan_schedule, WorkIter): split tiles' partial
+// accumulators go through a per-stream workspace to the worker that owns the
+// tile. Kernels are launched with programmatic stream serialisation: their
+// set-up overlaps the previous kernel's tail and griddepcontrol.wait precedes
+// every data read.
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -65,15 +69,21 @@ struct GemmParams {
   int32_t* acc;                        // raw s32 accumulators or null (int8 kind)
   int64_t ldacc;
   int32_t* err;                        // device error word
-  // Split tail: tiles [0, dp_tiles) run whole, round-robin over the workers
-  // (CTAs, or CTA pairs); each of the last split_tiles tiles is cut into two
-  // K-halves run by two workers (see WorkIter).
-  int32_t dp_tiles;
-  int32_t split_tiles;
+  // Stream-K schedule (see WorkIter): tiles [0, sk_tiles) form a row of
+  // sk_tiles * num_kb K-slice units cut into sk_workers contiguous ranges, one
+  // per worker (CTA, or CTA pair) w < sk_workers, processed first; tiles
+  // [sk_tiles, total_tiles) then run whole, round-robin over all workers.
+  int32_t sk_tiles;
+  int32_t sk_workers;
   int32_t* ws;        // partial accumulators: one kSlotElems slot per CTA
-  int32_t* ws_flags;  // one publish flag per slot and epilogue warp
+  int32_t* ws_flags;  // per slot and epilogue warp: the epoch of its last publish
+  int32_t epoch;      // this launch's publish value (never 0; differs from the
+                      // previous launches on the same workspace)
+  int32_t raster;     // column tiles per raster panel (tile order, decode_tile)
   int32_t y_tma;      // y is written by TMA stores through the y tensor map
   int32_t total_rows; // rows of A (and of y)
+  int32_t skip_publish;  // test hook: partial ranges are not published
+  long long wait_budget; // clock64 cycles each bounded wait may spin
 };
 
 // A partial slot holds one CTA's 128 rows x 256 columns of 32-bit accumulators
@@ -87,42 +97,77 @@ enum WorkRole : int { kRoleWhole = 0, kRolePartial = 1, kRoleOwner = 2 };
 
 struct Work {
   int tile;
-  int kb0, kb1;  // K-slices [kb0, kb1) of the tile
+  int kb0, kb1;        // K-slices [kb0, kb1) of the tile
   int role;
-  int contrib;   // owner: the worker that computes the other K-half
+  int c_first, c_last; // owner: the workers holding the tile's other K-slices
 };
 
+// First stream-K unit of worker w: floor(w * U / S) for U units on S workers.
+__device__ __forceinline__ int64_t sk_start(int64_t w, int64_t units, int64_t workers) {
+  return w * units / workers;
+}
+
+// The worker whose stream-K range holds unit u: the largest w with
+// sk_start(w) <= u, i.e. floor(((u + 1) * S - 1) / U).
+__device__ __forceinline__ int sk_worker_of(int64_t u, int64_t units, int64_t workers) {
+  return static_cast<int>(((u + 1) * workers - 1) / units);
+}
+
 // The work list of one worker, identical in its producer, MMA and epilogue
-// roles: whole tiles worker, worker + W, ... < dp_tiles, then, for workers
-// w < 2 * split_tiles, one K-half of tail tile dp_tiles + w / 2: the first half
-// (even w) makes w the tile's owner, which adds the second half's partial
-// accumulators, published by worker w + 1, before writing the tile.
+// roles. Stream-K first: worker w < sk_workers walks its contiguous range of
+// the units of tiles [0, sk_tiles) in order. A range starting inside a tile
+// begins with a partial item (its accumulators go to the worker's slot and are
+// published); a range ending inside a tile ends with that tile's head, whose
+// worker owns the tile: it adds the partials of the later workers that hold
+// the rest of the tile and writes it. A partial is always its worker's first
+// item and an owned head its worker's last stream-K item, so no owner waits on
+// a worker that is itself waiting. Then whole tiles sk_tiles + w, + W, ...
 struct WorkIter {
-  int w, W;
+  int W;
+  int64_t u, u_end, units;
   int next_dp;
-  bool tail_done;
-  __device__ WorkIter(const GemmParams& p, int worker, int workers)
-      : w(worker), W(workers), next_dp(worker), tail_done(false) {}
+  __device__ WorkIter(const GemmParams& p, int worker, int workers) : W(workers) {
+    units = static_cast<int64_t>(p.sk_tiles) * p.num_kb;
+    if (worker < p.sk_workers) {
+      u = sk_start(worker, units, p.sk_workers);
+      u_end = sk_start(worker + 1, units, p.sk_workers);
+    } else {
+      u = u_end = 0;
+    }
+    next_dp = p.sk_tiles + worker;
+  }
   __device__ bool next(const GemmParams& p, Work& out) {
-    if (next_dp < p.dp_tiles) {
+    if (u < u_end) {
+      const int tile = static_cast<int>(u / p.num_kb);
+      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.num_kb;
+      const int64_t tile_u1 = tile_u0 + p.num_kb;
+      const int64_t stop = tile_u1 < u_end ? tile_u1 : u_end;
+      out.tile = tile;
+      out.kb0 = static_cast<int>(u - tile_u0);
+      out.kb1 = static_cast<int>(stop - tile_u0);
+      out.c_first = out.c_last = 0;
+      if (out.kb0 > 0) {
+        out.role = kRolePartial;
+      } else if (stop == tile_u1) {
+        out.role = kRoleWhole;
+      } else {
+        out.role = kRoleOwner;
+        out.c_first = sk_worker_of(stop, units, p.sk_workers);
+        out.c_last = sk_worker_of(tile_u1 - 1, units, p.sk_workers);
+      }
+      u = stop;
+      return true;
+    }
+    if (next_dp < p.total_tiles) {
       out.tile = next_dp;
       out.kb0 = 0;
       out.kb1 = p.num_kb;
       out.role = kRoleWhole;
-      out.contrib = 0;
+      out.c_first = out.c_last = 0;
       next_dp += W;
       return true;
     }
-    if (tail_done || w >= 2 * p.split_tiles) return false;
-    tail_done = true;
-    const int half = w & 1;
-    const int h = p.num_kb / 2;
-    out.tile = p.dp_tiles + w / 2;
-    out.kb0 = half ? h : 0;
-    out.kb1 = half ? p.num_kb : h;
-    out.role = half ? kRolePartial : kRoleOwner;
-    out.contrib = w + 1;
-    return true;
+    return false;
   }
 };
 
@@ -136,16 +181,19 @@ __device__ __forceinline__ void st_release_gpu(int32_t* ptr, int32_t v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
-// Bounded wait until a warp block's partial is published. Lane 0 polls and the
-// outcome is broadcast, so the whole warp takes the same branch (the
-// epilogue's tcgen05.ld needs the full warp); each lane then performs its own
-// acquire load before it reads the block.
-__device__ __forceinline__ bool warp_wait_published(const int32_t* flag, int lane) {
+// Bounded wait until a warp block's partial of this launch is published (its
+// flag holds this launch's epoch; a flag left by an earlier launch, aborted or
+// not, holds another value). Lane 0 polls and the outcome is broadcast, so the
+// whole warp takes the same branch (the epilogue's tcgen05.ld needs the full
+// warp); each lane then performs its own acquire load before it reads the
+// block.
+__device__ __forceinline__ bool warp_wait_published(const int32_t* flag, int32_t epoch,
+                                                    long long budget, int lane) {
   int ok = 1;
-  if (lane == 0 && ld_acquire_gpu(flag) == 0) {
+  if (lane == 0 && ld_acquire_gpu(flag) != epoch) {
     const long long t0 = clock64();
-    while (ld_acquire_gpu(flag) == 0) {
-      if (clock64() - t0 > ptx::kWaitBudgetCycles) {
+    while (ld_acquire_gpu(flag) != epoch) {
+      if (clock64() - t0 > budget) {
         ok = 0;
         break;
       }
@@ -169,7 +217,11 @@ __device__ __forceinline__ bool aborted(const int* abort_flag) {
 }
 
 // Linear tile index -> (group, first A row, end row of the group, column tile)
-// for tiles TM rows high.
+// for tiles TM rows high. Inside a group the tiles are ordered in panels of
+// p.raster column tiles: panel by panel, and inside a panel row tile by row
+// tile with the panel's column tiles fastest (the last panel may be narrower).
+// Workers running consecutive tiles then cover a compact block of rows and
+// columns, so the A rows and B columns they read stay in L2 between them.
 template <int TM>
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, int& row0,
                                             int& row_end, int& n_tile) {
@@ -178,8 +230,12 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, 
   const int local = t - p.tile_start[g];
   const int rows = p.row_start[g + 1] - p.row_start[g];
   const int m_tiles = (rows + TM - 1) / TM;
-  const int mt = local % m_tiles;
-  const int nt = local / m_tiles;
+  const int panel = local / (m_tiles * p.raster);
+  const int r = local - panel * m_tiles * p.raster;
+  const int rest = p.num_n_tiles - panel * p.raster;
+  const int width = rest < p.raster ? rest : p.raster;
+  const int mt = r / width;
+  const int nt = panel * p.raster + (r - mt * width);
   row0 = p.row_start[g] + mt * TM;
   row_end = p.row_start[g + 1];
   n_tile = nt;
@@ -205,16 +261,34 @@ constexpr int kEpiStageBytes = 2048;
 constexpr int kEpiSwOffset = 2 * kEpiStageBytes;
 constexpr int kEpiBiasOffset = kEpiSwOffset + 256 * 4;
 
-// v[j] += partial[j * 32] (the other K-half of a split tile, in shared memory).
+// Other workers' K-ranges of a tile this worker owns: `count` partial blocks in
+// the workspace, `stride` elements apart, each in the block layout (element
+// (row, col) of the warp's 32 x 256 block at col * 32 + row).
+struct Partials {
+  const int32_t* first;
+  int count;
+  int64_t stride;
+};
+
+// v[j] += partial[j * 32] for every partial block, in contributor order (exact
+// for s32; one fp32 add each for bf16). The blocks were written by other SMs:
+// the loads go to L2 (ld.global.cg), past this SM's L1.
 template <int KIND>
-__device__ __forceinline__ void add_partial(uint32_t (&v)[32], const int32_t* pc) {
+__device__ __forceinline__ void add_partials(uint32_t (&v)[32], const Partials& parts,
+                                             int64_t offset) {
+#pragma unroll 1
+  for (int i = 0; i < parts.count; ++i) {
+    const int32_t* pc = parts.first + i * parts.stride + offset;
+    int32_t add[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int32_t add = pc[j * 32];
-    if (KIND == kKindI8)
-      v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + add);
-    else
-      v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __int_as_float(add)));
+    for (int j = 0; j < 32; ++j) add[j] = __ldcg(pc + j * 32);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (KIND == kKindI8)
+        v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + add[j]);
+      else
+        v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __int_as_float(add[j])));
+    }
   }
 }
 
@@ -222,14 +296,13 @@ __device__ __forceinline__ void add_partial(uint32_t (&v)[32], const int32_t* pc
 // columns [col0, col0 + NCHUNK*32) of this warp's lane quarter. Row r of the
 // output is this thread's row (row lr of the CTA's 128); columns start at n0.
 // slot != null (a partial K-range): the raw accumulators go to this warp's
-// block of the slot and nothing else is written. part != null (the owner of a
-// split tile): the other K-half's accumulators, copied to shared memory in the
-// same block layout, are added first (exact for s32; one fp32 add for bf16).
+// block of the slot and nothing else is written. parts.count > 0 (the owner of
+// a split tile): the other workers' partial blocks are added first.
 template <int KIND, int NCHUNK>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem_row_base,
                                               uint32_t col0, int r, bool rvalid, int g, int n0,
                                               bool y_vec, bool acc_vec, int lane,
-                                              const int32_t* part, int32_t* slot) {
+                                              const Partials& parts, int32_t* slot) {
   float sxr = 0.f;
   if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
   // no column scales (sw null): every column scale is 1
@@ -250,7 +323,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
     }
     const int n = n0 + c * 32;
     if (!rvalid || n >= p.n) continue;
-    if (part != nullptr) add_partial<KIND>(v, part + c * 32 * 32 + lane);
+    if (parts.count > 0) add_partials<KIND>(v, parts, c * 32 * 32 + lane);
     const bool full_chunk = (n + 32) <= p.n;
     if (p.acc != nullptr) {  // raw accumulators: s32 (int8 kind) or fp32 bits (bf16 kind)
       int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
@@ -315,7 +388,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
                                              uint8_t* epi, uint32_t& store_count,
                                              uint32_t tmem_row_base, uint32_t col0, int r_base,
                                              int lane, bool rvalid, int g, int n0,
-                                             const int32_t* part) {
+                                             const Partials& parts) {
   float* sw_s = reinterpret_cast<float*>(epi + kEpiSwOffset);
   __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(epi + kEpiBiasOffset);
   const bool has_bias = p.bias != nullptr;
@@ -342,7 +415,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
     ptx::tmem_ld_wait();
     const int n = n0 + c * 32;
     if (n >= p.n) continue;  // uniform over the warp
-    if (part != nullptr) add_partial<KIND>(v, part + c * 32 * 32 + lane);
+    if (parts.count > 0) add_partials<KIND>(v, parts, c * 32 * 32 + lane);
     uint32_t packed[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -388,39 +461,34 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
 
 // Epilogue of one work item by one epilogue warp (CTAS = CTAs per worker,
 // quarter = the warp's 32-row block of the CTA's 128 rows). The owner of a
-// split tile first waits for the matching warp of the contributor to publish
-// its block, then copies the block into the CTA's operand ring (idle once the
-// tile's MMAs are done: a split half is every worker's last item) with
-// cp.async and adds it from there. Returns false when that wait ran out (the
-// error is recorded).
+// split tile first waits for the matching warp of every contributor to publish
+// its block of this launch, then adds the blocks while it converts the tile.
+// Returns false when such a wait ran out (the error is recorded).
 template <int KIND, int NCHUNK, int CTAS>
 __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w, int worker,
                                               int rank, const CUtensorMap* tmap_y, uint8_t* epi,
-                                              uint8_t* ring, uint32_t& store_count,
-                                              uint32_t tmem_row_base, uint32_t col0, int r_base,
-                                              int row_end, int g, int n0, bool y_vec,
-                                              bool acc_vec, int quarter, int lane,
-                                              int* abort_flag) {
+                                              uint32_t& store_count, uint32_t tmem_row_base,
+                                              uint32_t col0, int r_base, int row_end, int g,
+                                              int n0, bool y_vec, bool acc_vec, int quarter,
+                                              int lane, int* abort_flag) {
   if (r_base >= row_end) return true;  // no row of this warp is in the tile (owner and
-                                       // contributor agree: same tile, same rows)
+                                       // contributors agree: same tile, same rows)
   const int r = r_base + lane;
   const bool rvalid = r < row_end;
-  const int32_t* part = nullptr;
+  Partials parts{nullptr, 0, static_cast<int64_t>(CTAS) * kSlotElems};
   int32_t* slot = nullptr;
   if (w.role == kRoleOwner) {
-    const int cslot = w.contrib * CTAS + rank;
-    if (!warp_wait_published(p.ws_flags + cslot * 4 + quarter, lane)) {
-      record_error(p.err, kDevErrSplitTimeout, abort_flag);
-      return false;
+    for (int c = w.c_first; c <= w.c_last; ++c) {
+      const int cslot = c * CTAS + rank;
+      if (!warp_wait_published(p.ws_flags + cslot * 4 + quarter, p.epoch, p.wait_budget,
+                               lane)) {
+        record_error(p.err, kDevErrSplitTimeout, abort_flag);
+        return false;
+      }
     }
-    const int32_t* src =
-        p.ws + static_cast<int64_t>(cslot) * kSlotElems + quarter * kSlotWarpElems;
-    int32_t* dst = reinterpret_cast<int32_t*>(ring) + quarter * kSlotWarpElems;
-#pragma unroll 8
-    for (int i = lane; i < kSlotWarpElems / 4; i += 32) ptx::cp_async_16(dst + 4 * i, src + 4 * i);
-    ptx::cp_async_wait_all();
-    __syncwarp();
-    part = dst;
+    parts.first = p.ws + static_cast<int64_t>(w.c_first * CTAS + rank) * kSlotElems +
+                  quarter * kSlotWarpElems;
+    parts.count = w.c_last - w.c_first + 1;
   } else if (w.role == kRolePartial) {
     slot = p.ws + static_cast<int64_t>(worker * CTAS + rank) * kSlotElems +
            quarter * kSlotWarpElems;
@@ -431,28 +499,24 @@ __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w
                    (r_base + 32 <= row_end || row_end >= p.total_rows);
   if (tma)
     epilogue_tma<KIND, NCHUNK>(p, tmap_y, epi, store_count, tmem_row_base, col0, r_base, lane,
-                               rvalid, g, n0, part);
+                               rvalid, g, n0, parts);
   else
     epilogue_rows<KIND, NCHUNK>(p, tmem_row_base, col0, r, rvalid, g, n0, y_vec, acc_vec, lane,
-                                part, slot);
+                                parts, slot);
   return true;
 }
 
 // After the warp's part of a work item: a partial block is published (each
-// lane's stores made visible, then the warp's flag set); the owner clears the
-// flag it consumed, ready for the next launch.
+// lane's stores made visible, then the warp's flag set to this launch's
+// epoch). Owners leave the flags as they are: the next launch on the same
+// workspace publishes and waits for another epoch.
 template <int CTAS>
 __device__ __forceinline__ void epilogue_publish(const GemmParams& p, const Work& w, int worker,
                                                  int rank, int quarter, int lane, bool active) {
-  if (!active) return;
-  if (w.role == kRolePartial) {
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) st_release_gpu(p.ws_flags + (worker * CTAS + rank) * 4 + quarter, 1);
-  } else if (w.role == kRoleOwner) {
-    __syncwarp();
-    if (lane == 0) p.ws_flags[(w.contrib * CTAS + rank) * 4 + quarter] = 0;
-  }
+  if (!active || w.role != kRolePartial || p.skip_publish) return;
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(p.ws_flags + (worker * CTAS + rank) * 4 + quarter, p.epoch);
 }
 
 // ------------------------------ 1-SM kernel --------------------------------
@@ -526,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode_tile<kBM>(p, w.tile, g, row0, row_end, nt);
         const int b_row0 = g * p.n + nt * BN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.wait_budget)) {
             record_error(p.err, kDevErrProducerTimeout, abort_flag);
             break;
           }
@@ -546,7 +610,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Drain: the last (up to STAGES) issued loads must land before this
         // CTA's shared memory is released.
         for (int64_t i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
-          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
+          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1),
+                              p.wait_budget);
       }
     }
   } else if (warp == 1) {
@@ -560,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       WorkIter it(p, blockIdx.x, gridDim.x);
       Work w;
       while (!aborted(abort_flag) && it.next(p, w)) {
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.wait_budget)) {
           record_error(p.err, kDevErrMmaTimeout, abort_flag);
           break;
         }
@@ -568,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!ptx::mbar_wait(&full[stage], phase)) {
+          if (!ptx::mbar_wait(&full[stage], phase, p.wait_budget)) {
             record_error(p.err, kDevErrMmaTimeout, abort_flag);
             ok = false;
             break;
@@ -601,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (aborted(abort_flag) && issued_any) {
         // Drain outstanding MMAs before TMEM is released.
         ptx::mma_commit(&tmem_full[acc]);
-        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase);
+        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget);
       }
     }
   } else {
@@ -620,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (it.next(p, w)) {
       int g, row0, row_end, nt;
       decode_tile<kBM>(p, w.tile, g, row0, row_end, nt);
-      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
+      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
@@ -628,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int r_base = row0 + quarter * 32;
       const bool ok = epilogue_work<KIND, BN / 32, 1>(
-          p, w, blockIdx.x, 0, &tma_y, epi, smem, store_count,
+          p, w, blockIdx.x, 0, &tma_y, epi, store_count,
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
           static_cast<uint32_t>(acc * BN), r_base, row_end, g, nt * BN, y_vec, acc_vec, quarter,
           lane, abort_flag);
@@ -739,7 +804,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = row0 + static_cast<int>(rank) * 128;
         const int b_row = g * p.n + nt * kTN + static_cast<int>(rank) * 128;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.wait_budget)) {
             record_error(p.err, kDevErrProducerTimeout, abort_flag);
             break;
           }
@@ -760,7 +825,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The leader's full barriers count both CTAs' bytes: drain them before
         // either CTA can pass the final cluster barrier.
         for (int64_t i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
-          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
+          (void)ptx::mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1),
+                              p.wait_budget);
       }
     }
   } else if (warp == 1) {
@@ -774,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       WorkIter it(p, pair, npairs);
       Work w;
       while (!aborted(abort_flag) && it.next(p, w)) {
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.wait_budget)) {
           record_error(p.err, kDevErrMmaTimeout, abort_flag);
           break;
         }
@@ -782,7 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTN);
         bool ok = true;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!ptx::mbar_wait(&full[stage], phase)) {
+          if (!ptx::mbar_wait(&full[stage], phase, p.wait_budget)) {
             record_error(p.err, kDevErrMmaTimeout, abort_flag);
             ok = false;
             break;
@@ -814,7 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (aborted(abort_flag) && issued_any) {
         ptx::mma_commit_pair(&tmem_full[acc], 0x1);
-        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase);
+        (void)ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget);
       }
     }
   } else {
@@ -835,7 +901,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (it.next(p, w)) {
       int g, row0, row_end, nt;
       decode_tile<kTM>(p, w.tile, g, row0, row_end, nt);
-      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase)) {
+      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
@@ -843,7 +909,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int r_base = row0 + crank * 128 + quarter * 32;
       const bool ok = epilogue_work<KIND, kTN / 32, 2>(
-          p, w, pair, crank, &tma_y, epi, smem, store_count,
+          p, w, pair, crank, &tma_y, epi, store_count,
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
           static_cast<uint32_t>(acc * kTN), r_base, row_end, g, nt * kTN, y_vec, acc_vec,
           quarter, lane, abort_flag);
@@ -1022,13 +1088,18 @@ struct Groups {
   int64_t row_start[kMaxGroups + 1];
 };
 
-// ---- split tail: plan and per-stream workspace ----------------------------
+// ---- stream-K: plan and per-stream workspace -------------------------------
 
 thread_local bool t_no_split = false;
+
+// Test hooks (lema_gemm_set_test_hooks): read at every launch.
+std::atomic<int32_t> g_skip_publish{0};
+std::atomic<long long> g_wait_budget{ptx::kWaitBudgetCycles};
 
 struct SplitWorkspace {
   int32_t* slots = nullptr;
   int32_t* flags = nullptr;
+  int32_t epoch = 0;  // the last epoch handed to a launch on this workspace
   bool failed = false;
 };
 
@@ -1038,10 +1109,13 @@ constexpr size_t kMaxSplitWorkspaces = 8;  // (device, stream) pairs, 19 MB each
 
 // Partial slots for every CTA of a full grid (one per SM: 128 KB each) and
 // their publish flags, allocated once per (device, stream) so that GEMMs on
-// different streams never share them; GEMMs on one stream run in order. None
-// while this thread holds a ScopedNoGemmWorkspace, or while the stream is
-// being captured into a graph (a replay may run on another stream).
-bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags) {
+// different streams never share them; GEMMs on one stream run in order. Each
+// launch gets the workspace's next epoch, which its partials publish and its
+// owners wait for, so flags left by an earlier launch (finished or aborted)
+// never pass for this launch's. None while this thread holds a
+// ScopedNoGemmWorkspace, or while the stream is being captured into a graph (a
+// replay may run on another stream).
+bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags, int32_t* epoch) {
   if (t_no_split) return false;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
@@ -1075,29 +1149,61 @@ bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags) {
     w.slots = static_cast<int32_t*>(ptr);
     w.flags = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ptr) + slot_bytes);
   }
+  w.epoch = w.epoch == INT32_MAX ? 1 : w.epoch + 1;  // never 0, the flags' initial value
   *slots = w.slots;
   *flags = w.flags;
+  *epoch = w.epoch;
   return true;
 }
 
-// Whole tiles for floor(T / W) waves. When the remaining R tiles would occupy
-// at most half of the W workers, each is cut into two K-halves on two workers:
-// the last wave then takes half a tile-time plus the owner's fix-up (about
-// 2 us: publish, a 32 KB copy per epilogue warp, the add). Measured on B200
-// (interleaved A/B, 256 x 256 tiles): a gain from 64 K-slices of 128 B up
-// (int8 K = 11008: -6 %; bf16 K = 4096: -4 %, K = 11008: -10 %), a loss at 32
-// (int8 K = 4096: +4 %), so tiles with fewer than 64 slices run whole.
-// LEMA_GEMM_SPLIT=0 turns the split off, =1 forces it from 8 slices (tests).
-void plan_split(GemmParams& p, int workers) {
-  p.dp_tiles = p.total_tiles;
-  p.split_tiles = 0;
+// Stream-K plan. T tiles of KB K-slices (128 bytes of K each) on W workers:
+// whole tiles take ceil(T / W) waves, so when T is not a multiple of W the
+// last wave leaves workers idle. Stream-K instead gives every worker the same
+// number of K-slice units: with F = floor(T / W) >= 1 full waves, the first
+// (T mod W) + W tiles are cut into W contiguous unit ranges (each at least
+// one tile long, so a tile has at most two workers) and the other
+// (F - 1) * W tiles run whole; with F = 0, all T tiles are cut, over at most
+// one worker per kMinUnits units. Each split tile costs its owner a fix-up
+// (waiting for and adding the partials), mostly hidden behind the next
+// tile's MMAs because partials are every worker's first item; the plan is
+// used when its makespan, in K-slice times plus kFixupSlices, beats the waves.
+// LEMA_GEMM_SPLIT=0 turns stream-K off; =1 uses it whenever a tile count
+// allows it, down to one unit per worker (tests). Returns the workers to
+// launch.
+constexpr int kMinUnits = 8;
+constexpr int kFixupSlices = 4;
+
+int plan_schedule(GemmParams& p, int workers) {
+  p.sk_tiles = 0;
+  p.sk_workers = 0;
+  const int T = p.total_tiles;
+  const int W = workers;
   const char* env = std::getenv("LEMA_GEMM_SPLIT");
-  if (env != nullptr && std::strcmp(env, "0") == 0) return;
-  const int min_kb = (env != nullptr && std::strcmp(env, "1") == 0) ? 8 : 64;
-  const int rem = p.total_tiles % workers;
-  if (rem == 0 || 2 * rem > workers || p.num_kb < min_kb) return;
-  p.dp_tiles = p.total_tiles - rem;
-  p.split_tiles = rem;
+  const bool off = env != nullptr && std::strcmp(env, "0") == 0;
+  const bool forced = env != nullptr && std::strcmp(env, "1") == 0;
+  const int whole = std::min(T, W);
+  if (off || T % W == 0) return whole;
+  const int64_t KB = p.num_kb;
+  const int full = T / W;
+  const int sk_tiles = full >= 1 ? T % W + W : T;
+  const int64_t units = static_cast<int64_t>(sk_tiles) * KB;
+  const int64_t per = forced ? 1 : kMinUnits;
+  const int S = static_cast<int>(std::min<int64_t>(W, units / per));
+  if (S < 2) return whole;
+  const int64_t dp_cost = static_cast<int64_t>(full + 1) * KB;
+  const int64_t sk_cost =
+      static_cast<int64_t>(full >= 1 ? full - 1 : 0) * KB + (units + S - 1) / S + kFixupSlices;
+  if (!forced && sk_cost >= dp_cost) return whole;
+  p.sk_tiles = sk_tiles;
+  p.sk_workers = S;
+  return full >= 1 ? W : S;
+}
+
+// Column tiles per raster panel (decode_tile): LEMA_GEMM_RASTER=n overrides.
+int raster_width(int n_tiles) {
+  int r = 1;
+  if (const char* env = std::getenv("LEMA_GEMM_RASTER")) r = std::atoi(env);
+  return std::max(1, std::min(r, std::max(1, n_tiles)));
 }
 
 // Optional timing of the int8 GEMM launches (the bench's tensor roofline):
@@ -1231,18 +1337,21 @@ int run_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
   p.total_tiles = static_cast<int32_t>(tiles);
   if (tiles == 0) return LEMA_OK;
 
-  // Workers: resident CTA pairs or SMs. Split the last wave when it pays and a
-  // workspace is available; otherwise every tile runs whole.
+  // Workers: resident CTA pairs or SMs. Stream-K when it pays and a workspace
+  // is available; otherwise every tile runs whole.
   const int max_workers = path == kPathPair
                               ? (kind == kKindI8 ? pair_slots<kKindI8>() : pair_slots<kKindBF16>())
                               : device_sm_count();
   if (max_workers <= 0) return set_error(LEMA_ERR_CUDA, "cannot size the GEMM grid");
-  plan_split(p, max_workers);
-  if (p.split_tiles > 0 && !split_workspace(stream, &p.ws, &p.ws_flags)) {
-    p.dp_tiles = p.total_tiles;
-    p.split_tiles = 0;
+  p.raster = raster_width(p.num_n_tiles);
+  p.skip_publish = g_skip_publish.load();
+  p.wait_budget = g_wait_budget.load();
+  int workers = plan_schedule(p, max_workers);
+  if (p.sk_workers > 0 && !split_workspace(stream, &p.ws, &p.ws_flags, &p.epoch)) {
+    p.sk_tiles = 0;
+    p.sk_workers = 0;
+    workers = std::min(p.total_tiles, max_workers);
   }
-  const int workers = p.split_tiles > 0 ? max_workers : std::min(p.total_tiles, max_workers);
 
   const CUtensorMapDataType dt =
       (kind == kKindI8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -1307,6 +1416,13 @@ int k_zero_outputs(void* y, int64_t ldy, const void* bias, int32_t* acc, int64_t
   if (acc) fill_zero_i32_kernel<<<grid, 256, 0, s>>>(acc, ldacc, m, n);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
+}
+
+// Moves the error word into a host word (mapped pinned memory) when it is
+// nonzero, and clears it: the host reads the word later without a sync.
+__global__ void error_snapshot_kernel(int32_t* host_word) {
+  const int32_t v = atomicExch(&g_gemm_err, 0);
+  if (v != 0) *reinterpret_cast<volatile int32_t*>(host_word) = v;
 }
 
 }  // namespace
@@ -1478,5 +1594,40 @@ extern "C" int lema_gemm_timer_stop(double* total_ops, double* total_ms, int64_t
   if (launches) *launches = t.used;
   if (dropped) *dropped = t.dropped;
   t.used = 0;
+  return LEMA_OK;
+}
+
+extern "C" int lema_device_error_async(int32_t* host_word, void* stream) {
+  clear_error();
+  if (host_word == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null host_word");
+  cudaPointerAttributes attr;
+  LEMA_CUDA_TRY(cudaPointerGetAttributes(&attr, host_word));
+  if (attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT,
+                     "host_word must be page-locked host memory mapped into the device "
+                     "(cudaHostAlloc / pin_memory)");
+  error_snapshot_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<int32_t*>(attr.devicePointer));
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_gemm_set_test_hooks(int32_t skip_publish, int64_t wait_budget_cycles) {
+  clear_error();
+  if (wait_budget_cycles < 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "wait_budget_cycles must be >= 0");
+  g_skip_publish.store(skip_publish != 0 ? 1 : 0);
+  g_wait_budget.store(wait_budget_cycles == 0 ? ptx::kWaitBudgetCycles
+                                              : static_cast<long long>(wait_budget_cycles));
+  return LEMA_OK;
+}
+
+extern "C" int lema_gemm_workspace_count(int64_t* count) {
+  clear_error();
+  if (count == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null count");
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  int64_t n = 0;
+  for (const auto& kv : g_ws) n += kv.second.slots != nullptr ? 1 : 0;
+  *count = n;
   return LEMA_OK;
 }

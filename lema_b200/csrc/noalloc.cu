@@ -27,6 +27,7 @@
 //     no ordering between them) race on the arrays and must be serialised by
 //     the caller.
 //   * no cudaMalloc, cudaFree or allocating library routine is called.
+#include <algorithm>
 #include <mutex>
 
 #include "internal.h"
@@ -79,16 +80,23 @@ extern "C" int lema_w8a8_linear_fwd_noalloc(const void* x_bf16, int64_t ldx, con
                                             int64_t K, void* stream) {
   lema::clear_error();
   if (M < 0 || N < 0 || K < 0) return lema::set_error(LEMA_ERR_INVALID_ARGUMENT, "negative size");
-  const int64_t ldq = K > 0 ? (K + 15) / 16 * 16 : 16;
   if (M > kNoallocMaxRows)
     return lema::set_error(LEMA_ERR_UNSUPPORTED,
                            "lema_w8a8_linear_fwd_noalloc: M = " + std::to_string(M) +
                                " rows exceeds the fixed workspace limit of 65536 rows");
-  if (M * ldq > static_cast<int64_t>(kNoallocXqBytes))
+  // K is checked before it is rounded up, and the product is never formed, so
+  // no size can overflow past the check.
+  const int64_t limit = static_cast<int64_t>(kNoallocXqBytes);
+  if (K > limit)
     return lema::set_error(LEMA_ERR_UNSUPPORTED,
-                           "lema_w8a8_linear_fwd_noalloc: M * round_up(K, 16) = " +
-                               std::to_string(M * ldq) +
-                               " bytes exceeds the fixed 16 MiB activation workspace");
+                           "lema_w8a8_linear_fwd_noalloc: K = " + std::to_string(K) +
+                               " exceeds the fixed 16 MiB activation workspace");
+  const int64_t ldq = K > 0 ? (K + 15) / 16 * 16 : 16;
+  if (ldq > limit / std::max<int64_t>(M, 1))
+    return lema::set_error(LEMA_ERR_UNSUPPORTED,
+                           "lema_w8a8_linear_fwd_noalloc: M = " + std::to_string(M) +
+                               " rows of round_up(K, 16) = " + std::to_string(ldq) +
+                               " bytes exceed the fixed 16 MiB activation workspace");
   NoallocScratch s;
   int rc = noalloc_scratch(&s);
   if (rc) return rc;

@@ -191,6 +191,11 @@ class StreamedLoraTrainer:
                                               mode=ckpt_mode, h2d_stream=self.ws.h2d_stream)
         self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
         self.reducer = LoraGradReducer(group)
+        # device-side failures (a bounded wait in a kernel that ran out) are
+        # moved to pinned host memory at the end of each step and raised at the
+        # start of the first step after that step's kernels ran, without a sync
+        from ._native import DeviceErrorWatch
+        self.errors = DeviceErrorWatch()
         self.slot_layer = [-1] * self.nslots
         self.grad_accum = max(1, int(grad_accum))
         self.micro_step = 0
@@ -285,6 +290,7 @@ class StreamedLoraTrainer:
     def train_step(self, ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
         """One optimizer step on a [batch, seq] micro-batch of token ids (device or
         pinned host). Returns the loss as a 0-d device tensor."""
+        self.errors.check()
         dev = self.device
         ids = ids.to(dev, non_blocking=True)
         labels = ids if labels is None else labels.to(dev, non_blocking=True)
@@ -351,7 +357,13 @@ class StreamedLoraTrainer:
                     if b < len(self.resident):
                         self.resident[b].copy_(self.ws.ram[b])
             self.global_step += 1
+        self.errors.arm(torch.cuda.current_stream(dev).cuda_stream)
         return loss.detach()
+
+    def check_device_errors(self) -> None:
+        """Raises LemaError if a kernel of an earlier step recorded a failure
+        (the check ``train_step`` makes before each step)."""
+        self.errors.check()
 
     def close(self) -> None:
         self.ws.close()

@@ -113,6 +113,40 @@ class OracleExperts(nn.Module):
         return final
 
 
+def chunked_causal_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                 scale: float, chunk: int) -> torch.Tensor:
+    """The reference's chunked causal attention as its RoPE adapters drive it
+    (src/lema/adapters/_chunked_rope.py:63-117 calling
+    src/lema/_tensorstore.py:565-608), restated: K and V expanded to every
+    query head (GQA); for query chunk c, the fp32 scores against key chunks
+    0..c are concatenated along the key axis and scaled, keys after the query
+    position are set to finfo(fp32).min, the softmax runs in fp32 as max, exp,
+    sum and divide, the weights multiply the concatenated V in fp32 and the
+    result is cast to q's dtype. q [B, H, S, D], k/v [B, Hkv, S, D]."""
+    rep = q.shape[1] // k.shape[1]
+    if rep > 1:
+        k = k.repeat_interleave(rep, dim=1)
+        v = v.repeat_interleave(rep, dim=1)
+    S = q.shape[2]
+    outs = []
+    for s in range(0, S, chunk):
+        e = min(s + chunk, S)
+        qf = q[:, :, s:e].float()
+        parts = [qf @ k[:, :, c0:min(c0 + chunk, S)].float().transpose(-2, -1)
+                 for c0 in range(0, e, chunk)]
+        scores = torch.cat(parts, dim=-1) * scale
+        q_pos = torch.arange(s, e, device=q.device)
+        k_pos = torch.arange(0, scores.shape[-1], device=q.device)
+        masked = (q_pos[:, None] < k_pos[None, :])[None, None]
+        scores = torch.where(masked, torch.full_like(scores, torch.finfo(scores.dtype).min),
+                             scores)
+        m = scores.max(dim=-1, keepdim=True).values
+        p = (scores - m).exp()
+        p = p / p.sum(dim=-1, keepdim=True)
+        outs.append((p @ v[:, :, :e].float()).to(q.dtype))
+    return torch.cat(outs, dim=2)
+
+
 def adamw_step_ref(w_bf16: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray, step: int,
                    lr: float, wd: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """numpy fp32 restatement of the reference's per-layer AdamW

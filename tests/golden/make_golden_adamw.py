@@ -2,7 +2,7 @@
 
 Run from the repo root in a checkout that has the reference source next to it:
 
-    python tests/golden/make_golden_adamw.py /root/reference/src
+    python tests/golden/make_golden_adamw.py <reference>/src
 
 It runs the reference's per-layer clip and AdamW step of selective full
 fine-tuning (``FullFTManager.clip_grad_norm_`` and ``step_layer``,
@@ -72,4 +72,6 @@ def main(ref_src: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden_adamw.py <reference>/src")
+    main(sys.argv[1])

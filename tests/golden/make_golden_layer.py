@@ -2,7 +2,7 @@
 
 Run from the repo root in a checkout that has the reference source next to it:
 
-    python tests/golden/make_golden_layer.py /root/reference/src
+    python tests/golden/make_golden_layer.py <reference>/src
 
 It builds one Llama decoder layer with the reference's adapter
 (``LlamaAdapter.construct_layer_module``, src/lema/adapters/_llama.py:59-107)
@@ -76,4 +76,6 @@ def main(ref_src: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden_layer.py <reference>/src")
+    main(sys.argv[1])

@@ -2,7 +2,7 @@
 
 Run from the repo root in a checkout that has the reference source next to it:
 
-    python tests/golden/make_golden_model.py /root/reference/src
+    python tests/golden/make_golden_model.py <reference>/src
 
 It saves a tiny random Llama checkpoint (2 blocks, hidden 128, 4 heads x 32,
 MLP 352, vocab 256) as safetensors, builds the reference's ``LemaModel`` over it
@@ -141,4 +141,6 @@ def main(ref_src: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden_model.py <reference>/src")
+    main(sys.argv[1])

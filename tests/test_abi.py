@@ -173,3 +173,17 @@ def test_manager_prefetch_jobs_and_bounded_wait():
         assert done.value == 1
     finally:
         mm.close()
+
+
+def test_noalloc_size_checks_cannot_overflow():
+    """The allocation-free forward rejects sizes past its fixed workspace before
+    forming any product of them, so a huge K cannot wrap around the check."""
+    lib = N.lib()
+    huge = (1 << 63) - 3
+    for M, K in ((1, huge), (2, huge), (1, (1 << 24) + 1), (65536, 512)):
+        rc = lib.lema_w8a8_linear_fwd_noalloc(None, 16, None, 16, None, None, None, 16,
+                                              M, 16, K, None)
+        assert rc == N.LEMA_ERR_UNSUPPORTED and "16 MiB" in N.last_error(), (M, K)
+    rc = lib.lema_w8a8_linear_fwd_noalloc(None, 16, None, 16, None, None, None, 16,
+                                          65537, 16, 16, None)
+    assert rc == N.LEMA_ERR_UNSUPPORTED and "65536" in N.last_error()

@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 import torch
 
+from lema_b200 import _native
 from lema_b200 import ops
 
 pytestmark = pytest.mark.gpu
@@ -377,21 +378,26 @@ def test_bf16_gemm_tile_paths(cuda_device, oracle, monkeypatch, path):
     _dgrad_tol_check(bits(y), ref)
 
 
-# Split tail: when the last wave of tiles would occupy at most half of the
-# workers, each of its tiles is cut into two K-halves on two workers; the
-# second half's s32 sums are published to a per-stream workspace and added by
-# the tile's owner.
-SPLIT_CASES = [("pair", 768, 1024, 4096),     # 12 tiles halved over 24 of 74 pairs
-               ("pair", 300, 520, 8208),      # ragged M, N; 65 K-slices: halves 32 + 33
+# Stream-K: when the tile count leaves the last wave part-empty, every worker
+# gets an equal range of K-slices; a tile cut across workers is finished by its
+# owner (the worker holding its first slices), which adds the other workers'
+# s32 partials published through a per-stream workspace. LEMA_GEMM_SPLIT=1
+# forces the plan down to one K-slice per worker, so a tile can have many
+# contributors.
+SPLIT_CASES = [("pair", 768, 1024, 4096),     # 12 tiles over 74 pairs: 6-7 workers a tile
+               ("pair", 300, 520, 8208),      # ragged M, N; 65 K-slices per tile
+               ("pair", 512, 1024, 4096),     # 8 tiles, ~9 workers each
                ("1sm256", 384, 1024, 16384),  # 12 tiles over 148 CTAs
                ("1sm128", 333, 600, 11008),
-               ("pair", 4096, 4096, 4096)]    # 3 whole waves, then 34 tiles halved
+               ("1sm128", 128, 256, 2048),    # 2 tiles of 16 slices: 16 one-slice workers each
+               ("pair", 4096, 4096, 4096)]    # 2 whole waves, then 108 tiles over 74 ranges
 
 
+@pytest.mark.parametrize("raster", ["1", "8"])
 @pytest.mark.parametrize("path,M,N,K", SPLIT_CASES)
-def test_gemm_split_tail_bitexact(cuda_device, oracle, monkeypatch, path, M, N, K):
+def test_gemm_stream_k_bitexact(cuda_device, oracle, monkeypatch, path, M, N, K, raster):
     monkeypatch.setenv("LEMA_GEMM_TILE", path)
-    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")  # split from 8 K-slices up
+    monkeypatch.setenv("LEMA_GEMM_RASTER", raster)
     dev = cuda_device
     g = torch.Generator(device=dev).manual_seed(M * 7 + K)
     a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
@@ -401,7 +407,7 @@ def test_gemm_split_tail_bitexact(cuda_device, oracle, monkeypatch, path, M, N, 
     monkeypatch.setenv("LEMA_GEMM_SPLIT", "0")
     y_whole = ops.w8a8_gemm(a, sx, b, sw)
     monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")
-    for _ in range(2):  # the second launch reuses the workspace and its reset flags
+    for _ in range(2):  # the second launch reuses the workspace under a new epoch
         y, acc = ops.w8a8_gemm(a, sx, b, sw, want_acc=True)
         y2 = ops.w8a8_gemm(a, sx, b, sw)  # TMA-store epilogue (no raw accumulator output)
         assert torch.equal(y2.view(torch.int16), y_whole.view(torch.int16))
@@ -417,6 +423,56 @@ def test_gemm_split_tail_bitexact(cuda_device, oracle, monkeypatch, path, M, N, 
         yref = oracle.c_epilogue(acc.cpu().numpy(), sx.cpu().numpy(), sw.cpu().numpy(), None)
         np.testing.assert_array_equal(bits(y), yref)
         np.testing.assert_array_equal(bits(y2), yref)
+
+
+def test_gemm_stream_k_default_plan_bitexact(cuda_device, oracle, monkeypatch):
+    """The default plan (no forcing) at the training shapes: q/k/v stacked
+    (12288 columns), o (4096) and down (K = 11008), against the whole-tile
+    schedule, bit for bit."""
+    monkeypatch.delenv("LEMA_GEMM_SPLIT", raising=False)
+    monkeypatch.delenv("LEMA_GEMM_TILE", raising=False)
+    dev = cuda_device
+    for M, N, K in ((4096, 12288, 4096), (4096, 4096, 4096), (4096, 4096, 11008)):
+        g = torch.Generator(device=dev).manual_seed(N + K)
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        sx = torch.rand(M, device=dev, generator=g) * 0.01 + 1e-4
+        sw = torch.rand(N, device=dev, generator=g) * 1e-3 + 1e-5
+        y = ops.w8a8_gemm(a, sx, b, sw)
+        monkeypatch.setenv("LEMA_GEMM_SPLIT", "0")
+        y_whole = ops.w8a8_gemm(a, sx, b, sw)
+        monkeypatch.delenv("LEMA_GEMM_SPLIT")
+        assert torch.equal(y.view(torch.int16), y_whole.view(torch.int16)), (M, N, K)
+
+
+def test_gemm_stream_k_wait_timeout_records_error_and_recovers(cuda_device, oracle,
+                                                               monkeypatch):
+    """The abort path of the bounded waits: with the test hook that withholds
+    every partial's publish and a wait budget of about 1 ms, each owner's wait
+    for its contributors runs out; the kernel records 0x104 in the error word,
+    drains, frees its TMEM and returns, and the next GEMM on the same stream
+    and workspace is bit-exact."""
+    monkeypatch.setenv("LEMA_GEMM_TILE", "pair")
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")
+    dev = cuda_device
+    M, N_, K = 768, 1024, 4096  # 12 tiles cut over 74 pairs: every tile has contributors
+    g = torch.Generator(device=dev).manual_seed(77)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (N_, K), dtype=torch.int8, device=dev, generator=g)
+    sx = torch.rand(M, device=dev, generator=g) * 0.01 + 1e-4
+    sw = torch.rand(N_, device=dev, generator=g) * 1e-3 + 1e-5
+    assert _native.device_error() == 0
+    _native.gemm_set_test_hooks(skip_publish=True, wait_budget_cycles=2_000_000)
+    try:
+        ops.w8a8_gemm(a, sx, b, sw)
+        torch.cuda.synchronize()
+    finally:
+        _native.gemm_set_test_hooks(False, 0)
+    assert _native.device_error() == 0x104
+    y, acc = ops.w8a8_gemm(a, sx, b, sw, want_acc=True)
+    np.testing.assert_array_equal(acc.cpu().numpy(),
+                                  oracle.c_int8_gemm(a.cpu().numpy(), b.cpu().numpy()))
+    assert _native.device_error() == 0
 
 
 def test_bf16_gemm_split_tail_deterministic(cuda_device, oracle, monkeypatch):

@@ -8,6 +8,7 @@
    path (tests/golden/make_golden_layer.py) bit for bit: outputs, input
    gradient and LoRA gradients.
 """
+import pytest
 import torch
 from transformers.models.llama.modeling_llama import LlamaConfig, LlamaDecoderLayer
 
@@ -129,3 +130,20 @@ def test_oracle_model_reproduces_reference_trainer_step():
         for n, (a, b) in params.items():
             assert (torch_bf16_to_bits(a.grad) == d[f"grad/{i + 1}.self_attn.{n}/A"]).all(), (i, n)
             assert (torch_bf16_to_bits(b.grad) == d[f"grad/{i + 1}.self_attn.{n}/B"]).all(), (i, n)
+
+
+@pytest.mark.parametrize("case", ["ragged", "one_chunk"])
+def test_chunked_attention_oracle_reproduces_reference(case):
+    """tests/golden/chunked_attention.npz holds the output of the reference's own
+    chunked_attention (src/lema/_tensorstore.py:565-608) over query chunks as its
+    RoPE adapter drives it; the oracle's restatement gives the same bits."""
+    import numpy as np
+    from pathlib import Path
+
+    from oracle.torch_ref import chunked_causal_attention_ref
+    d = np.load(Path(__file__).parent / "golden" / "chunked_attention.npz")
+    B, H, Hkv, S, D, chunk = (int(v) for v in d[f"{case}/meta"])
+    q, k, v = (bf16(d[f"{case}/{n}"]) for n in ("q", "k", "v"))
+    assert q.shape == (B, H, S, D) and k.shape == (B, Hkv, S, D)
+    o = chunked_causal_attention_ref(q, k, v, D ** -0.5, chunk)
+    assert (torch_bf16_to_bits(o) == d[f"{case}/o"]).all()

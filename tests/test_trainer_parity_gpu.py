@@ -1,0 +1,245 @@
+"""The streamed trainer on the sm_100a kernels against the reference's trainer,
+and config 4's training path (512-token chunked causal attention, selective
+full fine-tuning of q/k/v/o in the last layer) against the CPU oracle.
+
+1. tests/golden/llama_model_w8a8.npz holds one ``LemaTrainer.train_step`` of
+   the reference (src/lema/_trainer.py:75-194) on a 2-block Llama with the
+   oracle's W8A8 linears in every projection, LoRA r4 alpha 8 on q/v, bf16,
+   CPU, eager attention. The checkpoint in the fixture is loaded into
+   ``StreamedLoraTrainer(weights=...)`` (segments quantised on the device),
+   the fixture's LoRA parameters are bound, and one step runs over the
+   fixture's token ids: the loss and all eight LoRA gradients are compared.
+   Two device paths: the fused block path with flash SDPA, and the
+   per-projection path with the reference's eager attention.
+2. A 3-block Llama with 128-wide heads at seq 1024, chunked attention in
+   512-token query chunks, q/k/v/o of the last block fully fine-tuned: the
+   trainer's loss and fp32 weight gradients (dW = dy^T x) against a CPU
+   model with the oracle's W8A8 linears and the oracle's restatement of the
+   reference's chunked attention (src/lema/_tensorstore.py:565-608 as driven
+   by src/lema/adapters/_chunked_rope.py:63-117); then the AdamW step and
+   re-quantisation against the restatement of the reference's step
+   (src/lema/_full_ft.py:204-229) applied to the trainer's own gradients.
+
+Tolerances. The int8 values and s32 accumulators of every projection are
+bit-exact against the oracle (tests/test_kernels_gpu.py); what differs here
+is the order of floating-point reductions (RMSNorm, attention, the bf16 LoRA
+matmuls, the fp32 dgrad accumulation), which moves a quantiser input by an
+ulp now and then and so one int8 step. The bars, stated per quantity as
+relative RMS error (and max-abs error over the reference's RMS):
+  loss (a bf16 value, as in the reference): |d| <= one bf16 ulp of the loss;
+  LoRA gradients: 1e-2 (eager attention, per-projection path) and
+  2.5e-2 (flash SDPA, fused path); max-abs <= 0.25 * RMS;
+  selective-FT weight gradients: 1e-2; max-abs <= 0.25 * RMS.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from lema_b200.llama import LlamaShape
+from lema_b200.trainer import StreamedLoraTrainer
+
+from layer_fixture import bf16
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN_MODEL = "golden/llama_model_w8a8.npz"
+
+
+def rel_err(dev_t, ref_t):
+    a = dev_t.detach().float().cpu()
+    b = ref_t.detach().float().cpu()
+    rms = b.pow(2).mean().sqrt().item() + 1e-30
+    err = a - b
+    return err.pow(2).mean().sqrt().item() / rms, err.abs().max().item() / rms
+
+
+def bf16_ulp(x: float) -> float:
+    return float(np.ldexp(1.0, int(np.frexp(abs(x))[1]) - 8))
+
+
+def close(dev_t, ref_t, rel_rms, max_rel, what):
+    rel, mx = rel_err(dev_t, ref_t)
+    print(f"[parity] {what}: rel-rms {rel:.3e} max/rms {mx:.3e}")
+    assert rel <= rel_rms and mx <= max_rel, f"{what}: rel-rms {rel:.3e} max/rms {mx:.3e}"
+
+
+def _write_hf(tmp_path, tensors: dict[str, torch.Tensor]) -> str:
+    from safetensors.torch import save_file
+    d = tmp_path / "hf"
+    d.mkdir()
+    save_file({k: v.contiguous() for k, v in tensors.items()}, str(d / "model.safetensors"))
+    return str(d)
+
+
+@pytest.mark.parametrize("attn", ["eager", "sdpa"])
+def test_streamed_trainer_matches_reference_trainer_step(cuda_device, tmp_path, attn):
+    from pathlib import Path
+    dev = cuda_device
+    d = np.load(Path(__file__).parent / GOLDEN_MODEL)
+    hidden, heads, inter, layers, vocab, seq, batch, rank, alpha = (int(v) for v in d["meta"])
+    shape = LlamaShape(hidden=hidden, heads=heads, kv_heads=heads, intermediate=inter,
+                       vocab=vocab, layers=layers)
+    ck = {k[len("ckpt/"):]: bf16(d[k]) for k in d.files if k.startswith("ckpt/")}
+    # grad_accum=2: the first micro-step leaves the optimizer alone, so the LoRA
+    # gradients of loss / 2 (exactly half of the reference's) are still there
+    tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=rank, lora_alpha=alpha,
+                             targets=("q_proj", "v_proj"), grad_accum=2,
+                             weights=_write_hf(tmp_path, ck))
+    for blk in tr.blocks:
+        blk.self_attn.attn_impl = attn
+    with torch.no_grad():
+        for i in range(layers):
+            for n in ("q_proj", "v_proj"):
+                a, b = tr.lora[i][n]
+                a.copy_(bf16(d[f"lora/{i + 1}.self_attn.{n}/A"]).to(dev))
+                b.copy_(bf16(d[f"lora/{i + 1}.self_attn.{n}/B"]).to(dev))
+    ids = torch.from_numpy(d["ids"]).to(dev)
+    loss = float(tr.train_step(ids))
+    torch.cuda.synchronize()
+    ref_loss = float(d["loss"])
+    print(f"[parity] {attn} loss {loss:.6f} reference {ref_loss:.6f}")
+    assert abs(loss - ref_loss) <= bf16_ulp(ref_loss), (loss, ref_loss)
+    bar = 1e-2 if attn == "eager" else 2.5e-2
+    for i in range(layers):
+        for n in ("q_proj", "v_proj"):
+            a, b = tr.lora[i][n]
+            for which, p in (("A", a), ("B", b)):
+                close(2.0 * p.grad, bf16(d[f"grad/{i + 1}.self_attn.{n}/{which}"]), bar, 0.25,
+                      f"{attn} layer {i} {n} d{which}")
+    tr.close()
+
+
+CFG4 = LlamaShape(hidden=256, heads=2, kv_heads=2, intermediate=512, vocab=512, layers=3)
+FT_MODULES = ("q_proj", "k_proj", "v_proj", "o_proj")
+
+
+def _cfg4_checkpoint(seed: int) -> dict[str, torch.Tensor]:
+    sh = CFG4
+    g = torch.Generator().manual_seed(seed)
+    sd = {"model.embed_tokens.weight": 0.5 * torch.randn(sh.vocab, sh.hidden, generator=g),
+          "model.norm.weight": 1.0 + 0.1 * torch.randn(sh.hidden, generator=g),
+          "lm_head.weight": 0.05 * torch.randn(sh.vocab, sh.hidden, generator=g)}
+    for i in range(sh.layers):
+        p = f"model.layers.{i}"
+        sd[f"{p}.input_layernorm.weight"] = 1.0 + 0.1 * torch.randn(sh.hidden, generator=g)
+        sd[f"{p}.post_attention_layernorm.weight"] = 1.0 + 0.1 * torch.randn(sh.hidden, generator=g)
+        for n, (o, k) in sh.proj_shapes().items():
+            part = "self_attn" if n in FT_MODULES else "mlp"
+            sd[f"{p}.{part}.{n}.weight"] = 0.06 * torch.randn(o, k, generator=g)
+    return {k: v.to(torch.bfloat16) for k, v in sd.items()}
+
+
+def _cfg4_oracle(ck, ids, chunk):
+    """CPU model: bf16 embedding, LlamaBlocks with the oracle's W8A8 linears and
+    the oracle's chunked attention, bf16 head, shifted cross entropy. Returns the
+    loss and dW = dy^T x (fp32 from the bf16 operands) of q/k/v/o of the last
+    block."""
+    from unittest import mock
+
+    from lema_b200 import llama as LL
+    from lema_b200.llama import LlamaBlock, LlamaHead, rope_cos_sin
+    from oracle.torch_ref import chunked_causal_attention_ref, swap_linears
+
+    sh = CFG4
+    embed = torch.nn.Embedding(sh.vocab, sh.hidden, dtype=torch.bfloat16)
+    embed.weight.data.copy_(ck["model.embed_tokens.weight"])
+    head = LlamaHead(sh)
+    head.norm.weight.data.copy_(ck["model.norm.weight"])
+    head.lm_head.weight.data.copy_(ck["lm_head.weight"])
+    blocks = []
+    for i in range(sh.layers):
+        blk = LlamaBlock(sh, quantized=False)
+        p = f"model.layers.{i}."
+        blk.input_layernorm.weight.data.copy_(ck[p + "input_layernorm.weight"])
+        blk.post_attention_layernorm.weight.data.copy_(ck[p + "post_attention_layernorm.weight"])
+        for n in sh.proj_shapes():
+            part = "self_attn" if n in FT_MODULES else "mlp"
+            blk.base_projection(n).weight.data.copy_(ck[f"{p}{part}.{n}.weight"])
+        swap_linears(blk)
+        blk.self_attn.attn_chunk = chunk
+        for prm in blk.parameters():
+            prm.requires_grad_(False)
+        blocks.append(blk)
+    saved = {}
+
+    def keep(name):
+        def hook(mod, inp, out):
+            x = inp[0]
+            out.register_hook(lambda gy: saved.__setitem__(name, (x.detach(), gy.detach())))
+        return hook
+    last = blocks[-1]
+    for n in FT_MODULES:
+        last.base_projection(n).register_forward_hook(keep(n))
+
+    def attn(q, k, v, scale, c, gqa):
+        return chunked_causal_attention_ref(q, k, v, scale, c)
+    cos, sin = rope_cos_sin(sh, ids.shape[1], "cpu", torch.bfloat16)
+    with mock.patch.object(LL, "_chunked_causal_attention", attn):
+        h = embed(ids).requires_grad_(True)
+        for blk in blocks:
+            h = blk(h, cos, sin)
+        logits = head(h)
+        loss = F.cross_entropy(logits[:, :-1].reshape(-1, sh.vocab), ids[:, 1:].reshape(-1))
+        loss.backward()
+    dw = {}
+    for n, (x, gy) in saved.items():
+        x2 = x.reshape(-1, x.shape[-1]).float()
+        g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16).float()
+        dw[n] = g2.t() @ x2
+    return float(loss.detach()), dw
+
+
+def test_cfg4_chunked_attention_selective_ft_step_matches_oracle(cuda_device, tmp_path):
+    from oracle import oracle as O
+    from oracle.torch_ref import adamw_step_ref
+    dev = cuda_device
+    sh = CFG4
+    seq, chunk, lr, wd = 1024, 512, 1e-3, 0.01
+    last = sh.layers - 1
+    ck = _cfg4_checkpoint(seed=41)
+    ids = torch.randint(0, sh.vocab, (1, seq), generator=torch.Generator().manual_seed(42))
+    tr = StreamedLoraTrainer(sh, dev, batch=1, seq=seq, targets=(), lr=lr, weight_decay=wd,
+                             attn_chunk=chunk, full_ft_layers=(last,),
+                             full_ft_modules=FT_MODULES, weights=_write_hf(tmp_path, ck))
+    ft = tr.full_ft
+    before = {k: O.torch_bf16_to_bits(w).copy() for k, w in ft.true.items()}
+    grads, clipped = {}, {}
+    orig_clip, orig_step = ft.clip_layer_, ft.step_layer
+
+    def capture_clip(layer, max_norm=1.0):  # the accumulated dW, before the clip
+        for n in ft.modules:
+            grads[(layer, n)] = ft.acc[(layer, n)].detach().cpu().clone()
+        return orig_clip(layer, max_norm)
+
+    def capture_step(layer):  # what the AdamW step consumes
+        for n in ft.modules:
+            clipped[(layer, n)] = ft.acc[(layer, n)].detach().cpu().clone()
+        return orig_step(layer)
+    ft.clip_layer_, ft.step_layer = capture_clip, capture_step
+    loss = float(tr.train_step(ids.to(dev)))
+    torch.cuda.synchronize()
+
+    ref_loss, ref_dw = _cfg4_oracle(ck, ids, chunk)
+    print(f"[parity] cfg4 loss {loss:.6f} oracle {ref_loss:.6f}")
+    assert abs(loss - ref_loss) <= bf16_ulp(ref_loss), (loss, ref_loss)
+    for n in FT_MODULES:
+        g = grads[(last, n)]
+        assert g.abs().max() > 0, n
+        close(g, ref_dw[n], 1e-2, 0.25, f"cfg4 dW {n}")
+    # the step applied to the trainer's own gradients: the restatement of the
+    # reference's AdamW (one bf16 ulp, as in the selective-FT tests), and the
+    # segment rows re-quantised from the new weights by the K1 rule
+    for (layer, n), w0 in before.items():
+        g = clipped[(layer, n)].numpy()
+        ref_w, _, _ = adamw_step_ref(w0, g, np.zeros_like(g), np.zeros_like(g), 1, lr, wd)
+        got = O.torch_bf16_to_bits(ft.true[(layer, n)])
+        gf, rf = O.bf16_bits_to_f32(got), O.bf16_bits_to_f32(ref_w)
+        ulp = np.ldexp(np.float32(1.0), np.frexp(np.abs(rf))[1] - 8)
+        bound = np.maximum(ulp, np.float32(2.0 ** -20 * lr))
+        assert (np.abs(gf - rf) - bound).max() <= 0, n
+        wq_ref, sw_ref = O.c_quantize_rows(got)
+        ram = tr.ws.ram[layer]
+        assert np.array_equal(tr.ws._view(ram, n + ".wq").numpy(), wq_ref), n
+        assert np.array_equal(tr.ws._view(ram, n + ".sw").numpy(), sw_ref), n
+    tr.close()

@@ -80,3 +80,38 @@ def test_noalloc_rejects_oversized_requests(cuda_device):
         N.call("lema_w8a8_linear_fwd_noalloc", None, 16, wq.data_ptr(), 16, sw.data_ptr(),
                None, y.data_ptr(), 16, 65537, 16, 16, None)
     assert e.value.code == N.LEMA_ERR_UNSUPPORTED and "65536" in str(e.value)
+
+
+def test_noalloc_never_allocates_a_stream_k_workspace(cuda_device, monkeypatch):
+    """With stream-K forced (LEMA_GEMM_SPLIT=1, every shape whose tile count
+    leaves a part-empty wave is cut), the allocating forward would create a
+    per-stream workspace on its first GEMM on a stream; the allocation-free
+    entry point runs every tile whole instead. On a fresh stream, after the
+    library's module is loaded (the fixed arrays are part of it), a call leaves
+    the workspace count and the device's free memory unchanged, and its output
+    is still bit-identical to the allocating forward's."""
+    dev = cuda_device
+    monkeypatch.setenv("LEMA_GEMM_SPLIT", "1")
+    M, N_, K = 768, 1024, 4096  # 12 tiles of 256 x 256: the forced plan would split them
+    x, w, bias = _inputs(M, N_, K, 3, dev)
+    wq, sw = ops.quantize_weight(w)
+    _noalloc(x, wq, sw, bias)  # module load and symbol lookup happen here at the latest
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        y = torch.empty(M, N_, dtype=torch.bfloat16, device=dev)
+        torch.cuda.synchronize()
+        before_ws = N.gemm_workspace_count()
+        free_before, _ = torch.cuda.mem_get_info()
+        for _ in range(2):
+            N.call("lema_w8a8_linear_fwd_noalloc", x.data_ptr(), x.stride(0), wq.data_ptr(),
+                   wq.stride(0), sw.data_ptr(), bias.data_ptr(), y.data_ptr(), N_, M, N_, K,
+                   s.cuda_stream)
+        s.synchronize()
+        free_after, _ = torch.cuda.mem_get_info()
+        assert N.gemm_workspace_count() == before_ws
+        assert free_after == free_before
+        y_ref = _allocating(x, wq, sw, bias)  # this one may create the stream's workspace
+        s.synchronize()
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    assert N.device_error() == 0
