@@ -49,7 +49,14 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kRowBytes = 128;  // K bytes per stage row (one 128B swizzle atom row)
 constexpr int kMaxGroups = 64;
-constexpr int kThreads = 192;
+// Warps: 0 = TMA producer, 1 = MMA issuer and TMEM owner, then the epilogue
+// warps: 4 in the 1-SM kernel (one per TMEM lane quarter), 8 in the pair kernel
+// (two per lane quarter, each converting half of the tile's columns, so the
+// last tile's epilogue, which nothing overlaps, takes half as long).
+constexpr int kEpiWarps1 = 4;
+constexpr int kEpiWarpsPair = 8;
+constexpr int kMaxEpiWarps = 8;  // publish flags per workspace slot
+constexpr int threads_for(int epi_warps) { return 64 + 32 * epi_warps; }
 
 enum GemmKind : int { kKindI8 = 0, kKindBF16 = 1 };
 
@@ -87,9 +94,11 @@ struct GemmParams {
 };
 
 // A partial slot holds one CTA's 128 rows x 256 columns of 32-bit accumulators
-// as four 32 KB blocks, one per epilogue warp (32 rows each); inside a block,
-// element (row, col) sits at col * 32 + row, so the warp's lanes store and the
-// owner's lanes read consecutive words.
+// as four 32 KB blocks, one per TMEM lane quarter (32 rows each). Inside a
+// block, element (row, col) of 32-column chunk c = col / 32 sits at
+// c * 1024 + ((col % 32) / 4) * 128 + row * 4 + col % 4: each lane (row) moves
+// four columns with one 16-byte access, and the 32 lanes of a warp together
+// cover 512 contiguous bytes.
 constexpr int kSlotElems = 128 * 256;
 constexpr int kSlotWarpElems = 32 * 256;
 
@@ -241,47 +250,57 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t, int& g, 
   n_tile = nt;
 }
 
-template <int BN, int STAGES>
+// BROWS: B rows a CTA loads per stage; EPI: epilogue warps; ECOLS: output
+// columns one epilogue warp converts per tile.
+template <int BROWS, int STAGES, int EPI, int ECOLS>
 struct SmemLayout {
   static constexpr int kABytes = kBM * kRowBytes;
-  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kBBytes = BROWS * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   // full[S], empty[S], tmem_full[2], tmem_empty[2], then tmem addr + abort flag
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   // Per epilogue warp: two 2 KB staging buffers for TMA stores (32 rows x 64 B,
-  // 64-byte swizzle, 1024-byte aligned), the tile's 256 column scales (fp32) and
-  // 256 biases (bf16).
+  // 64-byte swizzle, 1024-byte aligned), then the warp's ECOLS column scales
+  // (fp32) and biases (bf16) of the current tile.
   static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 1023) / 1024 * 1024;
-  static constexpr int kEpiWarpBytes = 6144;
-  static constexpr int kTotal = kEpiOffset + 4 * kEpiWarpBytes + 1024;  // + alignment slack
+  static constexpr int kEpiSwOffset = 4096;
+  static constexpr int kEpiBiasOffset = kEpiSwOffset + ECOLS * 4;
+  static constexpr int kEpiWarpBytes = (kEpiBiasOffset + ECOLS * 2 + 1023) / 1024 * 1024;
+  static constexpr int kTotal = kEpiOffset + EPI * kEpiWarpBytes + 1024;  // + alignment slack
+  static_assert(kTotal <= 227 * 1024, "shared memory per CTA");
 };
 
 constexpr int kEpiStageBytes = 2048;
-constexpr int kEpiSwOffset = 2 * kEpiStageBytes;
-constexpr int kEpiBiasOffset = kEpiSwOffset + 256 * 4;
 
 // Other workers' K-ranges of a tile this worker owns: `count` partial blocks in
-// the workspace, `stride` elements apart, each in the block layout (element
-// (row, col) of the warp's 32 x 256 block at col * 32 + row).
+// the workspace, `stride` elements apart, each in the block layout above.
 struct Partials {
   const int32_t* first;
   int count;
   int64_t stride;
 };
 
-// v[j] += partial[j * 32] for every partial block, in contributor order (exact
-// for s32; one fp32 add each for bf16). The blocks were written by other SMs:
-// the loads go to L2 (ld.global.cg), past this SM's L1.
+// v[j] += the partials' column j of this lane's row in chunk `chunk`, for every
+// partial block, in contributor order (exact for s32; one fp32 add each for
+// bf16). The blocks were written by other SMs: the loads go to L2
+// (ld.global.cg), past this SM's L1.
 template <int KIND>
 __device__ __forceinline__ void add_partials(uint32_t (&v)[32], const Partials& parts,
-                                             int64_t offset) {
+                                             int chunk, int lane) {
 #pragma unroll 1
   for (int i = 0; i < parts.count; ++i) {
-    const int32_t* pc = parts.first + i * parts.stride + offset;
+    const int4* pc = reinterpret_cast<const int4*>(parts.first + i * parts.stride +
+                                                   chunk * 1024 + lane * 4);
     int32_t add[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) add[j] = __ldcg(pc + j * 32);
+    for (int q = 0; q < 8; ++q) {
+      const int4 a = __ldcg(pc + q * 32);
+      add[4 * q] = a.x;
+      add[4 * q + 1] = a.y;
+      add[4 * q + 2] = a.z;
+      add[4 * q + 3] = a.w;
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (KIND == kKindI8)
@@ -292,16 +311,17 @@ __device__ __forceinline__ void add_partials(uint32_t (&v)[32], const Partials& 
   }
 }
 
-// Epilogue of one 128-row x (NCHUNK*32)-column accumulator block held in TMEM
-// columns [col0, col0 + NCHUNK*32) of this warp's lane quarter. Row r of the
-// output is this thread's row (row lr of the CTA's 128); columns start at n0.
-// slot != null (a partial K-range): the raw accumulators go to this warp's
-// block of the slot and nothing else is written. parts.count > 0 (the owner of
-// a split tile): the other workers' partial blocks are added first.
+// Epilogue of one warp's 32 rows x (NCHUNK*32) columns of accumulators held in
+// TMEM columns [col0, col0 + NCHUNK*32) of the warp's lane quarter. Row r of
+// the output is this thread's row; columns start at n0. Chunk c of the warp is
+// chunk chunk_base + c of the quarter's 32 x 256 partial block. slot != null
+// (a partial K-range): the raw accumulators go to the warp's chunks of the slot
+// block and nothing else is written. parts.count > 0 (the owner of a split
+// tile): the other workers' partial chunks are added first.
 template <int KIND, int NCHUNK>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem_row_base,
                                               uint32_t col0, int r, bool rvalid, int g, int n0,
-                                              bool y_vec, bool acc_vec, int lane,
+                                              int chunk_base, bool y_vec, bool acc_vec, int lane,
                                               const Partials& parts, int32_t* slot) {
   float sxr = 0.f;
   if (KIND == kKindI8 && rvalid && p.sx != nullptr) sxr = p.sx[r];
@@ -316,14 +336,17 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
     ptx::tmem_ld_32x32b_x32(tmem_row_base + col0 + static_cast<uint32_t>(c * 32), v);
     ptx::tmem_ld_wait();
     if (slot != nullptr) {
-      int32_t* sc = slot + c * 32 * 32 + lane;
+      int4* sc = reinterpret_cast<int4*>(slot + (chunk_base + c) * 1024 + lane * 4);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sc[j * 32] = static_cast<int32_t>(v[j]);
+      for (int q = 0; q < 8; ++q)
+        sc[q * 32] = make_int4(static_cast<int32_t>(v[4 * q]), static_cast<int32_t>(v[4 * q + 1]),
+                               static_cast<int32_t>(v[4 * q + 2]),
+                               static_cast<int32_t>(v[4 * q + 3]));
       continue;
     }
     const int n = n0 + c * 32;
     if (!rvalid || n >= p.n) continue;
-    if (parts.count > 0) add_partials<KIND>(v, parts, c * 32 * 32 + lane);
+    if (parts.count > 0) add_partials<KIND>(v, parts, chunk_base + c, lane);
     const bool full_chunk = (n + 32) <= p.n;
     if (p.acc != nullptr) {  // raw accumulators: s32 (int8 kind) or fp32 bits (bf16 kind)
       int32_t* arow = p.acc + static_cast<int64_t>(r) * p.ldacc + n;
@@ -373,40 +396,46 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tmem
   }
 }
 
+// Stages one epilogue warp's ECOLS column scales (fp32; 1 without column
+// scales) and biases (bf16) of a tile, from column n0 on, into its shared
+// memory: issued before the warp waits for the tile's accumulators, so the
+// global loads overlap the tile's MMAs. Columns >= n get zeros.
+template <int KIND, int ECOLS>
+__device__ __forceinline__ void stage_scales(const GemmParams& p, float* sw_s,
+                                             __nv_bfloat16* bias_s, int g, int n0, int lane) {
+  __syncwarp();  // every lane is done with the previous tile's scales
+#pragma unroll
+  for (int j = 0; j < ECOLS / 32; ++j) {
+    const int c = lane * (ECOLS / 32) + j;
+    const int n = n0 + c;
+    const bool in = n < p.n;
+    if (KIND == kKindI8)
+      sw_s[c] = !in ? 0.f : p.sw != nullptr ? __ldg(p.sw + static_cast<int64_t>(g) * p.n + n) : 1.f;
+    if (p.bias != nullptr)
+      bias_s[c] = in ? p.bias[static_cast<int64_t>(g) * p.n + n] : __float2bfloat16_rn(0.f);
+  }
+  __syncwarp();
+}
+
 // Epilogue of one warp's 32 rows x (NCHUNK*32) columns through shared memory
 // and TMA stores: per 32-column chunk, the warp's results (one row per lane,
 // 64 B) go to a 64-byte-swizzled staging buffer (conflict-free 16-byte writes)
 // and one lane stores the 32 x 32 block with cp.async.bulk.tensor; two buffers
 // alternate so the next chunk is computed while the previous one is stored.
-// The column scales and biases of the tile are staged in shared memory once
-// per tile and read as warp-wide broadcasts. This keeps the epilogue's traffic
-// through the SM's L1/shared-memory path small: that path also carries the
-// main loop's TMA writes and MMA operand reads. Row r_base + lane of the
-// output; rows past the tensor map's extent and columns >= n are clipped.
+// The column scales and biases (stage_scales) are read from shared memory as
+// warp-wide broadcasts; sxr is this lane's row scale. This keeps the
+// epilogue's traffic through the SM's L1/shared-memory path small: that path
+// also carries the main loop's TMA writes and MMA operand reads. Row
+// r_base + lane of the output; rows past the tensor map's extent and columns
+// >= n are clipped.
 template <int KIND, int NCHUNK>
 __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensorMap* tmap_y,
-                                             uint8_t* epi, uint32_t& store_count,
-                                             uint32_t tmem_row_base, uint32_t col0, int r_base,
-                                             int lane, bool rvalid, int g, int n0,
-                                             const Partials& parts) {
-  float* sw_s = reinterpret_cast<float*>(epi + kEpiSwOffset);
-  __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(epi + kEpiBiasOffset);
+                                             uint8_t* epi, const float* sw_s,
+                                             const __nv_bfloat16* bias_s, float sxr,
+                                             uint32_t& store_count, uint32_t tmem_row_base,
+                                             uint32_t col0, int r_base, int lane, int n0,
+                                             int chunk_base, const Partials& parts) {
   const bool has_bias = p.bias != nullptr;
-  __syncwarp();  // every lane is done with the previous tile's scales
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int c = lane * 8 + j;
-    const int n = n0 + c;
-    const bool in = n < p.n && c < NCHUNK * 32;
-    if (KIND == kKindI8)
-      sw_s[c] = !in ? 0.f : p.sw != nullptr ? __ldg(p.sw + static_cast<int64_t>(g) * p.n + n) : 1.f;
-    if (has_bias)
-      bias_s[c] = in ? p.bias[static_cast<int64_t>(g) * p.n + n] : __float2bfloat16_rn(0.f);
-  }
-  __syncwarp();
-  const int r = r_base + lane;
-  float sxr = 0.f;
-  if (KIND == kKindI8 && rvalid) sxr = p.sx[r];
 #pragma unroll 1
   for (int c = 0; c < NCHUNK; ++c) {
     uint32_t v[32];
@@ -415,7 +444,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
     ptx::tmem_ld_wait();
     const int n = n0 + c * 32;
     if (n >= p.n) continue;  // uniform over the warp
-    if (parts.count > 0) add_partials<KIND>(v, parts, c * 32 * 32 + lane);
+    if (parts.count > 0) add_partials<KIND>(v, parts, chunk_base + c, lane);
     uint32_t packed[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -460,16 +489,19 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
 }
 
 // Epilogue of one work item by one epilogue warp (CTAS = CTAs per worker,
-// quarter = the warp's 32-row block of the CTA's 128 rows). The owner of a
-// split tile first waits for the matching warp of every contributor to publish
-// its block of this launch, then adds the blocks while it converts the tile.
-// Returns false when such a wait ran out (the error is recorded).
+// quarter = the warp's 32-row block of the CTA's 128 rows, ew = its index among
+// the CTA's epilogue warps). The owner of a split tile first waits for the
+// matching warp of every contributor to publish its chunks of this launch,
+// then adds them while it converts the tile. Returns false when such a wait
+// ran out (the error is recorded).
 template <int KIND, int NCHUNK, int CTAS>
 __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w, int worker,
                                               int rank, const CUtensorMap* tmap_y, uint8_t* epi,
-                                              uint32_t& store_count, uint32_t tmem_row_base,
-                                              uint32_t col0, int r_base, int row_end, int g,
-                                              int n0, bool y_vec, bool acc_vec, int quarter,
+                                              const float* sw_s, const __nv_bfloat16* bias_s,
+                                              float sxr, uint32_t& store_count,
+                                              uint32_t tmem_row_base, uint32_t col0, int r_base,
+                                              int row_end, int g, int n0, int chunk_base,
+                                              bool y_vec, bool acc_vec, int quarter, int ew,
                                               int lane, int* abort_flag) {
   if (r_base >= row_end) return true;  // no row of this warp is in the tile (owner and
                                        // contributors agree: same tile, same rows)
@@ -480,7 +512,7 @@ __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w
   if (w.role == kRoleOwner) {
     for (int c = w.c_first; c <= w.c_last; ++c) {
       const int cslot = c * CTAS + rank;
-      if (!warp_wait_published(p.ws_flags + cslot * 4 + quarter, p.epoch, p.wait_budget,
+      if (!warp_wait_published(p.ws_flags + cslot * kMaxEpiWarps + ew, p.epoch, p.wait_budget,
                                lane)) {
         record_error(p.err, kDevErrSplitTimeout, abort_flag);
         return false;
@@ -498,11 +530,11 @@ __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w
   const bool tma = p.y_tma && p.acc == nullptr && slot == nullptr &&
                    (r_base + 32 <= row_end || row_end >= p.total_rows);
   if (tma)
-    epilogue_tma<KIND, NCHUNK>(p, tmap_y, epi, store_count, tmem_row_base, col0, r_base, lane,
-                               rvalid, g, n0, parts);
+    epilogue_tma<KIND, NCHUNK>(p, tmap_y, epi, sw_s, bias_s, sxr, store_count, tmem_row_base,
+                               col0, r_base, lane, n0, chunk_base, parts);
   else
-    epilogue_rows<KIND, NCHUNK>(p, tmem_row_base, col0, r, rvalid, g, n0, y_vec, acc_vec, lane,
-                                parts, slot);
+    epilogue_rows<KIND, NCHUNK>(p, tmem_row_base, col0, r, rvalid, g, n0, chunk_base, y_vec,
+                                acc_vec, lane, parts, slot);
   return true;
 }
 
@@ -512,22 +544,23 @@ __device__ __forceinline__ bool epilogue_work(const GemmParams& p, const Work& w
 // workspace publishes and waits for another epoch.
 template <int CTAS>
 __device__ __forceinline__ void epilogue_publish(const GemmParams& p, const Work& w, int worker,
-                                                 int rank, int quarter, int lane, bool active) {
+                                                 int rank, int ew, int lane, bool active) {
   if (!active || w.role != kRolePartial || p.skip_publish) return;
   __threadfence();
   __syncwarp();
-  if (lane == 0) st_release_gpu(p.ws_flags + (worker * CTAS + rank) * 4 + quarter, p.epoch);
+  if (lane == 0)
+    st_release_gpu(p.ws_flags + (worker * CTAS + rank) * kMaxEpiWarps + ew, p.epoch);
 }
 
 // ------------------------------ 1-SM kernel --------------------------------
 
 template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(kEpiWarps1), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
                       const __grid_constant__ CUtensorMap tma_y,
                       const __grid_constant__ GemmParams p) {
-  using L = SmemLayout<BN, STAGES>;
+  using L = SmemLayout<BN, STAGES, kEpiWarps1, BN>;
   constexpr int kTmemCols = 2 * BN;  // 256 or 512: a power of two >= 32
   constexpr int kElemsPerRow = (KIND == kKindI8) ? 128 : 64;
   constexpr int kKStepBytes = 32;  // K=32 int8 or K=16 bf16 per MMA instruction
@@ -559,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&tmem_full[b], 1);
-      ptx::mbar_init(&tmem_empty[b], 128);
+      ptx::mbar_init(&tmem_empty[b], 32 * kEpiWarps1);  // every epilogue thread arrives
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -672,35 +705,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may read: [32q, 32q+32)
+    const int ew = warp - 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool y_vec = p.y != nullptr && (p.ldy % 8) == 0 &&
                        (reinterpret_cast<uintptr_t>(p.y) & 15u) == 0;
     const bool acc_vec = p.acc != nullptr && (p.ldacc % 4) == 0 &&
                          (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
-    uint8_t* epi = smem + L::kEpiOffset + quarter * L::kEpiWarpBytes;
+    uint8_t* epi = smem + L::kEpiOffset + ew * L::kEpiWarpBytes;
+    float* sw_s = reinterpret_cast<float*>(epi + L::kEpiSwOffset);
+    __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(epi + L::kEpiBiasOffset);
     uint32_t store_count = 0;
     WorkIter it(p, blockIdx.x, gridDim.x);
     Work w;
     while (it.next(p, w)) {
       int g, row0, row_end, nt;
       decode_tile<kBM>(p, w.tile, g, row0, row_end, nt);
+      const int r_base = row0 + quarter * 32;
+      float sxr = 0.f;
+      if (r_base < row_end) {  // scales first: their loads overlap the tile's MMAs
+        stage_scales<KIND, BN>(p, sw_s, bias_s, g, nt * BN, lane);
+        if (KIND == kKindI8 && r_base + lane < row_end) sxr = p.sx[r_base + lane];
+      }
       if (!ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
       if (aborted(abort_flag)) break;
       ptx::tc_fence_after();
-      const int r_base = row0 + quarter * 32;
       const bool ok = epilogue_work<KIND, BN / 32, 1>(
-          p, w, blockIdx.x, 0, &tma_y, epi, store_count,
+          p, w, blockIdx.x, 0, &tma_y, epi, sw_s, bias_s, sxr, store_count,
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
-          static_cast<uint32_t>(acc * BN), r_base, row_end, g, nt * BN, y_vec, acc_vec, quarter,
-          lane, abort_flag);
+          static_cast<uint32_t>(acc * BN), r_base, row_end, g, nt * BN, 0, y_vec, acc_vec,
+          quarter, ew, lane, abort_flag);
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tmem_empty[acc]);
       if (!ok) break;
-      epilogue_publish<1>(p, w, blockIdx.x, 0, quarter, lane, r_base < row_end);
+      epilogue_publish<1>(p, w, blockIdx.x, 0, ew, lane, r_base < row_end);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -729,13 +770,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // collects one arrival per epilogue warp of both CTAs (8).
 
 template <int KIND, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(kEpiWarpsPair), 1)
     gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                            const __grid_constant__ CUtensorMap tma_b,
                            const __grid_constant__ CUtensorMap tma_y,
                            const __grid_constant__ GemmParams p) {
   constexpr int kTM = 256, kTN = 256;
-  using L = SmemLayout<128, STAGES>;  // per CTA: 128 A rows + 128 B rows per stage
+  constexpr int kSplit = kEpiWarpsPair / 4;      // epilogue warps per TMEM lane quarter
+  constexpr int kWarpCols = kTN / kSplit;        // output columns per epilogue warp
+  // per CTA: 128 A rows + 128 B rows per stage
+  using L = SmemLayout<128, STAGES, kEpiWarpsPair, kWarpCols>;
   constexpr int kTmemCols = 2 * kTN;  // double-buffered 128 x 256 accumulators
   constexpr int kElemsPerRow = (KIND == kKindI8) ? 128 : 64;
   constexpr int kKStepBytes = 32;
@@ -771,7 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&tmem_full[b], 1);
-      ptx::mbar_init(&tmem_empty[b], 8);
+      ptx::mbar_init(&tmem_empty[b], 2 * kEpiWarpsPair);  // lane 0 of every epilogue warp
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -884,8 +928,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
-    const int quarter = warp & 3;
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may read: [32q, 32q+32)
+    const int ew = warp - 2;
+    const int half = ew / 4;       // which kWarpCols columns of the tile this warp converts
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool y_vec = p.y != nullptr && (p.ldy % 8) == 0 &&
@@ -894,30 +940,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (reinterpret_cast<uintptr_t>(p.acc) & 15u) == 0;
     const uint32_t leader_tmem_empty0 = ptx::mapa_shared(ptx::smem_u32(&tmem_empty[0]), rank & ~1u);
     const int crank = static_cast<int>(rank & 1u);
-    uint8_t* epi = smem + L::kEpiOffset + quarter * L::kEpiWarpBytes;
+    uint8_t* epi = smem + L::kEpiOffset + ew * L::kEpiWarpBytes;
+    float* sw_s = reinterpret_cast<float*>(epi + L::kEpiSwOffset);
+    __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(epi + L::kEpiBiasOffset);
     uint32_t store_count = 0;
     WorkIter it(p, pair, npairs);
     Work w;
     while (it.next(p, w)) {
       int g, row0, row_end, nt;
       decode_tile<kTM>(p, w.tile, g, row0, row_end, nt);
+      const int r_base = row0 + crank * 128 + quarter * 32;
+      const int n0 = nt * kTN + half * kWarpCols;
+      float sxr = 0.f;
+      if (r_base < row_end) {  // scales first: their loads overlap the tile's MMAs
+        stage_scales<KIND, kWarpCols>(p, sw_s, bias_s, g, n0, lane);
+        if (KIND == kKindI8 && r_base + lane < row_end) sxr = p.sx[r_base + lane];
+      }
       if (!ptx::mbar_wait(&tmem_full[acc], acc_phase, p.wait_budget)) {
         record_error(p.err, kDevErrEpilogueTimeout, abort_flag);
         break;
       }
       if (aborted(abort_flag)) break;
       ptx::tc_fence_after();
-      const int r_base = row0 + crank * 128 + quarter * 32;
-      const bool ok = epilogue_work<KIND, kTN / 32, 2>(
-          p, w, pair, crank, &tma_y, epi, store_count,
+      const bool ok = epilogue_work<KIND, kWarpCols / 32, 2>(
+          p, w, pair, crank, &tma_y, epi, sw_s, bias_s, sxr, store_count,
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16),
-          static_cast<uint32_t>(acc * kTN), r_base, row_end, g, nt * kTN, y_vec, acc_vec,
-          quarter, lane, abort_flag);
+          static_cast<uint32_t>(acc * kTN + half * kWarpCols), r_base, row_end, g, n0,
+          half * (kWarpCols / 32), y_vec, acc_vec, quarter, ew, lane, abort_flag);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(leader_tmem_empty0 + static_cast<uint32_t>(acc * 8));
       if (!ok) break;
-      epilogue_publish<2>(p, w, pair, crank, quarter, lane, r_base < row_end);
+      epilogue_publish<2>(p, w, pair, crank, ew, lane, r_base < row_end);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -994,7 +1048,7 @@ int make_y_map(CUtensorMap* map, void* y, int64_t rows, int64_t n, int64_t ldy) 
 template <int KIND, int BN, int STAGES>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
            const GemmParams& p, int workers, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES>;
+  using L = SmemLayout<BN, STAGES, kEpiWarps1, BN>;
   auto kern = gemm_sm100_kernel<KIND, BN, STAGES>;
   static bool attr_done[64] = {};
   const int dev = current_device();
@@ -1009,7 +1063,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(workers);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_for(kEpiWarps1));
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -1018,12 +1072,13 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
   return LEMA_OK;
 }
 
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 5;
+using PairLayout = SmemLayout<128, kPairStages, kEpiWarpsPair, 256 / (kEpiWarpsPair / 4)>;
 
 // Pairs (clusters of 2 CTAs, 1 CTA per SM) the device can keep resident.
 template <int KIND>
 int pair_slots() {
-  using L = SmemLayout<128, kPairStages>;
+  using L = PairLayout;
   auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
   static int cache[64] = {};
   const int dev = current_device();
@@ -1039,7 +1094,7 @@ int pair_slots() {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * (device_sm_count() / 2));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for(kEpiWarpsPair));
     cfg.dynamicSmemBytes = L::kTotal;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -1056,7 +1111,7 @@ int pair_slots() {
 template <int KIND>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
                 const GemmParams& p, int workers, cudaStream_t stream) {
-  using L = SmemLayout<128, kPairStages>;
+  using L = PairLayout;
   auto kern = gemm_sm100_pair_kernel<KIND, kPairStages>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -1067,7 +1122,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * workers);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_for(kEpiWarpsPair));
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -1132,7 +1187,7 @@ bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags, int3
   if (w.slots == nullptr) {
     const size_t n = static_cast<size_t>(device_sm_count());
     const size_t slot_bytes = n * kSlotElems * sizeof(int32_t);
-    const size_t flag_bytes = n * 4 * sizeof(int32_t);  // one per slot and epilogue warp
+    const size_t flag_bytes = n * kMaxEpiWarps * sizeof(int32_t);  // per slot and epilogue warp
     void* ptr = nullptr;
     if (cudaMalloc(&ptr, slot_bytes + flag_bytes) != cudaSuccess) {
       (void)cudaGetLastError();
@@ -1159,18 +1214,25 @@ bool split_workspace(cudaStream_t stream, int32_t** slots, int32_t** flags, int3
 // Stream-K plan. T tiles of KB K-slices (128 bytes of K each) on W workers:
 // whole tiles take ceil(T / W) waves, so when T is not a multiple of W the
 // last wave leaves workers idle. Stream-K instead gives every worker the same
-// number of K-slice units: with F = floor(T / W) >= 1 full waves, the first
-// (T mod W) + W tiles are cut into W contiguous unit ranges (each at least
-// one tile long, so a tile has at most two workers) and the other
-// (F - 1) * W tiles run whole; with F = 0, all T tiles are cut, over at most
-// one worker per kMinUnits units. Each split tile costs its owner a fix-up
-// (waiting for and adding the partials), mostly hidden behind the next
-// tile's MMAs because partials are every worker's first item; the plan is
-// used when its makespan, in K-slice times plus kFixupSlices, beats the waves.
+// number of K-slice units: the R = T mod W tiles of the part-empty wave are
+// cut into contiguous unit ranges over all W workers (at most one worker per
+// kMinUnits units), run first, and the other F * W tiles (F = floor(T / W))
+// follow whole, F per worker, every worker on the same K-slice of its tile at
+// the same time (so concurrently running tiles share their operands in L2).
+// Each split tile costs its owner a fix-up (waiting for and adding the
+// partials), hidden behind its next tile's MMAs because partials are every
+// worker's first item; the plan is used for tiles of at least kMinSlices
+// K-slices when its makespan, in K-slice times plus kFixupSlices, beats the
+// waves. Measured on B200 (interleaved, 256 x 256 tiles): -9 % at int8
+// K = 11008 (86 slices); +3 to +5 % at K = 4096 (32 slices), where the
+// partials' exchange and the owners' fix-ups cost more than the part-empty
+// wave, and where whole tiles also let the next launch's set-up start on the
+// SMs the last wave leaves idle.
 // LEMA_GEMM_SPLIT=0 turns stream-K off; =1 uses it whenever a tile count
 // allows it, down to one unit per worker (tests). Returns the workers to
 // launch.
 constexpr int kMinUnits = 8;
+constexpr int kMinSlices = 64;
 constexpr int kFixupSlices = 4;
 
 int plan_schedule(GemmParams& p, int workers) {
@@ -1182,17 +1244,16 @@ int plan_schedule(GemmParams& p, int workers) {
   const bool off = env != nullptr && std::strcmp(env, "0") == 0;
   const bool forced = env != nullptr && std::strcmp(env, "1") == 0;
   const int whole = std::min(T, W);
-  if (off || T % W == 0) return whole;
+  if (off || T % W == 0 || (!forced && p.num_kb < kMinSlices)) return whole;
   const int64_t KB = p.num_kb;
   const int full = T / W;
-  const int sk_tiles = full >= 1 ? T % W + W : T;
+  const int sk_tiles = T % W;
   const int64_t units = static_cast<int64_t>(sk_tiles) * KB;
   const int64_t per = forced ? 1 : kMinUnits;
   const int S = static_cast<int>(std::min<int64_t>(W, units / per));
   if (S < 2) return whole;
   const int64_t dp_cost = static_cast<int64_t>(full + 1) * KB;
-  const int64_t sk_cost =
-      static_cast<int64_t>(full >= 1 ? full - 1 : 0) * KB + (units + S - 1) / S + kFixupSlices;
+  const int64_t sk_cost = static_cast<int64_t>(full) * KB + (units + S - 1) / S + kFixupSlices;
   if (!forced && sk_cost >= dp_cost) return whole;
   p.sk_tiles = sk_tiles;
   p.sk_workers = S;

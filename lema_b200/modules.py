@@ -62,6 +62,46 @@ class W8A8Linear(nn.Linear):
             m.bias.data.copy_(linear.bias.detach().to(dev, torch.bfloat16))
         return m
 
+    @classmethod
+    def from_conv1d(cls, conv: nn.Module, device: torch.device | str | None = None
+                    ) -> "W8A8Linear":
+        """Quantises a GPT-2 ``Conv1D`` (transformers.pytorch_utils; weight stored
+        [in, out], y = x W + b) per output channel: its weight is transposed to the
+        nn.Linear orientation [out, in] first (the pack-time transpose the GPT-2
+        adapter's weights need, src/lema/adapters/_gpt2.py:33-49). The bias
+        Parameter object is kept, so a name-based weight binding that copies
+        into it keeps working."""
+        dev = torch.device(device) if device is not None else conv.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("W8A8Linear.from_conv1d quantises on a CUDA device")
+        in_f, out_f = conv.weight.shape
+        m = cls(in_f, out_f, bias=False, device=dev)
+        m.requantize_(conv.weight.detach().to(dev).t())
+        if getattr(conv, "bias", None) is not None:
+            m.bias = conv.bias
+        return m
+
+    @torch.no_grad()
+    def requantize_(self, w: torch.Tensor) -> None:
+        """Quantises a float weight [out, in] (any strides; e.g. a slice of a
+        streamed flat buffer, or a transposed Conv1D weight) per output channel
+        into this module's own int8 weight and scales, in place (K1)."""
+        if tuple(w.shape) != (self.out_features, self.in_features):
+            raise ValueError(f"weight of shape {tuple(w.shape)} for a "
+                             f"[{self.out_features}, {self.in_features}] projection")
+        if w.dtype not in (torch.bfloat16, torch.float32):
+            w = w.to(torch.bfloat16)
+        q = self.weight.data
+        if q.stride(1) != 1 or q.stride(0) % 16 or q.data_ptr() % 16:
+            ldw = ops.pad_to(max(self.in_features, 1), 16)
+            q = torch.zeros(self.out_features, ldw, dtype=torch.int8, device=w.device)
+            q = q[:, :self.in_features]
+            self.weight.data = q
+        if self.weight_scale.stride(0) != 1:
+            self.weight_scale = torch.empty(self.out_features, dtype=torch.float32,
+                                            device=w.device)
+        ops.quantize_rows(w, out=q, scale=self.weight_scale)
+
     @torch.no_grad()
     def load_float_weight(self, w: torch.Tensor) -> None:
         """Re-quantises from a float weight [out, in] (e.g. after an optimizer step)."""

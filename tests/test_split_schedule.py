@@ -5,7 +5,7 @@ lema_b200/csrc/gemm_sm100.cu.
 
 Properties proved over a sweep of tile counts, worker counts and K lengths:
 every K-slice of every tile is computed exactly once; every stream-K range is
-non-empty; a split tile's owner computes its head (slice 0) and names exactly
+non-empty; every worker gets the same number of whole tiles after its range; a split tile's owner computes its head (slice 0) and names exactly
 the workers that hold the rest of it; a partial item is always its worker's
 first item and an owned head its worker's last stream-K item, so an owner only
 ever waits on items that wait on nothing; the tile raster is a bijection."""
@@ -14,23 +14,24 @@ import itertools
 import pytest
 
 K_MIN_UNITS = 8
+K_MIN_SLICES = 64
 K_FIXUP_SLICES = 4
 
 
 def plan_schedule(T, W, KB, mode=None):
     """-> (sk_tiles, sk_workers, workers to launch)."""
     whole = min(T, W)
-    if mode == "0" or T % W == 0:
-        return 0, 0, whole
     forced = mode == "1"
+    if mode == "0" or T % W == 0 or (not forced and KB < K_MIN_SLICES):
+        return 0, 0, whole
     full = T // W
-    sk_tiles = T % W + W if full >= 1 else T
+    sk_tiles = T % W
     units = sk_tiles * KB
     S = min(W, units // (1 if forced else K_MIN_UNITS))
     if S < 2:
         return 0, 0, whole
     dp_cost = (full + 1) * KB
-    sk_cost = (full - 1 if full >= 1 else 0) * KB + -(-units // S) + K_FIXUP_SLICES
+    sk_cost = full * KB + -(-units // S) + K_FIXUP_SLICES
     if not forced and sk_cost >= dp_cost:
         return 0, 0, whole
     return sk_tiles, S, (W if full >= 1 else S)
@@ -108,24 +109,28 @@ def test_schedule_covers_every_slice_once_and_orders_waits(T, W, KB, mode):
     # every partial is consumed by exactly one owner
     assert sorted(partial_at) == sorted(c for (w, c0, c1) in owners.values()
                                         for c in range(c0, c1 + 1))
-    if sk_tiles and T >= W:
-        # with a full wave, every range is at least one tile: at most two workers a tile
-        assert all(c0 == c1 for (_, c0, c1) in owners.values())
+    # the whole tiles after the stream-K ranges: the same count for every worker
+    dp = [sum(1 for it in work_list(w, workers, T, KB, sk_tiles, S) if it[0] >= sk_tiles)
+          for w in range(workers)]
+    if sk_tiles:
+        assert len(set(dp)) == 1
 
 
 def test_plan_for_the_training_shapes():
-    # int8 M = 4096 on 74 CTA pairs (256 x 256 tiles), K = 4096 -> 32 slices
-    assert plan_schedule(256, 74, 32) == (108, 74, 74)      # o, 4096^3: 3.46 waves -> SK
-    assert plan_schedule(768, 74, 32) == (102, 74, 74)      # qkv: 10.38 waves -> SK
-    assert plan_schedule(256, 74, 86) == (108, 74, 74)      # down, K = 11008
-    assert plan_schedule(148 * 3, 148, 32) == (0, 0, 148)   # full waves: whole tiles
-    assert plan_schedule(256, 74, 32, "0") == (0, 0, 74)    # switched off
-    # 1376 tiles (gate_up): 18.6 waves, the last wave 59 % full: SK still shorter
-    sk, S, w = plan_schedule(1376, 74, 32)
-    assert (sk, S, w) == (1376 % 74 + 74, 74, 74)
-    # fewer tiles than workers: every tile is cut
-    assert plan_schedule(32, 74, 32) == (32, 74, 74)
+    # int8 M = 4096 on 74 CTA pairs (256 x 256 tiles): K = 4096 -> 32 slices run whole
+    assert plan_schedule(256, 74, 32) == (0, 0, 74)         # o, 4096^3
+    assert plan_schedule(768, 74, 32) == (0, 0, 74)         # qkv
+    assert plan_schedule(256, 74, 86) == (34, 74, 74)       # down, K = 11008: stream-K
+    assert plan_schedule(256, 74, 64) == (34, 74, 74)       # bf16 dgrad, K = 4096
+    assert plan_schedule(148 * 3, 148, 86) == (0, 0, 148)   # full waves: whole tiles
+    assert plan_schedule(256, 74, 86, "0") == (0, 0, 74)    # switched off
+    # forced (tests): the K = 4096 shapes too
+    assert plan_schedule(256, 74, 32, "1") == (34, 74, 74)
+    assert plan_schedule(1376, 74, 32, "1") == (1376 % 74, 74, 74)
+    assert plan_schedule(32, 74, 32, "1") == (32, 74, 74)
     assert plan_schedule(4, 148, 4, "1") == (4, 16, 16)
+    # a nearly full last wave is not worth the fix-ups
+    assert plan_schedule(147, 74, 64) == (0, 0, 74)
 
 
 def decode(local, m_tiles, n_tiles, raster):
