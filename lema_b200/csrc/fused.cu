@@ -64,6 +64,15 @@ union V8 {
   __nv_bfloat16 h[8];
 };
 
+// 16-byte load of data read once (not kept in L1).
+__device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
 // ---------------------------------------------------------------- RMSNorm
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
@@ -74,12 +83,15 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
   const int64_t row = blockIdx.x;
   const int nvec = cols / 8;
   V8 v[VPT];
-  float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kThreads;
-    if (idx < nvec) {
-      v[i].u = __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+    if (idx < nvec) v[i].u = ld_stream16(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    if (threadIdx.x + i * kThreads < nvec) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float f = __bfloat162float(v[i].h[j]);
@@ -122,6 +134,86 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
     if (threadIdx.x == 0) scale[row] = s;
   }
   if (threadIdx.x == 0 && rstd_out != nullptr) rstd_out[row] = rstd;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// The same arithmetic for rows of up to 4096 columns with one warp per row and
+// four rows per CTA: the row in registers (VPL vectors per lane), both
+// reductions (sum of squares, |max|) by warp shuffles, so no thread waits on a
+// barrier.
+template <int VPL>
+__global__ void __launch_bounds__(kThreads) rmsnorm_quant_warp_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ g,
+    int64_t rows, int cols, float eps, __nv_bfloat16* __restrict__ hn, int64_t ldh,
+    int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale, float* __restrict__ rstd_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = cols / 8;
+  V8 v[VPL];
+  // every load is issued before any is used: one memory round trip per row
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = lane + i * 32;
+    if (idx < nvec) v[i].u = ld_stream16(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    if (lane + i * 32 < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = __bfloat162float(v[i].h[j]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / static_cast<float>(cols) + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = lane + i * 32;
+    if (idx < nvec) {
+      V8 gv;
+      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __nv_bfloat16 xh = __float2bfloat16_rn(__bfloat162float(v[i].h[j]) * rstd);
+        const __nv_bfloat16 o =
+            __float2bfloat16_rn(__bfloat162float(gv.h[j]) * __bfloat162float(xh));
+        v[i].h[j] = o;
+        amax = fmaxf(amax, fabsf(__bfloat162float(o)));
+      }
+      reinterpret_cast<uint4*>(hn + row * ldh)[idx] = v[i].u;
+    }
+  }
+  if (q != nullptr) {
+    amax = warp_max(amax);
+    float s, inv_s;
+    row_scale(amax, s, inv_s);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int idx = lane + i * 32;
+      if (idx < nvec) {
+        *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
+            quant8_bf16(v[i].u, s, inv_s);
+      }
+    }
+    if (lane == 0) scale[row] = s;
+  }
+  if (lane == 0 && rstd_out != nullptr) rstd_out[row] = rstd;
 }
 
 template <int VPT>
@@ -254,7 +346,10 @@ __global__ void rope_kernel(const __grid_constant__ RopeArgs a,
 }
 
 // ---------------------------------------------------------------- SwiGLU
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+// silu(x) = x / (1 + e^-x) with the fast exponential and a correctly rounded
+// reciprocal (a few ulps of fp32 from the IEEE quotient; the result is rounded
+// to bf16 next). The IEEE expf and division made this kernel compute-bound.
+__device__ __forceinline__ float silu_f(float x) { return x * __frcp_rn(1.f + __expf(-x)); }
 
 constexpr int kSwThreads = 256;  // wide rows (I = 11008 / 14336): 256 threads per row
 
@@ -267,15 +362,22 @@ __global__ void __launch_bounds__(kSwThreads) swiglu_quant_kernel(
   const int nvec = inter / 8;
   const __nv_bfloat16* gate = gu + row * ldgu;
   const __nv_bfloat16* up = gate + inter;
-  V8 mv[VPT];
+  V8 mv[VPT], uvs[VPT];
+  // every load is issued before any is used: one memory round trip per row
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * kSwThreads;
+    if (idx < nvec) {
+      mv[i].u = ld_stream16(reinterpret_cast<const uint4*>(gate) + idx);
+      uvs[i].u = ld_stream16(reinterpret_cast<const uint4*>(up) + idx);
+    }
+  }
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kSwThreads;
     if (idx < nvec) {
-      V8 gv, uv;
-      gv.u = __ldg(reinterpret_cast<const uint4*>(gate) + idx);
-      uv.u = __ldg(reinterpret_cast<const uint4*>(up) + idx);
+      const V8 gv = mv[i], uv = uvs[i];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const __nv_bfloat16 a = __float2bfloat16_rn(silu_f(__bfloat162float(gv.h[j])));
@@ -368,6 +470,25 @@ extern "C" int lema_rmsnorm_quant(const void* x_bf16, int64_t ldx, const void* g
       (q && (reinterpret_cast<uintptr_t>(q) % 8 != 0 || ldq % 8 != 0)))
     return set_error(LEMA_ERR_MISALIGNED, "rmsnorm_quant needs 16-byte aligned rows");
   auto s = static_cast<cudaStream_t>(stream);
+  const int per_lane = static_cast<int>((cols / 8 + 31) / 32);
+  if (per_lane <= 16) {
+    const unsigned grid = static_cast<unsigned>((rows + 3) / 4);
+    auto xb = static_cast<const __nv_bfloat16*>(x_bf16);
+    auto gb = static_cast<const __nv_bfloat16*>(g_bf16);
+    auto hb = static_cast<__nv_bfloat16*>(hn_bf16);
+    const int c = static_cast<int>(cols);
+    if (per_lane <= 4)
+      rmsnorm_quant_warp_kernel<4><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb, ldh,
+                                                             q, ldq, scale, rstd);
+    else if (per_lane <= 8)
+      rmsnorm_quant_warp_kernel<8><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb, ldh,
+                                                             q, ldq, scale, rstd);
+    else
+      rmsnorm_quant_warp_kernel<16><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb,
+                                                              ldh, q, ldq, scale, rstd);
+    LEMA_CUDA_TRY(cudaGetLastError());
+    return LEMA_OK;
+  }
   LEMA_VPT_LAUNCH(vpt, rmsnorm_quant_kernel, (
       static_cast<const __nv_bfloat16*>(x_bf16), ldx, static_cast<const __nv_bfloat16*>(g_bf16),
       static_cast<int>(cols), eps, static_cast<__nv_bfloat16*>(hn_bf16), ldh, q, ldq, scale,
