@@ -82,138 +82,63 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_quant_kernel(
   __shared__ float red[4];
   const int64_t row = blockIdx.x;
   const int nvec = cols / 8;
-  V8 v[VPT];
+  uint4 v[VPT];
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kThreads;
-    if (idx < nvec) v[i].u = ld_stream16(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
+    v[i] = idx < nvec ? ld_stream16(reinterpret_cast<const uint4*>(x + row * ldx) + idx)
+                      : make_uint4(0u, 0u, 0u, 0u);
   }
-  float ss = 0.f;
+  // sum of squares in two fp32 lanes (even / odd columns), packed
+  uint64_t ss2 = f2_splat(0.f);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    if (threadIdx.x + i * kThreads < nvec) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float f = __bfloat162float(v[i].h[j]);
-        ss = fmaf(f, f, ss);
-      }
-    }
+    const uint64_t a = f2_from_bf16x2(v[i].x), b = f2_from_bf16x2(v[i].y);
+    const uint64_t c = f2_from_bf16x2(v[i].z), d = f2_from_bf16x2(v[i].w);
+    ss2 = f2_fma(d, d, f2_fma(c, c, f2_fma(b, b, f2_fma(a, a, ss2))));
   }
-  ss = block_sum(ss, red);
+  float ss_lo, ss_hi;
+  f2_unpack(ss2, ss_lo, ss_hi);
+  const float ss = block_sum(ss_lo + ss_hi, red);
   const float rstd = rsqrtf(ss / static_cast<float>(cols) + eps);
-  float amax = 0.f;
+  const uint64_t rstd2 = f2_splat(rstd);
+  // hn = bf16(g * bf16(x * rstd)): the bf16 x bf16 product is exact in fp32, so
+  // one bf16x2 multiply rounds it as the fp32 product followed by RN to bf16 does
+  __nv_bfloat162 amax2 = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < nvec) {
-      V8 gv;
-      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v[i]);
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const __nv_bfloat16 xh = __float2bfloat16_rn(__bfloat162float(v[i].h[j]) * rstd);
-        const __nv_bfloat16 o =
-            __float2bfloat16_rn(__bfloat162float(gv.h[j]) * __bfloat162float(xh));
-        v[i].h[j] = o;
-        amax = fmaxf(amax, fabsf(__bfloat162float(o)));
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t xh = bf16x2_from_f2(f2_mul(f2_from_bf16x2(w[j]), rstd2));
+        const __nv_bfloat162 o = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&gw[j]),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&xh));
+        amax2 = __hmax2(amax2, __habs2(o));
+        w[j] = *reinterpret_cast<const uint32_t*>(&o);
       }
-      reinterpret_cast<uint4*>(hn + row * ldh)[idx] = v[i].u;
+      reinterpret_cast<uint4*>(hn + row * ldh)[idx] = v[i];
     }
   }
   if (q != nullptr) {
-    amax = block_max(amax, red);
+    const float amax = block_max(
+        fmaxf(__bfloat162float(__low2bfloat16(amax2)), __bfloat162float(__high2bfloat16(amax2))),
+        red);
     float s, inv_s;
     row_scale(amax, s, inv_s);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int idx = threadIdx.x + i * kThreads;
-      if (idx < nvec) {
+      if (idx < nvec)
         *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
-            quant8_bf16(v[i].u, s, inv_s);
-      }
+            quant8_bf16(v[i], s, inv_s);
     }
     if (threadIdx.x == 0) scale[row] = s;
   }
   if (threadIdx.x == 0 && rstd_out != nullptr) rstd_out[row] = rstd;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// The same arithmetic for rows of up to 4096 columns with one warp per row and
-// four rows per CTA: the row in registers (VPL vectors per lane), both
-// reductions (sum of squares, |max|) by warp shuffles, so no thread waits on a
-// barrier.
-template <int VPL>
-__global__ void __launch_bounds__(kThreads) rmsnorm_quant_warp_kernel(
-    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ g,
-    int64_t rows, int cols, float eps, __nv_bfloat16* __restrict__ hn, int64_t ldh,
-    int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale, float* __restrict__ rstd_out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int nvec = cols / 8;
-  V8 v[VPL];
-  // every load is issued before any is used: one memory round trip per row
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int idx = lane + i * 32;
-    if (idx < nvec) v[i].u = ld_stream16(reinterpret_cast<const uint4*>(x + row * ldx) + idx);
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    if (lane + i * 32 < nvec) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float f = __bfloat162float(v[i].h[j]);
-        ss = fmaf(f, f, ss);
-      }
-    }
-  }
-  ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / static_cast<float>(cols) + eps);
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int idx = lane + i * 32;
-    if (idx < nvec) {
-      V8 gv;
-      gv.u = __ldg(reinterpret_cast<const uint4*>(g) + idx);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const __nv_bfloat16 xh = __float2bfloat16_rn(__bfloat162float(v[i].h[j]) * rstd);
-        const __nv_bfloat16 o =
-            __float2bfloat16_rn(__bfloat162float(gv.h[j]) * __bfloat162float(xh));
-        v[i].h[j] = o;
-        amax = fmaxf(amax, fabsf(__bfloat162float(o)));
-      }
-      reinterpret_cast<uint4*>(hn + row * ldh)[idx] = v[i].u;
-    }
-  }
-  if (q != nullptr) {
-    amax = warp_max(amax);
-    float s, inv_s;
-    row_scale(amax, s, inv_s);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int idx = lane + i * 32;
-      if (idx < nvec) {
-        *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
-            quant8_bf16(v[i].u, s, inv_s);
-      }
-    }
-    if (lane == 0) scale[row] = s;
-  }
-  if (lane == 0 && rstd_out != nullptr) rstd_out[row] = rstd;
 }
 
 template <int VPT>
@@ -346,10 +271,32 @@ __global__ void rope_kernel(const __grid_constant__ RopeArgs a,
 }
 
 // ---------------------------------------------------------------- SwiGLU
-// silu(x) = x / (1 + e^-x) with the fast exponential and a correctly rounded
-// reciprocal (a few ulps of fp32 from the IEEE quotient; the result is rounded
-// to bf16 next). The IEEE expf and division made this kernel compute-bound.
-__device__ __forceinline__ float silu_f(float x) { return x * __frcp_rn(1.f + __expf(-x)); }
+// silu(x) = x / (1 + 2^(-x log2 e)) with the hardware's approximate base-2
+// exponential and reciprocal (a few ulps of fp32 from the IEEE expression; the
+// result is rounded to bf16 next), two columns at a time where the arithmetic
+// has a packed fp32 form.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+constexpr float kNegLog2E = -1.4426950408889634f;
+
+// bf16(silu(g)) for the two bf16 of a word, low half first.
+__device__ __forceinline__ uint32_t silu_bf16x2(uint32_t gw) {
+  const uint64_t g2 = f2_from_bf16x2(gw);
+  float a, b;
+  f2_unpack(f2_mul(g2, f2_splat(kNegLog2E)), a, b);
+  f2_unpack(f2_add(f2_pack(ex2_approx(a), ex2_approx(b)), f2_splat(1.f)), a, b);
+  return bf16x2_from_f2(f2_mul(g2, f2_pack(rcp_approx(a), rcp_approx(b))));
+}
 
 constexpr int kSwThreads = 256;  // wide rows (I = 11008 / 14336): 256 threads per row
 
@@ -362,43 +309,46 @@ __global__ void __launch_bounds__(kSwThreads) swiglu_quant_kernel(
   const int nvec = inter / 8;
   const __nv_bfloat16* gate = gu + row * ldgu;
   const __nv_bfloat16* up = gate + inter;
-  V8 mv[VPT], uvs[VPT];
+  uint4 mv[VPT], uv[VPT];
   // every load is issued before any is used: one memory round trip per row
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kSwThreads;
+    mv[i] = uv[i] = make_uint4(0u, 0u, 0u, 0u);
     if (idx < nvec) {
-      mv[i].u = ld_stream16(reinterpret_cast<const uint4*>(gate) + idx);
-      uvs[i].u = ld_stream16(reinterpret_cast<const uint4*>(up) + idx);
+      mv[i] = ld_stream16(reinterpret_cast<const uint4*>(gate) + idx);
+      uv[i] = ld_stream16(reinterpret_cast<const uint4*>(up) + idx);
     }
   }
-  float amax = 0.f;
+  // m = bf16(bf16(silu(gate)) * up): the bf16 x bf16 product is exact in fp32,
+  // so one bf16x2 multiply rounds it as the fp32 product followed by RN does
+  __nv_bfloat162 amax2 = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int idx = threadIdx.x + i * kSwThreads;
-    if (idx < nvec) {
-      const V8 gv = mv[i], uv = uvs[i];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&mv[i]);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&uv[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const __nv_bfloat16 a = __float2bfloat16_rn(silu_f(__bfloat162float(gv.h[j])));
-        const __nv_bfloat16 m =
-            __float2bfloat16_rn(__bfloat162float(a) * __bfloat162float(uv.h[j]));
-        mv[i].h[j] = m;
-        amax = fmaxf(amax, fabsf(__bfloat162float(m)));
-      }
-      if (m_out != nullptr) reinterpret_cast<uint4*>(m_out + row * ldm)[idx] = mv[i].u;
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a = silu_bf16x2(w[j]);
+      const __nv_bfloat162 m = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&u[j]));
+      amax2 = __hmax2(amax2, __habs2(m));
+      w[j] = *reinterpret_cast<const uint32_t*>(&m);
     }
+    const int idx = threadIdx.x + i * kSwThreads;
+    if (m_out != nullptr && idx < nvec) reinterpret_cast<uint4*>(m_out + row * ldm)[idx] = mv[i];
   }
-  amax = block_max<kSwThreads / 32>(amax, red);
+  const float amax = block_max<kSwThreads / 32>(
+      fmaxf(__bfloat162float(__low2bfloat16(amax2)), __bfloat162float(__high2bfloat16(amax2))),
+      red);
   float s, inv_s;
   row_scale(amax, s, inv_s);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kSwThreads;
-    if (idx < nvec) {
+    if (idx < nvec)
       *reinterpret_cast<uint2*>(q + row * ldq + static_cast<int64_t>(idx) * 8) =
-          quant8_bf16(mv[i].u, s, inv_s);
-    }
+          quant8_bf16(mv[i], s, inv_s);
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
@@ -470,25 +420,6 @@ extern "C" int lema_rmsnorm_quant(const void* x_bf16, int64_t ldx, const void* g
       (q && (reinterpret_cast<uintptr_t>(q) % 8 != 0 || ldq % 8 != 0)))
     return set_error(LEMA_ERR_MISALIGNED, "rmsnorm_quant needs 16-byte aligned rows");
   auto s = static_cast<cudaStream_t>(stream);
-  const int per_lane = static_cast<int>((cols / 8 + 31) / 32);
-  if (per_lane <= 16) {
-    const unsigned grid = static_cast<unsigned>((rows + 3) / 4);
-    auto xb = static_cast<const __nv_bfloat16*>(x_bf16);
-    auto gb = static_cast<const __nv_bfloat16*>(g_bf16);
-    auto hb = static_cast<__nv_bfloat16*>(hn_bf16);
-    const int c = static_cast<int>(cols);
-    if (per_lane <= 4)
-      rmsnorm_quant_warp_kernel<4><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb, ldh,
-                                                             q, ldq, scale, rstd);
-    else if (per_lane <= 8)
-      rmsnorm_quant_warp_kernel<8><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb, ldh,
-                                                             q, ldq, scale, rstd);
-    else
-      rmsnorm_quant_warp_kernel<16><<<grid, kThreads, 0, s>>>(xb, ldx, gb, rows, c, eps, hb,
-                                                              ldh, q, ldq, scale, rstd);
-    LEMA_CUDA_TRY(cudaGetLastError());
-    return LEMA_OK;
-  }
   LEMA_VPT_LAUNCH(vpt, rmsnorm_quant_kernel, (
       static_cast<const __nv_bfloat16*>(x_bf16), ldx, static_cast<const __nv_bfloat16*>(g_bf16),
       static_cast<int>(cols), eps, static_cast<__nv_bfloat16*>(hn_bf16), ldh, q, ldq, scale,

@@ -30,7 +30,13 @@
 namespace lema {
 
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-constexpr float kTieGuard = 0.4999f;
+// The fast form takes t = rint(x * RN(1/s)) while |d| = |x * RN(1/s) - t| <=
+// kTieGuard. For |x / s| <= 127.5 the exact product x * RN(1/s) is within
+// 127.5 * 2^-24 (7.6e-6) of x / s, the contract's fp32 quotient RN(x / s) within
+// 2^-18 (3.8e-6) of x / s, and d carries one more rounding (2^-25): the two
+// round to the same integer whenever |d| <= 0.5 - 1.2e-5. The guard keeps a
+// margin of 2e-5.
+constexpr float kTieGuard = 0.49998f;
 
 __device__ __forceinline__ float quant_row_scale(float amax) {
   return amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
@@ -79,6 +85,101 @@ __device__ __forceinline__ uint32_t quant4(float x0, float x1, float x2, float x
   return pack4_low_bytes(t[0], t[1], t[2], t[3]);
 }
 
+// ---- packed fp32 pairs (sm_100: one instruction computes two fp32 lanes) ----
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+// a * b + c per lane, each rounded once (round to nearest even).
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
+
+// The two bf16 of a 32-bit word (low half first) as an fp32 pair.
+__device__ __forceinline__ uint64_t f2_from_bf16x2(uint32_t w) {
+  return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// An fp32 pair rounded (to nearest even) to two bf16 in one word, low half first.
+__device__ __forceinline__ uint32_t bf16x2_from_f2(uint64_t v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// max(m, |a|), NaN if either is NaN.
+__device__ __forceinline__ float max_abs_nan(float m, float a) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(m), "f"(fabsf(a)));
+  return r;
+}
+
+// The fast form for 4 values held as two fp32 pairs, two elements per
+// instruction: t = RN(x * inv_s + 1.5 * 2^23) (its low byte is the candidate),
+// d = RN(x * inv_s - (t - 1.5 * 2^23)) (the distance to it, exact up to one
+// fp32 rounding). Folds max |d| into dmax (NaN-propagating); the caller takes
+// the candidates only while dmax <= kTieGuard and inv_s != 0.
+__device__ __forceinline__ uint32_t quant4_fast(uint64_t x01, uint64_t x23, uint64_t inv2,
+                                                float& dmax) {
+  const uint64_t mag2 = f2_splat(kRoundMagic);
+  const uint64_t neg1 = f2_splat(-1.f);
+  const uint64_t t01 = f2_fma(x01, inv2, mag2);
+  const uint64_t t23 = f2_fma(x23, inv2, mag2);
+  const uint64_t d01 = f2_fma(x01, inv2, f2_fma(t01, neg1, mag2));
+  const uint64_t d23 = f2_fma(x23, inv2, f2_fma(t23, neg1, mag2));
+  float d0, d1, d2, d3, t0, t1, t2, t3;
+  f2_unpack(d01, d0, d1);
+  f2_unpack(d23, d2, d3);
+  dmax = max_abs_nan(max_abs_nan(dmax, d0), d1);
+  dmax = max_abs_nan(max_abs_nan(dmax, d2), d3);
+  f2_unpack(t01, t0, t1);
+  f2_unpack(t23, t2, t3);
+  return pack4_low_bytes(__float_as_uint(t0), __float_as_uint(t1), __float_as_uint(t2),
+                         __float_as_uint(t3));
+}
+
+// Quantises 4 values held as two fp32 pairs: the fast form, or the exact
+// division for all 4 when one of them is within the guard of a tie (bf16 rows
+// sit on a coarse grid, so exact ties are common: about 1 element in 3000 of
+// Gaussian rows) or when fast_ok (inv_s != 0) is false. Checked per 4 values so
+// that a tie costs its warp 4 divisions.
+__device__ __forceinline__ uint32_t quant4_pairs(uint64_t x01, uint64_t x23, uint64_t inv2,
+                                                 float s, bool fast_ok) {
+  float dmax = 0.f;
+  const uint32_t r = quant4_fast(x01, x23, inv2, dmax);
+  if (__builtin_expect(!(dmax <= kTieGuard) || !fast_ok, 0)) {
+    float x0, x1, x2, x3;
+    f2_unpack(x01, x0, x1);
+    f2_unpack(x23, x2, x3);
+    return quant4_exact(x0, x1, x2, x3, s);
+  }
+  return r;
+}
+
 // Quantises 8 values; returns the 8 int8 results packed little-endian.
 __device__ __forceinline__ uint2 quant8(const float (&x)[8], float s, float inv_s) {
   return make_uint2(quant4(x[0], x[1], x[2], x[3], s, inv_s),
@@ -92,9 +193,10 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 
 // Quantises the 8 bf16 of a 16-byte vector.
 __device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float s, float inv_s) {
-  const float x[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
-                      bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
-  return quant8(x, s, inv_s);
+  const uint64_t inv2 = f2_splat(inv_s);
+  const bool fast_ok = inv_s != 0.f;
+  return make_uint2(quant4_pairs(f2_from_bf16x2(v.x), f2_from_bf16x2(v.y), inv2, s, fast_ok),
+                    quant4_pairs(f2_from_bf16x2(v.z), f2_from_bf16x2(v.w), inv2, s, fast_ok));
 }
 
 }  // namespace lema

@@ -92,48 +92,8 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return r;
 }
 
-// Rows of up to 16 x 32 vectors (4096 bf16 / 2048 fp32 columns): one warp per
-// row, four rows per CTA. The row stays in registers (VPL 16-byte vectors per
-// lane, all loads issued before the first use) and its |max| is a warp-shuffle
-// reduction, so no thread ever waits on a barrier; the many independent warps
-// per SM keep enough loads in flight to run at the HBM rate.
-template <typename T, int VPL>
-__global__ void __launch_bounds__(kQThreads) quant_rows_warp_kernel(
-    const T* __restrict__ x, int64_t ldx, int64_t rows, int cols, int8_t* __restrict__ q,
-    int64_t ldq, float* __restrict__ scale) {
-  constexpr int E = Vec<T>::kElems;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kQThreads / 32) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
-  const int nvec = cols / E;
-  uint4 v[VPL];
-  // every load is issued before any is used: one memory round trip per row
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int idx = lane + i * 32;
-    if (idx < nvec) v[i] = ld_stream(xr + idx);
-  }
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-    if (lane + i * 32 < nvec) amax = fmaxf(amax, Vec<T>::absmax(v[i]));
-  amax = warp_max(amax);
-  const float s = quant_row_scale(amax);
-  const float inv_s = quant_row_inv_scale(s);
-  int8_t* qr = q + row * ldq;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int idx = lane + i * 32;
-    if (idx < nvec)
-      *reinterpret_cast<decltype(Vec<T>::quant(v[i], s, inv_s))*>(
-          qr + static_cast<int64_t>(idx) * E) = Vec<T>::quant(v[i], s, inv_s);
-  }
-  if (lane == 0) scale[row] = s;
-}
-
-// Register-resident path for wider rows: cols % kElems == 0, 16-byte aligned
-// rows, and cols <= VPT * 128 * kElems.
+// Register-resident path: cols % kElems == 0, 16-byte aligned rows, and
+// cols <= VPT * 128 * kElems.
 template <typename T, int VPT>
 __global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __restrict__ x,
                                                                    int64_t ldx, int cols,
@@ -149,7 +109,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec_kernel(const T* __re
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * kQThreads;
-    if (idx < nvec) v[i] = ld_stream(xr + idx);
+    v[i] = idx < nvec ? ld_stream(xr + idx) : make_uint4(0u, 0u, 0u, 0u);
   }
   float amax = 0.f;
 #pragma unroll
@@ -359,23 +319,8 @@ int quantize_rows_impl(const T* x, int64_t rows, int64_t cols, int64_t ldx, int8
   const bool vec_ok = cols > 0 && cols % E == 0 && aligned16(x) && (ldx * sizeof(T)) % 16 == 0 &&
                       (reinterpret_cast<uintptr_t>(q) % E) == 0 && ldq % E == 0;
   const int64_t per_thread = (cols / E + kQThreads - 1) / kQThreads;
-  const int64_t per_lane = (cols / E + 31) / 32;
   const dim3 grid(static_cast<unsigned>(rows));
-  if (vec_ok && per_lane <= 16) {
-    const dim3 wgrid(static_cast<unsigned>((rows + 3) / 4));
-    if (per_lane <= 2)
-      quant_rows_warp_kernel<T, 2><<<wgrid, kQThreads, 0, s>>>(x, ldx, rows, (int)cols, q, ldq,
-                                                               scale);
-    else if (per_lane <= 4)
-      quant_rows_warp_kernel<T, 4><<<wgrid, kQThreads, 0, s>>>(x, ldx, rows, (int)cols, q, ldq,
-                                                               scale);
-    else if (per_lane <= 8)
-      quant_rows_warp_kernel<T, 8><<<wgrid, kQThreads, 0, s>>>(x, ldx, rows, (int)cols, q, ldq,
-                                                               scale);
-    else
-      quant_rows_warp_kernel<T, 16><<<wgrid, kQThreads, 0, s>>>(x, ldx, rows, (int)cols, q, ldq,
-                                                                scale);
-  } else if (vec_ok && per_thread <= 16) {
+  if (vec_ok && per_thread <= 16) {
     if (per_thread <= 1)
       quant_rows_vec_kernel<T, 1><<<grid, kQThreads, 0, s>>>(x, ldx, (int)cols, q, ldq, scale);
     else if (per_thread <= 2)
