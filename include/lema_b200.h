@@ -277,6 +277,34 @@ LEMA_API int lema_swiglu_bwd(const void* gu_bf16, int64_t ldgu, const void* dm_b
                              int64_t lddm, int64_t rows, int64_t inter, void* dgu_bf16,
                              int64_t lddgu, void* stream);
 
+/* ---- causal attention (head_dim 128, GQA) on tcgen05 ----------------------- */
+/* Replaces the block's torch scaled_dot_product_attention(q, k, v,
+ * is_causal=True, scale=scale, enable_gqa=H != Hkv) that the reference's Llama
+ * adapter reaches through HF attention (src/lema/adapters/_llama.py:236-252).
+ * q [B*S, H*128] (row stride ldq), k / v [B*S, Hkv*128], o [B*S, H*128], all
+ * bf16 token-major with 16-byte aligned bases and strides a multiple of 8;
+ * query head h reads kv head h / (H / Hkv). lse [B, H, S] fp32 receives each
+ * row's log2-domain log-sum-exp of the scaled scores (the backward's input). */
+LEMA_API int lema_attn_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                           const void* v, int64_t ldv, void* o, int64_t ldo, float* lse,
+                           int64_t B, int64_t S, int64_t H, int64_t Hkv, int64_t head_dim,
+                           float scale, void* stream);
+
+/* Gradients of lema_attn_fwd: dq [B*S, H*128], dk / dv [B*S, Hkv*128] (bf16,
+ * written whole; dk / dv of a kv head sum over its query heads) from q, k, v,
+ * the forward's o and lse, and dout. delta [B, H, S] fp32 is caller-provided
+ * scratch (receives rowsum(dout * o)). Three kernels on `stream`. */
+LEMA_API int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                           const void* v, int64_t ldv, const void* o, int64_t ldo,
+                           const void* dout, int64_t lddo, const float* lse, float* delta,
+                           void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
+                           int64_t lddv, int64_t B, int64_t S, int64_t H, int64_t Hkv,
+                           int64_t head_dim, float scale, void* stream);
+
+/* Wait budget (clock cycles) of the attention kernels' bounded waits; 0
+ * restores the default. A wait that runs out records device error 0x105. */
+LEMA_API int lema_attn_set_wait_budget(int64_t cycles);
+
 /* ---- K6: grouped W8A8 GEMM (MoE experts) -------------------------------- */
 /* Tokens are pre-sorted by expert: rows [offsets[e], offsets[e+1]) of xq/sx/y
  * belong to expert e, whose weights are wq + e*N*ldw, sw + e*N and

@@ -61,6 +61,11 @@ _SIGNATURES: dict[str, list] = {
                       vp, vp, vp, i32, vp],
     "lema_swiglu_quant": [vp, i64, i64, i64, vp, i64, vp, vp, i64, vp],
     "lema_swiglu_bwd": [vp, i64, vp, i64, i64, i64, vp, i64, vp],
+    "lema_attn_fwd": [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, i64,
+                      C.c_float, vp],
+    "lema_attn_bwd": [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64,
+                      vp, i64, i64, i64, i64, i64, i64, C.c_float, vp],
+    "lema_attn_set_wait_budget": [i64],
     "lema_ckpt_save": [vp, vp, sz, i32, vp, vp, vp],
     "lema_ckpt_restore": [vp, vp, sz, vp, vp, vp],
     "lema_mm_create": [i64, i64, i32, C.POINTER(vp)],
@@ -140,7 +145,8 @@ KERNELS_PER_CALL = {
     "lema_quantize_rows_colscaled": 1, "lema_transpose_i8": 1, "lema_w8a8_dgrad_int8": 3,
     "lema_grouped_w8a8_dgrad": 2, "lema_rmsnorm_quant": 1, "lema_rmsnorm_bwd": 1,
     "lema_rope": 1, "lema_rope_qkv": 1, "lema_swiglu_quant": 1, "lema_swiglu_bwd": 1,
-    "lema_adamw_requant_rows": 1, "lema_device_error_async": 1,
+    "lema_adamw_requant_rows": 1, "lema_device_error_async": 1, "lema_attn_fwd": 1,
+    "lema_attn_bwd": 3,
 }
 # Running count of this library's kernel launches issued by this process.
 kernel_launches = 0
@@ -196,6 +202,7 @@ DEVICE_ERROR_NAMES = {
     0x102: "a GEMM's MMA issuer timed out waiting for operands or accumulators",
     0x103: "a GEMM's epilogue timed out waiting for accumulators",
     0x104: "a split GEMM tile's partial accumulators never arrived",
+    0x105: "an attention kernel timed out waiting for a tile, a score buffer or P",
 }
 
 

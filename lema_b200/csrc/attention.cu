@@ -1,0 +1,1076 @@
+// attention.cu — causal self-attention (head_dim 128, GQA) on the 5th-generation
+// tensor cores: forward and backward, bf16 in / bf16 out, fp32 softmax and
+// accumulators. It replaces the block's scaled-dot-product attention
+// (torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,
+// scale=head_dim ** -0.5, enable_gqa=...)), which the reference's Llama adapter
+// runs through HF's attention (src/lema/adapters/_llama.py:236-252).
+//
+// Layout in HBM: the token-major projections the block already produces —
+// q [B*S, H*128], k and v [B*S, Hkv*128], o [B*S, H*128] (row strides given),
+// addressed by 3-D tensor maps {columns, S, B} so that a 128-token tile never
+// reads into the next sequence (TMA zero-fills past S and clips stores there).
+// lse [B, H, S] fp32 holds each query row's log2-domain log-sum-exp of the
+// scaled scores; delta [B, H, S] fp32 holds rowsum(dO * O) for the backward.
+//
+// Forward (attn_fwd_kernel): one CTA per (b, h, 128-query tile), heaviest tiles
+// first. Warp 0 loads Q once and K / V tiles into two-slot rings (TMA, 128-byte
+// swizzle); warp 1 issues S = Q K^T (M = N = 128, K = 128) into one of two TMEM
+// score buffers and O += P V into a TMEM accumulator, with V read MN-major
+// straight from its token-major tile; warps 2..5 own one query row per thread:
+// they read the row's scores from TMEM, mask the diagonal tile, keep a running
+// row max and sum (online softmax; O is rescaled in TMEM only when a row max
+// grows by more than 2^8, so P stays below 256), write P as bf16 into a
+// swizzled shared tile for the P V MMA, and finally normalise O, write it
+// through a TMA store and record the row's log-sum-exp.
+//
+// Backward (two kernels, no atomics, deterministic):
+//   attn_bwd_dkdv_kernel: one CTA per (b, kv head, 128-key tile); for every
+//     query head of the group and every causal query tile it forms S^T = K Q^T
+//     and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse), dS^T = P^T (dP^T -
+//     delta), and accumulates dV += P^T dO and dK += dS^T Q (Q, dO read MN-major
+//     from the tiles the first two MMAs used K-major).
+//   attn_bwd_dq_kernel: one CTA per (b, h, 128-query tile); for every causal key
+//     tile it forms S = Q K^T and dP = dO V^T, dS = P (dP - delta), and
+//     accumulates dQ += dS K (K read MN-major).
+// dK, dQ carry the softmax scale; dK / dV of a kv head sum over its query heads.
+//
+// Every wait is bounded (clock64 budget) and also ends when another role of the
+// CTA has given up: a timeout records an error word and the CTA drains its
+// copies and MMAs in flight before TMEM is released.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include <cudaTypedefs.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace lema {
+namespace {
+
+constexpr int kHd = 128;          // head dim
+constexpr int kTile = 128;        // query / key rows per tile
+constexpr int kBox = 16384;       // one TMA box: 128 rows x 64 bf16 (128 B), swizzled
+constexpr int kTileBytes = 2 * kBox;  // a 128 x 128 bf16 tile = two boxes
+constexpr uint32_t kIdescKK = ptx::idesc_bf16_f32_major(128, 128, false, false);
+constexpr uint32_t kIdescKMn = ptx::idesc_bf16_f32_major(128, 128, false, true);
+constexpr float kRescaleLog2 = 8.f;  // O is rescaled when a row max grows by more
+
+struct AttnParams {
+  int B, S, H, Hkv, q_tiles;
+  float scale;       // softmax scale (head_dim ** -0.5)
+  float scale_log2;  // scale * log2(e)
+  float* lse;        // [B, H, S]
+  const float* delta;  // [B, H, S] (backward)
+  int32_t* err;
+  long long budget;
+};
+
+__device__ __forceinline__ void record_err(int32_t* err, int32_t code, int* abort_flag) {
+  atomicCAS(err, 0, code);
+  *reinterpret_cast<volatile int*>(abort_flag) = 1;
+}
+
+__device__ __forceinline__ bool is_aborted(const int* abort_flag) {
+  return *reinterpret_cast<const volatile int*>(abort_flag) != 0;
+}
+
+// mbar_wait that also gives up when another role of the CTA has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, long long budget,
+                                         const int* abort_flag) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (is_aborted(abort_flag) || clock64() - t0 > budget) return false;
+  }
+}
+
+// Byte offset of the 16-byte chunk holding columns [col, col + 8) (col a
+// multiple of 8, < 128) of row r (< 128) in a 128 x 128 bf16 tile stored as two
+// 128-byte-swizzled boxes of 64 columns (TMA's layout): box col / 64, row r at
+// 128 B, chunk (col / 8) % 8 exchanged with r % 8. Always < 32768.
+__device__ __forceinline__ uint32_t swz_chunk(int r, int col) {
+  return static_cast<uint32_t>((col >> 6) * kBox + r * 128 +
+                               ((((col >> 3) & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Named barrier over the 128 threads of warps 2..5.
+__device__ __forceinline__ void sync_rows() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// S or dP = A B^T over head_dim: A, B both [128 x 128] K-major tiles.
+__device__ __forceinline__ void mma_tile_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
+                                            bool accumulate_first) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t off = static_cast<uint32_t>((k >> 2) * kBox + (k & 3) * 32);
+    ptx::mma_bf16(d_tmem, ptx::desc_kmajor_sw128(a_addr + off),
+                  ptx::desc_kmajor_sw128(b_addr + off), kIdescKK,
+                  (accumulate_first || k > 0) ? 1u : 0u);
+  }
+}
+
+// D += A B over 128 inner rows: A [128 x 128] K-major (written by threads),
+// B a token-major [128 rows x 128 dims] tile read MN-major (N = dims).
+__device__ __forceinline__ void mma_tile_kmn(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
+                                             bool accumulate_first) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t aoff = static_cast<uint32_t>((k >> 2) * kBox + (k & 3) * 32);
+    ptx::mma_bf16(d_tmem, ptx::desc_kmajor_sw128(a_addr + aoff),
+                  ptx::desc_mnmajor_sw128(b_addr + k * 2048, kBox, 1024), kIdescKMn,
+                  (accumulate_first || k > 0) ? 1u : 0u);
+  }
+}
+
+// wait_bar whose result is the same for every lane of the warp (the warp then
+// takes the same path into warp-collective tcgen05 loads and stores).
+__device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, long long budget,
+                                              const int* abort_flag) {
+  const bool r = wait_bar(bar, parity, budget, abort_flag);
+  return __all_sync(0xffffffffu, r);
+}
+
+// 128 fp32 columns of this thread's TMEM lane, [col, col + 128).
+__device__ __forceinline__ void tmem_row128(uint32_t taddr, uint32_t (&v)[4][32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) ptx::tmem_ld_32x32b_x32(taddr + c * 32, v[c]);
+  ptx::tmem_ld_wait();
+}
+
+// ------------------------------------------------------------------ forward
+constexpr int kFwdThreads = 192;
+constexpr int kFwdBars = 18;
+constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 1024;
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mo,
+                    const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sq = smem;                     // Q tile; O staging at the end
+  uint8_t* sk = smem + kTileBytes;        // K ring, 2 slots
+  uint8_t* sv = smem + 3 * kTileBytes;    // V ring, 2 slots
+  uint8_t* sp = smem + 5 * kTileBytes;    // P (bf16), 2 slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 15;
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kFwdBars);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int bh_count = p.B * p.H;
+  const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kvh = h / (p.H / p.Hkv);
+  const int n_kv = qt + 1;
+  const int q0 = qt * kTile;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&mq);
+    ptx::prefetch_tmap(&mk);
+    ptx::prefetch_tmap(&mv);
+    ptx::prefetch_tmap(&mo);
+    for (int i = 0; i < kFwdBars; ++i) ptx::mbar_init(&bars[i], 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&s_free[s], 128);  // every row thread arrives
+      ptx::mbar_init(&p_full[s], 128);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 512);  // S0 [0,128), S1 [128,256), O [256,384)
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  ptx::griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      ptx::mbar_arrive_expect_tx(q_full, kTileBytes);
+      ptx::tma_load_3d(sq, &mq, q_full, h * kHd, q0, b);
+      ptx::tma_load_3d(sq + kBox, &mq, q_full, h * kHd + 64, q0, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_bar(&k_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        ptx::tma_load_3d(sk + s * kTileBytes, &mk, &k_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sk + s * kTileBytes + kBox, &mk, &k_full[s], kvh * kHd + 64, j * kTile, b);
+        ++k_issued;
+        if (j >= 2 && !wait_bar(&v_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        ptx::tma_load_3d(sv + s * kTileBytes, &mv, &v_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sv + s * kTileBytes + kBox, &mv, &v_full[s], kvh * kHd + 64, j * kTile, b);
+        ++v_issued;
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      // every issued load lands before this CTA's shared memory is released
+      (void)ptx::mbar_wait(q_full, 0, p.budget);
+      for (int i = k_issued - 1; i >= 0 && i >= k_issued - 2; --i)
+        (void)ptx::mbar_wait(&k_full[i & 1], (i >> 1) & 1, p.budget);
+      for (int i = v_issued - 1; i >= 0 && i >= v_issued - 2; --i)
+        (void)ptx::mbar_wait(&v_full[i & 1], (i >> 1) & 1, p.budget);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      bool ok = wait_bar(q_full, 0, p.budget, abort_flag);
+      bool issued = false;
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {  // S_j = Q K_j^T
+          const int s = j & 1;
+          if (!wait_bar(&k_full[s], (j >> 1) & 1, p.budget, abort_flag) ||
+              (j >= 2 && !wait_bar(&s_free[s], ((j - 2) >> 1) & 1, p.budget, abort_flag))) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kk(tmem + s * 128, ptx::smem_u32(sq), ptx::smem_u32(sk + s * kTileBytes), false);
+          issued = true;
+          ptx::mma_commit(&s_full[s]);
+          ptx::mma_commit(&k_empty[s]);
+        }
+        if (j >= 1) {  // O += P_{j-1} V_{j-1}
+          const int jj = j - 1, s = jj & 1;
+          if (!wait_bar(&p_full[s], (jj >> 1) & 1, p.budget, abort_flag) ||
+              !wait_bar(&v_full[s], (jj >> 1) & 1, p.budget, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kmn(tmem + 256, ptx::smem_u32(sp + s * kTileBytes),
+                       ptx::smem_u32(sv + s * kTileBytes), jj > 0);
+          ptx::mma_commit(&pv_done[s]);
+          ptx::mma_commit(&v_empty[s]);
+        }
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      if (issued) {  // all MMAs complete before TMEM is released
+        ptx::mma_commit(drain);
+        (void)ptx::mbar_wait(drain, 0, p.budget);
+      }
+    }
+  } else {
+    // ---------------- softmax rows (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    float m_run = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!wait_bar_warp(&s_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t v[4][32];
+      tmem_row128(trow + s * 128, v);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&s_free[s]);
+      const bool diag = j == qt;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(v[c4][i]) * p.scale_log2;
+          if (diag && c4 * 32 + i > row) x = -INFINITY;
+          v[c4][i] = __float_as_uint(x);
+          tmax = fmaxf(tmax, x);
+        }
+      }
+      const bool need = tmax > m_run + kRescaleLog2;
+      const float m_new = need ? tmax : m_run;
+      const float alpha = need ? ex2(m_run - m_new) : 1.f;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O *= alpha on this warp's rows, once P_{j-1} V_{j-1} has landed
+        if (!wait_bar_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, o);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          ptx::tmem_st_32x32b_x32(trow + 256 + c4 * 32, o);
+        }
+        ptx::tmem_st_wait();
+      }
+      l *= alpha;
+      m_run = m_new;
+      float rsum = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e = ex2(__uint_as_float(v[c4][i]) - m_run);
+          rsum += e;
+          v[c4][i] = __float_as_uint(e);
+        }
+      }
+      l += rsum;
+      // P_j goes to slot s once P_{j-2} V_{j-2} has read it
+      if (j >= 2 && !wait_bar_warp(&pv_done[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint32_t pbase = ptx::smem_u32(sp + s * kTileBytes);
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        const uint32_t* e = &v[c8 >> 2][(c8 & 3) * 8];
+        st_shared_v4(pbase + swz_chunk(row, c8 * 8),
+                     pack_bf16x2(__uint_as_float(e[0]), __uint_as_float(e[1])),
+                     pack_bf16x2(__uint_as_float(e[2]), __uint_as_float(e[3])),
+                     pack_bf16x2(__uint_as_float(e[4]), __uint_as_float(e[5])),
+                     pack_bf16x2(__uint_as_float(e[6]), __uint_as_float(e[7])));
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&p_full[s]);
+    }
+    // ---------------- epilogue: O / l -> bf16 -> TMA store; lse ----------------
+    if (ok && !wait_bar_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.budget,
+                             abort_flag))
+      ok = false;
+    if (!ok) {
+      record_err(p.err, kDevErrAttnTimeout, abort_flag);
+    } else {
+      ptx::tc_fence_after();
+      const float inv_l = 1.f / l;
+      const uint32_t obase = ptx::smem_u32(sq);
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, o);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t* e = &o[i * 8];
+          st_shared_v4(obase + swz_chunk(row, c4 * 32 + i * 8),
+                       pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
+                       pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
+                       pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
+                       pack_bf16x2(__uint_as_float(e[6]) * inv_l, __uint_as_float(e[7]) * inv_l));
+        }
+      }
+      const int q = q0 + row;
+      if (q < p.S) p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l);
+    }
+    ptx::fence_proxy_async_smem();
+    sync_rows();
+    if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
+      ptx::tma_store_3d(&mo, sq, h * kHd, q0, b);
+      ptx::tma_store_3d(&mo, sq + kBox, h * kHd + 64, q0, b);
+      ptx::bulk_commit_group();
+      ptx::bulk_wait_group_all();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------- backward
+
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d] (fp32), one warp per
+// (token, head): 4 columns per lane.
+__global__ void __launch_bounds__(256) attn_delta_kernel(const __nv_bfloat16* __restrict__ o,
+                                                         int64_t ldo,
+                                                         const __nv_bfloat16* __restrict__ dout,
+                                                         int64_t lddo, float* __restrict__ delta,
+                                                         int B, int S, int H) {
+  const int lane = threadIdx.x % 32;
+  const int64_t pairs = static_cast<int64_t>(B) * S * H;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+       w < pairs; w += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const int64_t tok = w / H;  // b * S + q
+    const int h = static_cast<int>(w % H);
+    const uint2 a = *reinterpret_cast<const uint2*>(o + tok * ldo + h * kHd + lane * 4);
+    const uint2 g = *reinterpret_cast<const uint2*>(dout + tok * lddo + h * kHd + lane * 4);
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 af = __bfloat1622float2(a2[i]), gf = __bfloat1622float2(g2[i]);
+      s = fmaf(af.x, gf.x, s);
+      s = fmaf(af.y, gf.y, s);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) {
+      const int64_t b = tok / S, q = tok % S;
+      delta[(b * H + h) * S + q] = s;
+    }
+  }
+}
+
+// Loads the 128 (lse, delta) values of query tile q0 of head (b, h) into shared
+// memory; rows past S get lse = +inf (P = 0 there) and delta = 0.
+__device__ __forceinline__ void stage_rows(const AttnParams& p, int b, int h, int q0, int tid,
+                                           float* lse_s, float* delta_s) {
+  const int q = q0 + tid;
+  const int64_t i = (static_cast<int64_t>(b) * p.H + h) * p.S + q;
+  lse_s[tid] = q < p.S ? p.lse[i] : INFINITY;
+  delta_s[tid] = q < p.S ? p.delta[i] : 0.f;
+}
+
+// Writes 32 fp32 values (columns [col, col + 32) of row r) as bf16 into a
+// swizzled 128 x 128 tile, each multiplied by mul.
+__device__ __forceinline__ void store_row32(uint32_t tile, int r, int col, const float (&x)[32],
+                                            float mul) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    st_shared_v4(tile + swz_chunk(r, col + i * 8),
+                 pack_bf16x2(x[i * 8 + 0] * mul, x[i * 8 + 1] * mul),
+                 pack_bf16x2(x[i * 8 + 2] * mul, x[i * 8 + 3] * mul),
+                 pack_bf16x2(x[i * 8 + 4] * mul, x[i * 8 + 5] * mul),
+                 pack_bf16x2(x[i * 8 + 6] * mul, x[i * 8 + 7] * mul));
+}
+
+constexpr int kBwdThreads = 192;
+constexpr int kDkdvBars = 6;
+constexpr int kDkdvSmem = 6 * kTileBytes + 1024 + kDkdvBars * 8 + 16 + 1024;
+
+// dK, dV of one (b, kv head, 128-key tile).
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap mq,
+                         const __grid_constant__ CUtensorMap mk,
+                         const __grid_constant__ CUtensorMap mv,
+                         const __grid_constant__ CUtensorMap mdo,
+                         const __grid_constant__ CUtensorMap mdk,
+                         const __grid_constant__ CUtensorMap mdv,
+                         const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sk = smem;
+  uint8_t* sv = smem + kTileBytes;
+  uint8_t* sq = smem + 2 * kTileBytes;
+  uint8_t* sdo = smem + 3 * kTileBytes;
+  uint8_t* spt = smem + 4 * kTileBytes;   // P^T (bf16); dV staging at the end
+  uint8_t* sdst = smem + 5 * kTileBytes;  // dS^T (bf16); dK staging at the end
+  float* lse_s = reinterpret_cast<float*>(smem + 6 * kTileBytes);
+  float* delta_s = lse_s + kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes + 1024);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = bars + 2;  // the item's four MMAs are complete
+  uint64_t* st_full = bars + 3;   // S^T and dP^T are in TMEM
+  uint64_t* pd_full = bars + 4;   // P^T and dS^T are in shared memory (128 arrivals)
+  uint64_t* drain = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDkdvBars);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int bkv = p.B * p.Hkv;
+  const int kt = static_cast<int>(blockIdx.x) / bkv;  // key tile 0 (the heaviest) first
+  const int b = (static_cast<int>(blockIdx.x) % bkv) / p.Hkv;
+  const int kvh = static_cast<int>(blockIdx.x) % p.Hkv;
+  const int rep = p.H / p.Hkv;
+  const int per_head = p.q_tiles - kt;  // causal query tiles kt .. q_tiles - 1
+  const int n_items = rep * per_head;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&mq);
+    ptx::prefetch_tmap(&mk);
+    ptx::prefetch_tmap(&mv);
+    ptx::prefetch_tmap(&mdo);
+    for (int i = 0; i < kDkdvBars; ++i) ptx::mbar_init(&bars[i], 1);
+    ptx::mbar_init(pd_full, 128);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 512);  // S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512)
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  ptx::griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int issued = 0;
+      bool ok = true;
+      ptx::mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+      ptx::tma_load_3d(sk, &mk, kv_full, kvh * kHd, kt * kTile, b);
+      ptx::tma_load_3d(sk + kBox, &mk, kv_full, kvh * kHd + 64, kt * kTile, b);
+      ptx::tma_load_3d(sv, &mv, kv_full, kvh * kHd, kt * kTile, b);
+      ptx::tma_load_3d(sv + kBox, &mv, kv_full, kvh * kHd + 64, kt * kTile, b);
+      for (int it = 0; it < n_items; ++it) {
+        const int h = kvh * rep + it / per_head;
+        const int q0 = (kt + it % per_head) * kTile;
+        if (it > 0 && !wait_bar(qd_empty, (it - 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(qd_full, 2 * kTileBytes);
+        ptx::tma_load_3d(sq, &mq, qd_full, h * kHd, q0, b);
+        ptx::tma_load_3d(sq + kBox, &mq, qd_full, h * kHd + 64, q0, b);
+        ptx::tma_load_3d(sdo, &mdo, qd_full, h * kHd, q0, b);
+        ptx::tma_load_3d(sdo + kBox, &mdo, qd_full, h * kHd + 64, q0, b);
+        ++issued;
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      (void)ptx::mbar_wait(kv_full, 0, p.budget);
+      if (issued > 0) (void)ptx::mbar_wait(qd_full, (issued - 1) & 1, p.budget);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      bool ok = wait_bar(kv_full, 0, p.budget, abort_flag);
+      bool issued = false;
+      for (int it = 0; ok && it < n_items; ++it) {
+        if (!wait_bar(qd_full, it & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        mma_tile_kk(tmem, ptx::smem_u32(sk), ptx::smem_u32(sq), false);         // S^T = K Q^T
+        mma_tile_kk(tmem + 128, ptx::smem_u32(sv), ptx::smem_u32(sdo), false);  // dP^T = V dO^T
+        issued = true;
+        ptx::mma_commit(st_full);
+        if (!wait_bar(pd_full, it & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        mma_tile_kmn(tmem + 256, ptx::smem_u32(spt), ptx::smem_u32(sdo), it > 0);   // dV += P^T dO
+        mma_tile_kmn(tmem + 384, ptx::smem_u32(sdst), ptx::smem_u32(sq), it > 0);   // dK += dS^T Q
+        ptx::mma_commit(qd_empty);
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      if (issued) {
+        ptx::mma_commit(drain);
+        (void)ptx::mbar_wait(drain, 0, p.budget);
+      }
+    }
+  } else {
+    // ---------------- elementwise rows (warps 2..5): one key per thread ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int tid = threadIdx.x - 64;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t pt_base = ptx::smem_u32(spt), dst_base = ptx::smem_u32(sdst);
+    bool ok = true;
+    for (int it = 0; it < n_items; ++it) {
+      const int h = kvh * rep + it / per_head;
+      const int qi = kt + it % per_head;
+      sync_rows();  // every row is done with the previous item's (lse, delta)
+      stage_rows(p, b, h, qi * kTile, tid, lse_s, delta_s);
+      sync_rows();
+      if (!wait_bar_warp(st_full, it & 1, p.budget, abort_flag)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const bool diag = qi == kt;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sv32[32], dp32[32];
+        ptx::tmem_ld_32x32b_x32(trow + c4 * 32, sv32);
+        ptx::tmem_ld_32x32b_x32(trow + 128 + c4 * 32, dp32);
+        ptx::tmem_ld_wait();
+        float pf[32], ds[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = c4 * 32 + i;  // query column
+          float pv = ex2(__uint_as_float(sv32[i]) * p.scale_log2 - lse_s[c]);
+          if (diag && c < row) pv = 0.f;  // key after query
+          pf[i] = pv;
+          ds[i] = pv * (__uint_as_float(dp32[i]) - delta_s[c]);
+        }
+        store_row32(pt_base, row, c4 * 32, pf, 1.f);
+        store_row32(dst_base, row, c4 * 32, ds, 1.f);
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(pd_full);
+    }
+    // ---------------- epilogue: dV, scale * dK -> bf16 -> TMA store ----------------
+    if (ok && !wait_bar_warp(qd_empty, (n_items - 1) & 1, p.budget, abort_flag)) ok = false;
+    if (!ok) {
+      record_err(p.err, kDevErrAttnTimeout, abort_flag);
+    } else {
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t a[32], g[32];
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
+        ptx::tmem_ld_32x32b_x32(trow + 384 + c4 * 32, g);
+        ptx::tmem_ld_wait();
+        float af[32], gf[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          af[i] = __uint_as_float(a[i]);
+          gf[i] = __uint_as_float(g[i]);
+        }
+        store_row32(pt_base, row, c4 * 32, af, 1.f);
+        store_row32(dst_base, row, c4 * 32, gf, p.scale);
+      }
+    }
+    ptx::fence_proxy_async_smem();
+    sync_rows();
+    if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
+      ptx::tma_store_3d(&mdv, spt, kvh * kHd, kt * kTile, b);
+      ptx::tma_store_3d(&mdv, spt + kBox, kvh * kHd + 64, kt * kTile, b);
+      ptx::tma_store_3d(&mdk, sdst, kvh * kHd, kt * kTile, b);
+      ptx::tma_store_3d(&mdk, sdst + kBox, kvh * kHd + 64, kt * kTile, b);
+      ptx::bulk_commit_group();
+      ptx::bulk_wait_group_all();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+constexpr int kDqBars = 11;
+constexpr int kDqSmem = 7 * kTileBytes + kDqBars * 8 + 16 + 1024;
+
+// dQ of one (b, h, 128-query tile).
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap mq,
+                       const __grid_constant__ CUtensorMap mk,
+                       const __grid_constant__ CUtensorMap mv,
+                       const __grid_constant__ CUtensorMap mdo,
+                       const __grid_constant__ CUtensorMap mdq,
+                       const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sq = smem;                   // Q; dQ staging at the end
+  uint8_t* sdo = smem + kTileBytes;
+  uint8_t* sk = smem + 2 * kTileBytes;  // K ring, 2 slots
+  uint8_t* sv = smem + 4 * kTileBytes;  // V ring, 2 slots
+  uint8_t* sds = smem + 6 * kTileBytes; // dS (bf16)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
+  uint64_t* qd_full = bars;
+  uint64_t* kv_full = bars + 1;   // 2
+  uint64_t* kv_empty = bars + 3;  // 2
+  uint64_t* sd_full = bars + 5;   // S and dP are in TMEM
+  uint64_t* sd_free = bars + 6;   // the rows have read them (128 arrivals)
+  uint64_t* ds_full = bars + 7;   // dS is in shared memory (128 arrivals)
+  uint64_t* dq_done = bars + 8;   // dQ += dS K complete
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDqBars);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int bh_count = p.B * p.H;
+  const int qi = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / bh_count;
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kvh = h / (p.H / p.Hkv);
+  const int n_kv = qi + 1;
+  const int q0 = qi * kTile;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&mq);
+    ptx::prefetch_tmap(&mk);
+    ptx::prefetch_tmap(&mv);
+    ptx::prefetch_tmap(&mdo);
+    for (int i = 0; i < kDqBars; ++i) ptx::mbar_init(&bars[i], 1);
+    ptx::mbar_init(sd_free, 128);
+    ptx::mbar_init(ds_full, 128);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 512);  // S [0,128), dP [128,256), dQ [256,384)
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  ptx::griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int issued = 0;
+      bool ok = true;
+      ptx::mbar_arrive_expect_tx(qd_full, 2 * kTileBytes);
+      ptx::tma_load_3d(sq, &mq, qd_full, h * kHd, q0, b);
+      ptx::tma_load_3d(sq + kBox, &mq, qd_full, h * kHd + 64, q0, b);
+      ptx::tma_load_3d(sdo, &mdo, qd_full, h * kHd, q0, b);
+      ptx::tma_load_3d(sdo + kBox, &mdo, qd_full, h * kHd + 64, q0, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_bar(&kv_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        ptx::tma_load_3d(sk + s * kTileBytes, &mk, &kv_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sk + s * kTileBytes + kBox, &mk, &kv_full[s], kvh * kHd + 64, j * kTile, b);
+        ptx::tma_load_3d(sv + s * kTileBytes, &mv, &kv_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sv + s * kTileBytes + kBox, &mv, &kv_full[s], kvh * kHd + 64, j * kTile, b);
+        ++issued;
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      (void)ptx::mbar_wait(qd_full, 0, p.budget);
+      for (int i = issued - 1; i >= 0 && i >= issued - 2; --i)
+        (void)ptx::mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.budget);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      bool ok = wait_bar(qd_full, 0, p.budget, abort_flag);
+      bool issued = false;
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {  // S_j = Q K_j^T, dP_j = dO V_j^T
+          const int s = j & 1;
+          if (!wait_bar(&kv_full[s], (j >> 1) & 1, p.budget, abort_flag) ||
+              (j >= 1 && !wait_bar(sd_free, (j - 1) & 1, p.budget, abort_flag))) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kk(tmem, ptx::smem_u32(sq), ptx::smem_u32(sk + s * kTileBytes), false);
+          mma_tile_kk(tmem + 128, ptx::smem_u32(sdo), ptx::smem_u32(sv + s * kTileBytes), false);
+          issued = true;
+          ptx::mma_commit(sd_full);
+        }
+        if (j >= 1) {  // dQ += dS_{j-1} K_{j-1}
+          const int jj = j - 1, s = jj & 1;
+          if (!wait_bar(ds_full, jj & 1, p.budget, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kmn(tmem + 256, ptx::smem_u32(sds), ptx::smem_u32(sk + s * kTileBytes), jj > 0);
+          ptx::mma_commit(dq_done);
+          ptx::mma_commit(&kv_empty[s]);
+        }
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      if (issued) {
+        ptx::mma_commit(drain);
+        (void)ptx::mbar_wait(drain, 0, p.budget);
+      }
+    }
+  } else {
+    // ---------------- elementwise rows (warps 2..5): one query per thread ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t ds_base = ptx::smem_u32(sds);
+    const int q = q0 + row;
+    const int64_t ri = (static_cast<int64_t>(b) * p.H + h) * p.S + q;
+    const float lse_r = q < p.S ? p.lse[ri] : INFINITY;
+    const float delta_r = q < p.S ? p.delta[ri] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!wait_bar_warp(sd_full, j & 1, p.budget, abort_flag) ||
+          (j >= 1 && !wait_bar_warp(dq_done, (j - 1) & 1, p.budget, abort_flag))) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const bool diag = j == qi;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sv32[32], dp32[32];
+        ptx::tmem_ld_32x32b_x32(trow + c4 * 32, sv32);
+        ptx::tmem_ld_32x32b_x32(trow + 128 + c4 * 32, dp32);
+        ptx::tmem_ld_wait();
+        float ds[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float pv = ex2(__uint_as_float(sv32[i]) * p.scale_log2 - lse_r);
+          if (diag && c4 * 32 + i > row) pv = 0.f;  // key after query
+          ds[i] = pv * (__uint_as_float(dp32[i]) - delta_r);
+        }
+        store_row32(ds_base, row, c4 * 32, ds, 1.f);
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(sd_free);
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(ds_full);
+    }
+    // ---------------- epilogue: scale * dQ -> bf16 -> TMA store ----------------
+    if (ok && !wait_bar_warp(dq_done, (n_kv - 1) & 1, p.budget, abort_flag)) ok = false;
+    if (!ok) {
+      record_err(p.err, kDevErrAttnTimeout, abort_flag);
+    } else {
+      ptx::tc_fence_after();
+      const uint32_t qbase = ptx::smem_u32(sq);
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t a[32];
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
+        ptx::tmem_ld_wait();
+        float af[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) af[i] = __uint_as_float(a[i]);
+        store_row32(qbase, row, c4 * 32, af, p.scale);
+      }
+    }
+    ptx::fence_proxy_async_smem();
+    sync_rows();
+    if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
+      ptx::tma_store_3d(&mdq, sq, h * kHd, q0, b);
+      ptx::tma_store_3d(&mdq, sq + kBox, h * kHd + 64, q0, b);
+      ptx::bulk_commit_group();
+      ptx::bulk_wait_group_all();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+// 3-D map over a token-major bf16 tensor [B, S, cols] with row stride ld
+// elements: box = 64 columns (128 B) x 128 tokens x 1 sequence, 128-byte
+// swizzle, zero fill past S (loads) and clipping past S (stores).
+int make_seq_map(CUtensorMap* map, const void* base, int64_t B, int64_t S, int64_t cols,
+                 int64_t ld) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (encode == nullptr)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2,
+                           static_cast<cuuint64_t>(ld) * 2 * static_cast<cuuint64_t>(S)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTile), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled (attention) failed (code " +
+                                        std::to_string(static_cast<int>(r)) + ")");
+  return LEMA_OK;
+}
+
+std::atomic<long long> g_attn_budget{ptx::kWaitBudgetCycles};
+
+// Shape and pointer checks shared by the entry points.
+int check_attn(int64_t B, int64_t S, int64_t H, int64_t Hkv, int64_t head_dim) {
+  if (head_dim != kHd) return set_error(LEMA_ERR_INVALID_ARGUMENT, "head_dim must be 128");
+  if (B < 0 || S < 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "bad B / S / heads (H must be a multiple of Hkv)");
+  if (B > 65535 || S > (1 << 24) || H > 1024)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "B, S or H out of range");
+  return LEMA_OK;
+}
+
+int check_tensor(const void* ptr, int64_t ld, int64_t cols, const char* name) {
+  if (ptr == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, std::string("null ") + name);
+  if (!aligned16(ptr) || ld % 8 != 0 || ld < cols)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT,
+                     std::string(name) + ": 16-byte aligned base and row stride >= columns, "
+                                         "a multiple of 8 elements, required");
+  return LEMA_OK;
+}
+
+AttnParams make_params(int64_t B, int64_t S, int64_t H, int64_t Hkv, float scale) {
+  AttnParams p{};
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.H = static_cast<int>(H);
+  p.Hkv = static_cast<int>(Hkv);
+  p.q_tiles = static_cast<int>((S + kTile - 1) / kTile);
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = gemm_error_word();
+  p.budget = g_attn_budget.load();
+  return p;
+}
+
+template <typename Kern>
+int set_smem(Kern kern, int bytes, bool* done) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(LEMA_ERR_CUDA, "bad device");
+  if (!done[dev]) {
+    LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev] = true;
+  }
+  return LEMA_OK;
+}
+
+}  // namespace
+}  // namespace lema
+
+using namespace lema;
+
+extern "C" int lema_attn_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                             const void* v, int64_t ldv, void* o, int64_t ldo, float* lse,
+                             int64_t B, int64_t S, int64_t H, int64_t Hkv, int64_t head_dim,
+                             float scale, void* stream) {
+  clear_error();
+  int rc = check_attn(B, S, H, Hkv, head_dim);
+  if (rc) return rc;
+  if (B == 0 || S == 0) return LEMA_OK;
+  if ((rc = check_tensor(q, ldq, H * kHd, "q")) || (rc = check_tensor(k, ldk, Hkv * kHd, "k")) ||
+      (rc = check_tensor(v, ldv, Hkv * kHd, "v")) || (rc = check_tensor(o, ldo, H * kHd, "o")))
+    return rc;
+  if (lse == nullptr) return set_error(LEMA_ERR_INVALID_ARGUMENT, "null lse");
+  AttnParams p = make_params(B, S, H, Hkv, scale);
+  if (p.err == nullptr) return set_error(LEMA_ERR_CUDA, "cannot resolve device error word");
+  p.lse = lse;
+  CUtensorMap mq, mk, mv, mo;
+  if ((rc = make_seq_map(&mq, q, B, S, H * kHd, ldq)) ||
+      (rc = make_seq_map(&mk, k, B, S, Hkv * kHd, ldk)) ||
+      (rc = make_seq_map(&mv, v, B, S, Hkv * kHd, ldv)) ||
+      (rc = make_seq_map(&mo, o, B, S, H * kHd, ldo)))
+    return rc;
+  static bool done[64] = {};
+  if ((rc = set_smem(attn_fwd_kernel, kFwdSmem, done))) return rc;
+  const int64_t ctas = B * H * p.q_tiles;
+  if (ctas > 0x7fffffff) return set_error(LEMA_ERR_INVALID_ARGUMENT, "too many tiles");
+  attn_fwd_kernel<<<static_cast<unsigned>(ctas), kFwdThreads, kFwdSmem,
+                    static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_attn_set_wait_budget(int64_t cycles) {
+  clear_error();
+  if (cycles < 0) return set_error(LEMA_ERR_INVALID_ARGUMENT, "cycles must be >= 0");
+  g_attn_budget.store(cycles == 0 ? ptx::kWaitBudgetCycles : static_cast<long long>(cycles));
+  return LEMA_OK;
+}
+
+extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                             const void* v, int64_t ldv, const void* o, int64_t ldo,
+                             const void* dout, int64_t lddo, const float* lse, float* delta,
+                             void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
+                             int64_t lddv, int64_t B, int64_t S, int64_t H, int64_t Hkv,
+                             int64_t head_dim, float scale, void* stream) {
+  clear_error();
+  int rc = check_attn(B, S, H, Hkv, head_dim);
+  if (rc) return rc;
+  if (B == 0 || S == 0) return LEMA_OK;
+  if ((rc = check_tensor(q, ldq, H * kHd, "q")) || (rc = check_tensor(k, ldk, Hkv * kHd, "k")) ||
+      (rc = check_tensor(v, ldv, Hkv * kHd, "v")) || (rc = check_tensor(o, ldo, H * kHd, "o")) ||
+      (rc = check_tensor(dout, lddo, H * kHd, "dout")) ||
+      (rc = check_tensor(dq, lddq, H * kHd, "dq")) ||
+      (rc = check_tensor(dk, lddk, Hkv * kHd, "dk")) ||
+      (rc = check_tensor(dv, lddv, Hkv * kHd, "dv")))
+    return rc;
+  if (lse == nullptr || delta == nullptr)
+    return set_error(LEMA_ERR_INVALID_ARGUMENT, "null lse or delta");
+  AttnParams p = make_params(B, S, H, Hkv, scale);
+  if (p.err == nullptr) return set_error(LEMA_ERR_CUDA, "cannot resolve device error word");
+  p.lse = const_cast<float*>(lse);
+  p.delta = delta;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
+  if ((rc = make_seq_map(&mq, q, B, S, H * kHd, ldq)) ||
+      (rc = make_seq_map(&mk, k, B, S, Hkv * kHd, ldk)) ||
+      (rc = make_seq_map(&mv, v, B, S, Hkv * kHd, ldv)) ||
+      (rc = make_seq_map(&mdo, dout, B, S, H * kHd, lddo)) ||
+      (rc = make_seq_map(&mdq, dq, B, S, H * kHd, lddq)) ||
+      (rc = make_seq_map(&mdk, dk, B, S, Hkv * kHd, lddk)) ||
+      (rc = make_seq_map(&mdv, dv, B, S, Hkv * kHd, lddv)))
+    return rc;
+  static bool done_kv[64] = {}, done_q[64] = {};
+  if ((rc = set_smem(attn_bwd_dkdv_kernel, kDkdvSmem, done_kv)) ||
+      (rc = set_smem(attn_bwd_dq_kernel, kDqSmem, done_q)))
+    return rc;
+  const int64_t q_ctas = B * H * p.q_tiles, kv_ctas = B * Hkv * p.q_tiles;
+  if (q_ctas > 0x7fffffff) return set_error(LEMA_ERR_INVALID_ARGUMENT, "too many tiles");
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t warps = B * S * H;
+  const int delta_blocks =
+      static_cast<int>(std::min<int64_t>((warps + 7) / 8, static_cast<int64_t>(device_sm_count()) * 16));
+  attn_delta_kernel<<<delta_blocks, 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo,
+      delta, static_cast<int>(B), static_cast<int>(S), static_cast<int>(H));
+  LEMA_CUDA_TRY(cudaGetLastError());
+  attn_bwd_dkdv_kernel<<<static_cast<unsigned>(kv_ctas), kBwdThreads, kDkdvSmem, s>>>(
+      mq, mk, mv, mdo, mdk, mdv, p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  attn_bwd_dq_kernel<<<static_cast<unsigned>(q_ctas), kBwdThreads, kDqSmem, s>>>(mq, mk, mv, mdo,
+                                                                                mdq, p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}

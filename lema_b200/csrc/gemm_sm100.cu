@@ -1491,6 +1491,8 @@ __global__ void error_snapshot_kernel(int32_t* host_word) {
 ScopedNoGemmWorkspace::ScopedNoGemmWorkspace() : prev(t_no_split) { t_no_split = true; }
 ScopedNoGemmWorkspace::~ScopedNoGemmWorkspace() { t_no_split = prev; }
 
+int32_t* gemm_error_word() { return gemm_err_ptr(); }
+
 int gemm_read_device_error(int32_t* out) {
   int32_t v = 0, zero = 0;
   LEMA_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(v)));

@@ -27,6 +27,9 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Per-translation-unit device error words: each .cu that launches kernels with
 // bounded waits exposes a reader that fetches and clears its word.
 int gemm_read_device_error(int32_t* out);
+// Device address of the GEMM's error word (also used by the attention kernels),
+// or null when it cannot be resolved on the current device.
+int32_t* gemm_error_word();
 int quant_read_device_error(int32_t* out);
 
 // Device-side error codes written into the error words.
@@ -36,6 +39,7 @@ enum DeviceErr : int32_t {
   kDevErrMmaTimeout = 0x102,
   kDevErrEpilogueTimeout = 0x103,
   kDevErrSplitTimeout = 0x104,  // a split tile's partial accumulators never arrived
+  kDevErrAttnTimeout = 0x105,   // an attention kernel's wait ran out
 };
 
 // While alive, GEMMs issued by this thread run every tile whole (no split-K

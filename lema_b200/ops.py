@@ -768,3 +768,52 @@ class RopeQKVFn(torch.autograd.Function):
         hq_, hk_, hv_ = ctx.has_add
         return (dqi, dki, dv, dqi if hq_ else None, dki if hk_ else None, dv if hv_ else None,
                 None, None, None, None, None, None)
+
+
+def attention_fwd(q2d: torch.Tensor, k2d: torch.Tensor, v2d: torch.Tensor, B: int, S: int,
+                  H: int, Hkv: int, scale: float):
+    """Causal attention on the tcgen05 kernel: q2d [B*S, H*128], k2d / v2d
+    [B*S, Hkv*128] token-major bf16 -> (o [B*S, H*128] bf16, lse [B, H, S] fp32
+    log2-domain log-sum-exp of the scaled scores)."""
+    dev = _require_cuda(q2d, k2d, v2d)
+    q2d, k2d, v2d = (_rows_view(t) for t in (q2d, k2d, v2d))
+    o = torch.empty(B * S, H * 128, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+    N.call("lema_attn_fwd", _ptr(q2d), _ld(q2d), _ptr(k2d), _ld(k2d), _ptr(v2d), _ld(v2d),
+           _ptr(o), H * 128, _ptr(lse), B, S, H, Hkv, 128, float(scale), _stream(dev))
+    return o, lse
+
+
+def attention_bwd(q2d, k2d, v2d, o2d, lse, dout2d, B: int, S: int, H: int, Hkv: int,
+                  scale: float):
+    """(dq [B*S, H*128], dk, dv [B*S, Hkv*128]) of attention_fwd."""
+    dev = _require_cuda(q2d, k2d, v2d, o2d, lse, dout2d)
+    q2d, k2d, v2d, o2d = (_rows_view(t) for t in (q2d, k2d, v2d, o2d))
+    dout2d = _rows_view(dout2d.to(torch.bfloat16))
+    dq = torch.empty(B * S, H * 128, dtype=torch.bfloat16, device=dev)
+    dk = torch.empty(B * S, Hkv * 128, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty(B * S, Hkv * 128, dtype=torch.bfloat16, device=dev)
+    delta = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+    N.call("lema_attn_bwd", _ptr(q2d), _ld(q2d), _ptr(k2d), _ld(k2d), _ptr(v2d), _ld(v2d),
+           _ptr(o2d), _ld(o2d), _ptr(dout2d), _ld(dout2d), _ptr(lse.contiguous()), _ptr(delta),
+           _ptr(dq), H * 128, _ptr(dk), Hkv * 128, _ptr(dv), Hkv * 128, B, S, H, Hkv, 128,
+           float(scale), _stream(dev))
+    return dq, dk, dv
+
+
+class AttentionFn(torch.autograd.Function):
+    """Causal attention (head_dim 128, GQA) on the tcgen05 kernels over the
+    token-major q [B*S, H*128], k / v [B*S, Hkv*128]; returns o [B*S, H*128]."""
+
+    @staticmethod
+    def forward(ctx, q2d, k2d, v2d, B, S, H, Hkv, scale):
+        o, lse = attention_fwd(q2d, k2d, v2d, B, S, H, Hkv, scale)
+        ctx.save_for_backward(q2d, k2d, v2d, o, lse)
+        ctx.meta = (B, S, H, Hkv, scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q2d, k2d, v2d, o, lse = ctx.saved_tensors
+        dq, dk, dv = attention_bwd(q2d, k2d, v2d, o, lse, do, *ctx.meta)
+        return dq, dk, dv, None, None, None, None, None

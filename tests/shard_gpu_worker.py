@@ -37,6 +37,37 @@ def run(shape, dev, rank, shard):
     return losses, params, chunk
 
 
+def stream_check(shape, dev, rank):
+    """Streaming alone: the same random segments packed sharded and unsharded;
+    after upload (+ all-gather) every slot byte equals the unsharded segment."""
+    from lema_b200.tensorstore import WeightSegments
+    blocks = 3
+    g = torch.Generator(device="cpu").manual_seed(5)
+    own = WeightSegments(shape, blocks, dev)
+    sh = WeightSegments(shape, blocks, dev, shard_group=dist.group.WORLD)
+    segs = [torch.randint(0, 256, (own.seg_bytes,), generator=g, dtype=torch.uint8)
+            for _ in range(blocks)]
+    for b in range(blocks):
+        own.ram[b].copy_(segs[b])
+        buf = sh.staging(b)
+        buf.zero_()
+        buf[:sh.seg_bytes].copy_(segs[b].to(dev))
+        sh.commit(b)
+    sh.drop_staging()
+    ok = True
+    for b in range(blocks):
+        slot = b % sh.num_slots
+        sh.upload(b, slot)
+        sh.acquire(slot)
+        torch.cuda.synchronize(dev)
+        ok &= bool(torch.equal(sh.vram[slot][:sh.seg_bytes].cpu(), segs[b]))
+        sh.release(slot)
+    torch.cuda.synchronize(dev)
+    own.close()
+    sh.close()
+    return ok
+
+
 def main(out_path):
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -49,9 +80,13 @@ def main(out_path):
         l_sh, p_sh, c_sh = run(shape, dev, rank, True)
         same = l_own == l_sh and all(torch.equal(a.view(torch.int16), b.view(torch.int16))
                                      for a, b in zip(p_own, p_sh))
-        flag = torch.tensor([1.0 if same else 0.0], device=dev)
+        streams = stream_check(shape, dev, rank)
+        flag = torch.tensor([1.0 if same else 0.0, 1.0 if streams else 0.0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        report[name] = {"same": bool(flag.item() == 1.0), "losses": l_sh,
+        diff = max(float((a.float() - b.float()).abs().max()) for a, b in zip(p_own, p_sh))
+        report[name] = {"same": bool(flag[0].item() == 1.0),
+                        "stream_bytes_equal": bool(flag[1].item() == 1.0),
+                        "losses": l_sh, "losses_own": l_own, "max_param_diff": diff,
                         "chunk_bytes": c_sh, "segment_bytes": c_own}
     if rank == 0:
         torch.save(report, out_path)

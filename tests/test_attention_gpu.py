@@ -1,0 +1,98 @@
+"""The tcgen05 causal attention against an fp32 restatement of the torch op it
+replaces (scaled_dot_product_attention(q, k, v, is_causal=True, scale=d**-0.5,
+enable_gqa=...)) on the same bf16 inputs. The bar is set by torch's own bf16
+SDPA: the kernel's error against the fp32 result stays within twice SDPA's
+(plus a floor of one bf16 ulp at the output's scale), and its log-sum-exp
+matches the fp32 one to 1e-3 (log2 units)."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from lema_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+
+
+def _inputs(B, S, H, Hkv, seed, dev):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(B * S, H * D, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B * S, Hkv * D, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(B * S, Hkv * D, generator=g).to(torch.bfloat16).to(dev)
+    return q, k, v
+
+
+def _heads(t, B, S, n):
+    return t.view(B, S, n, D).transpose(1, 2)
+
+
+def _ref_fp32(q, k, v, B, S, H, Hkv):
+    """fp32 causal attention and the log2-domain log-sum-exp of the scaled scores."""
+    qh, kh, vh = (_heads(t.float(), B, S, n) for t, n in ((q, H), (k, Hkv), (v, Hkv)))
+    kh = kh.repeat_interleave(H // Hkv, dim=1)
+    vh = vh.repeat_interleave(H // Hkv, dim=1)
+    s = (qh @ kh.transpose(-1, -2)) * D ** -0.5
+    mask = torch.ones(S, S, dtype=torch.bool, device=q.device).triu(1)
+    s = s.masked_fill(mask, float("-inf"))
+    lse2 = torch.logsumexp(s, dim=-1) / math.log(2.0)
+    o = torch.softmax(s, dim=-1) @ vh
+    return o, lse2
+
+
+SHAPES = [(1, 128, 1, 1), (2, 256, 4, 2), (1, 200, 2, 2), (2, 512, 8, 2), (1, 2048, 4, 1),
+          (3, 77, 2, 1)]
+
+
+@pytest.mark.parametrize("B,S,H,Hkv", SHAPES)
+def test_forward_matches_fp32_within_sdpa_error(cuda_device, B, S, H, Hkv):
+    q, k, v = _inputs(B, S, H, Hkv, B * 1000 + S + H, cuda_device)
+    o, lse = ops.attention_fwd(q, k, v, B, S, H, Hkv, D ** -0.5)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = _ref_fp32(q, k, v, B, S, H, Hkv)
+    o_sdpa = F.scaled_dot_product_attention(_heads(q, B, S, H), _heads(k, B, S, Hkv),
+                                            _heads(v, B, S, Hkv), is_causal=True,
+                                            scale=D ** -0.5, enable_gqa=H != Hkv)
+    got = _heads(o, B, S, H).float()
+    err = (got - o_ref).abs().max().item()
+    err_sdpa = (o_sdpa.float() - o_ref).abs().max().item()
+    floor = 2 ** -8 * o_ref.abs().max().item()
+    assert err <= 2 * err_sdpa + floor, (err, err_sdpa)
+    assert torch.isfinite(got).all()
+    assert (lse - lse_ref).abs().max().item() <= 1e-3
+
+
+BWD_SHAPES = [(1, 128, 1, 1), (2, 256, 4, 2), (1, 200, 2, 2), (2, 512, 8, 2), (1, 2048, 4, 1),
+              (3, 77, 2, 1)]
+
+
+@pytest.mark.parametrize("B,S,H,Hkv", BWD_SHAPES)
+def test_backward_matches_fp32_within_sdpa_error(cuda_device, B, S, H, Hkv):
+    """dq, dk, dv against fp32 autograd of the same op; the bar is twice torch
+    bf16 SDPA's own error on the same gradients plus one bf16 ulp at scale."""
+    q, k, v = _inputs(B, S, H, Hkv, 7 * S + H, cuda_device)
+    g = torch.Generator(device="cpu").manual_seed(S + 3)
+    do = torch.randn(B * S, H * D, generator=g).to(torch.bfloat16).to(cuda_device)
+    qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = ops.AttentionFn.apply(qg, kg, vg, B, S, H, Hkv, D ** -0.5)
+    o.backward(do)
+    torch.cuda.synchronize()
+
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    o_ref, _ = _ref_fp32(qf, kf, vf, B, S, H, Hkv)
+    o_ref.transpose(1, 2).reshape(B * S, H * D).backward(do.float())
+
+    qs, ks, vs = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o_s = F.scaled_dot_product_attention(_heads(qs, B, S, H), _heads(ks, B, S, Hkv),
+                                         _heads(vs, B, S, Hkv), is_causal=True,
+                                         scale=D ** -0.5, enable_gqa=H != Hkv)
+    o_s.transpose(1, 2).reshape(B * S, H * D).backward(do)
+    for name, got, ref, sd in (("dq", qg.grad, qf.grad, qs.grad), ("dk", kg.grad, kf.grad, ks.grad),
+                               ("dv", vg.grad, vf.grad, vs.grad)):
+        assert torch.isfinite(got).all(), name
+        err = (got.float() - ref).abs().max().item()
+        err_sdpa = (sd.float() - ref).abs().max().item()
+        floor = 2 ** -8 * ref.abs().max().item()
+        assert err <= 2 * err_sdpa + floor, (name, err, err_sdpa)

@@ -59,8 +59,9 @@ def test_sharded_weight_stream_equals_own_segments(cuda_device, tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     rep = torch.load(out)
     for name, v in rep.items():
-        assert v["same"], (name, v)
         assert v["chunk_bytes"] * 2 >= v["segment_bytes"] > v["chunk_bytes"], (name, v)
+    assert all(v["stream_bytes_equal"] for v in rep.values()), rep
+    assert all(v["same"] for v in rep.values()), rep
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
