@@ -562,7 +562,7 @@ def run_train(args, world, rank, local) -> dict | None:
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
                                  weight_shard=shard, vram_slots=args.vram_slots,
-                                 ckpt_mode=CKPT_MODES[args.ckpt])
+                                 ckpt_mode=CKPT_MODES[args.ckpt], attn_impl=args.attn)
         workload = (f"mixtral_streamed_lora: {shape.layers} x [hidden 4096, 32 q / 8 kv heads "
                     "x 128, 8 experts x SwiGLU 14336, top-2 softmax routing], vocab 32000, LoRA "
                     "r16 a32 on q/v, W8A8 attention projections and grouped W8A8 experts "
@@ -575,7 +575,8 @@ def run_train(args, world, rank, local) -> dict | None:
         last4 = tuple(range(max(0, shape.layers - 4), shape.layers))
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, targets=(), seed=0,
                                  resident_layers=args.resident_layers, attn_chunk=512,
-                                 full_ft_layers=last4, ckpt_mode=CKPT_MODES[args.ckpt])
+                                 full_ft_layers=last4, ckpt_mode=CKPT_MODES[args.ckpt],
+                                 attn_impl=args.attn)
         workload = (f"llama7b_selective_ft_2048: {shape.layers} x [hidden 4096, 32x128 heads, "
                     "MLP 11008], vocab 32000, bs 1 x seq 2048, 512-token chunked causal "
                     "attention, W8A8 projections streamed from pinned RAM, activation "
@@ -586,7 +587,7 @@ def run_train(args, world, rank, local) -> dict | None:
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
                                  weight_shard=shard, vram_slots=args.vram_slots,
-                                 ckpt_mode=CKPT_MODES[args.ckpt])
+                                 ckpt_mode=CKPT_MODES[args.ckpt], attn_impl=args.attn)
         workload = (f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 heads, MLP "
                     "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections streamed "
                     "from pinned RAM, activation checkpoints offloaded")
@@ -717,6 +718,7 @@ def run_train(args, world, rank, local) -> dict | None:
                    "resident_layers": args.resident_layers,
                    "vram_slots": args.vram_slots,
                    "dgrad": args.dgrad,
+                   "attention": args.attn,
                    "checkpoints": args.ckpt,
                    "weight_stream": ("sharded: 1/N of each segment per rank over PCIe, NCCL "
                                      "all-gather over NVLink" if shard else
@@ -982,6 +984,9 @@ def main():
     ap.add_argument("--dgrad", choices=["bf16", "int8"], default="bf16",
                     help="straight-through dgrad of the frozen projections: bf16 (the "
                          "operator contract, default) or the opt-in int8-dy variant")
+    ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
+                    help="block attention: torch SDPA (default) or this library's tcgen05 "
+                         "kernels (opt-in, head_dim 128)")
     ap.add_argument("--ckpt", choices=list(CKPT_MODES), default="host",
                     help="boundary activations: host (offloaded to pinned host by the copy "
                          "engine, default), host-kernel (offloaded by the SM store kernel) or "

@@ -49,6 +49,7 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "quant_core.cuh"
 
 namespace lema {
 namespace {
@@ -118,8 +119,11 @@ __device__ __forceinline__ float ex2(float x) {
   return r;
 }
 
-// Named barrier over the 128 threads of warps 2..5.
+// Named barrier over the 128 threads of warps 2..5 (backward kernels).
 __device__ __forceinline__ void sync_rows() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Named barrier over the 256 row threads of the forward (warps 2..9).
+__device__ __forceinline__ void sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // S or dP = A B^T over head_dim: A, B both [128 x 128] K-major tiles.
 __device__ __forceinline__ void mma_tile_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
@@ -154,17 +158,10 @@ __device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, lo
   return __all_sync(0xffffffffu, r);
 }
 
-// 128 fp32 columns of this thread's TMEM lane, [col, col + 128).
-__device__ __forceinline__ void tmem_row128(uint32_t taddr, uint32_t (&v)[4][32]) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) ptx::tmem_ld_32x32b_x32(taddr + c * 32, v[c]);
-  ptx::tmem_ld_wait();
-}
-
 // ------------------------------------------------------------------ forward
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 320;  // producer, MMA issuer, 8 row warps
 constexpr int kFwdBars = 18;
-constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 1024;
+constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 2 * kTile * 4 + 1024;
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
@@ -190,6 +187,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kFwdBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* xch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row-half exchange
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -208,8 +206,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     ptx::prefetch_tmap(&mo);
     for (int i = 0; i < kFwdBars; ++i) ptx::mbar_init(&bars[i], 1);
     for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(&s_free[s], 128);  // every row thread arrives
-      ptx::mbar_init(&p_full[s], 128);
+      ptx::mbar_init(&s_free[s], 256);  // every row thread arrives
+      ptx::mbar_init(&p_full[s], 256);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -300,84 +298,107 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax rows (warps 2..5) ----------------
+    // ---------------- softmax rows (warps 2..9): two threads per query row ----------------
+    // Warps w and w + 4 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..); warps
+    // 2..5 take score / O columns [0, 64) of their rows, warps 6..9 [64, 128).
+    // The halves of a row exchange their partial maxima (and, at the end, their
+    // sums) through shared memory. A thread whose wait fails keeps passing the
+    // named barriers with its work skipped, so no row warp is left waiting.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    const int c0 = half * 64;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float m_run = -INFINITY, l = 0.f;
+    const uint64_t c2 = f2_splat(p.scale_log2);
+    float m_run = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
-      if (!wait_bar_warp(&s_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
-      uint32_t v[4][32];
-      tmem_row128(trow + s * 128, v);
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&s_free[s]);
-      const bool diag = j == qt;
-      float tmax = -INFINITY;
+      uint32_t v[2][32];
+      float pmax = -INFINITY;
+      if (ok && wait_bar_warp(&s_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
+        ptx::tc_fence_after();
+        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0, v[0]);
+        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0 + 32, v[1]);
+        ptx::tmem_ld_wait();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&s_free[s]);
+        if (j == qt) {  // diagonal tile: keys after the query are masked
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+          for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c0 + k * 32 + i > row) v[k][i] = 0xff800000u;  // -inf
+        }
+        float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(v[c4][i]) * p.scale_log2;
-          if (diag && c4 * 32 + i > row) x = -INFINITY;
-          v[c4][i] = __float_as_uint(x);
-          tmax = fmaxf(tmax, x);
+          m0 = fmaxf(m0, __uint_as_float(v[0][i]));
+          m1 = fmaxf(m1, __uint_as_float(v[1][i]));
         }
+        pmax = fmaxf(m0, m1);
+      } else {
+        ok = false;
       }
+      xch[half * kTile + row] = pmax;
+      sync_softmax();
+      const float smax = fmaxf(pmax, xch[(half ^ 1) * kTile + row]);
+      sync_softmax();  // the partner has read it before the next tile writes
+      if (!ok) continue;
+      const float tmax = smax * p.scale_log2;  // scale > 0: max commutes with it
       const bool need = tmax > m_run + kRescaleLog2;
       const float m_new = need ? tmax : m_run;
       const float alpha = need ? ex2(m_run - m_new) : 1.f;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O *= alpha on this warp's rows, once P_{j-1} V_{j-1} has landed
+        // O *= alpha on this thread's half row, once P_{j-1} V_{j-1} has landed
         if (!wait_bar_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.budget, abort_flag)) {
           ok = false;
-          break;
+          continue;
         }
         ptx::tc_fence_after();
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int k = 0; k < 2; ++k) {
           uint32_t o[32];
-          ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, o);
+          ptx::tmem_ld_32x32b_x32(trow + 256 + c0 + k * 32, o);
           ptx::tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          ptx::tmem_st_32x32b_x32(trow + 256 + c4 * 32, o);
+          ptx::tmem_st_32x32b_x32(trow + 256 + c0 + k * 32, o);
         }
         ptx::tmem_st_wait();
       }
       l *= alpha;
       m_run = m_new;
-      float rsum = 0.f;
+      // P = 2^(s c - m): the scaling and the sum two columns per instruction
+      const uint64_t negm2 = f2_splat(-m_run);
+      uint64_t acc = f2_splat(0.f);
+      uint32_t pk[32];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int k = 0; k < 2; ++k) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = ex2(__uint_as_float(v[c4][i]) - m_run);
-          rsum += e;
-          v[c4][i] = __float_as_uint(e);
+        for (int i = 0; i < 16; ++i) {
+          float ta, tb;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(v[k][2 * i]), __uint_as_float(v[k][2 * i + 1])),
+                           c2, negm2),
+                    ta, tb);
+          const float ea = ex2(ta), eb = ex2(tb);
+          acc = f2_add(acc, f2_pack(ea, eb));
+          pk[k * 16 + i] = pack_bf16x2(ea, eb);
         }
       }
-      l += rsum;
+      float s_lo, s_hi;
+      f2_unpack(acc, s_lo, s_hi);
+      l += s_lo + s_hi;
       // P_j goes to slot s once P_{j-2} V_{j-2} has read it
       if (j >= 2 && !wait_bar_warp(&pv_done[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
         ok = false;
-        break;
+        continue;
       }
       const uint32_t pbase = ptx::smem_u32(sp + s * kTileBytes);
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        const uint32_t* e = &v[c8 >> 2][(c8 & 3) * 8];
-        st_shared_v4(pbase + swz_chunk(row, c8 * 8),
-                     pack_bf16x2(__uint_as_float(e[0]), __uint_as_float(e[1])),
-                     pack_bf16x2(__uint_as_float(e[2]), __uint_as_float(e[3])),
-                     pack_bf16x2(__uint_as_float(e[4]), __uint_as_float(e[5])),
-                     pack_bf16x2(__uint_as_float(e[6]), __uint_as_float(e[7])));
-      }
+      for (int cc = 0; cc < 8; ++cc)
+        st_shared_v4(pbase + swz_chunk(row, c0 + cc * 8), pk[cc * 4], pk[cc * 4 + 1],
+                     pk[cc * 4 + 2], pk[cc * 4 + 3]);
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       ptx::mbar_arrive(&p_full[s]);
@@ -386,21 +407,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (ok && !wait_bar_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.budget,
                              abort_flag))
       ok = false;
+    xch[half * kTile + row] = l;
+    sync_softmax();
+    const float l_row = l + xch[(half ^ 1) * kTile + row];
     if (!ok) {
       record_err(p.err, kDevErrAttnTimeout, abort_flag);
     } else {
       ptx::tc_fence_after();
-      const float inv_l = 1.f / l;
+      const float inv_l = 1.f / l_row;
       const uint32_t obase = ptx::smem_u32(sq);
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int k = 0; k < 2; ++k) {
         uint32_t o[32];
-        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, o);
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c0 + k * 32, o);
         ptx::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint32_t* e = &o[i * 8];
-          st_shared_v4(obase + swz_chunk(row, c4 * 32 + i * 8),
+          st_shared_v4(obase + swz_chunk(row, c0 + k * 32 + i * 8),
                        pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
                        pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
                        pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
@@ -408,10 +432,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
       const int q = q0 + row;
-      if (q < p.S) p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l);
+      if (half == 0 && q < p.S)
+        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l_row);
     }
     ptx::fence_proxy_async_smem();
-    sync_rows();
+    sync_softmax();
     if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
       ptx::tma_store_3d(&mo, sq, h * kHd, q0, b);
       ptx::tma_store_3d(&mo, sq + kBox, h * kHd + 64, q0, b);

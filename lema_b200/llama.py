@@ -10,8 +10,10 @@ checkpoints and the reference's name-based weight mapping
 (src/lema/adapters/_llama.py:41-57, 118-151) line up.
 
 Attention runs through ``torch.nn.functional.scaled_dot_product_attention``
-with ``is_causal=True`` (bf16 flash kernel on the GPU); it is not part of the
-W8A8 path.
+with ``is_causal=True`` (bf16 flash kernel on the GPU) by default; with
+``attn_impl = "tcgen05"`` (opt-in, head_dim 128) it runs on this library's own
+tensor-core kernels (``ops.AttentionFn``) straight from the token-major q / k / v.
+It is not part of the W8A8 path.
 """
 from __future__ import annotations
 
@@ -132,11 +134,23 @@ def _chunked_causal_attention(q, k, v, scale, chunk, gqa):
     return torch.cat(outs, dim=2)
 
 
+def _tc_attention(q2d, k2d, v2d, B: int, S: int, shape: LlamaShape) -> torch.Tensor:
+    """Causal attention of token-major q [B*S, H*d], k / v [B*S, Hkv*d] on the
+    tcgen05 kernels; returns o [B*S, H*d]."""
+    if shape.head_dim != 128:
+        raise ValueError(f"attn_impl='tcgen05' needs head_dim 128, got {shape.head_dim}")
+    from . import ops
+    return ops.AttentionFn.apply(q2d, k2d, v2d, B, S, shape.heads, shape.kv_heads,
+                                 shape.head_dim ** -0.5)
+
+
 class LlamaAttention(nn.Module):
     def __init__(self, shape: LlamaShape, quantized: bool, device=None, dtype=torch.bfloat16):
         super().__init__()
         self.shape = shape
-        self.attn_impl = "sdpa"  # "eager" reproduces HF eager attention op for op
+        # "sdpa"; "eager" reproduces HF eager attention op for op; "tcgen05" runs
+        # this library's attention kernels (head_dim 128)
+        self.attn_impl = "sdpa"
         self.attn_chunk = 0      # > 0: exact attention in query chunks of this many tokens
         ps = shape.proj_shapes()
         for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
@@ -149,6 +163,11 @@ class LlamaAttention(nn.Module):
         k = self.k_proj(h).view(B, S, -1, d).transpose(1, 2)
         v = self.v_proj(h).view(B, S, -1, d).transpose(1, 2)
         q, k = apply_rope(q, k, cos, sin)
+        if self.attn_impl == "tcgen05":
+            o2d = _tc_attention(q.transpose(1, 2).reshape(B * S, -1),
+                                k.transpose(1, 2).reshape(B * S, -1),
+                                v.transpose(1, 2).reshape(B * S, -1), B, S, self.shape)
+            return self.o_proj(o2d.view(B, S, -1))
         if self.attn_impl == "eager":
             o = _eager_causal_attention(q, k, v, d ** -0.5)
         elif self.attn_chunk and S > self.attn_chunk:
@@ -206,7 +225,7 @@ class LlamaBlock(nn.Module):
     def _can_fuse(self) -> bool:
         if not (self.use_fused and self.fused_weights is not None):
             return False
-        if self.gradient_checkpointing or self.self_attn.attn_impl != "sdpa":
+        if self.gradient_checkpointing or self.self_attn.attn_impl not in ("sdpa", "tcgen05"):
             return False
         for name in self.FUSABLE:
             m = self.projection(name)
@@ -277,6 +296,8 @@ class LlamaBlock(nn.Module):
         qv = qr.view(B, S, sh.heads, d).transpose(1, 2)
         kv = kr.view(B, S, sh.kv_heads, d).transpose(1, 2)
         vv = vc.view(B, S, sh.kv_heads, d).transpose(1, 2)
+        if att.attn_impl == "tcgen05":  # exact at any length: no query chunks needed
+            return h + att.o_proj(_tc_attention(qr, kr, vc, B, S, sh)).view(B, S, H)
         gqa = sh.heads != sh.kv_heads
         if att.attn_chunk and S > att.attn_chunk:
             o = _chunked_causal_attention(qv, kv, vv, d ** -0.5, att.attn_chunk, gqa)

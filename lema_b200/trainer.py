@@ -94,7 +94,7 @@ class StreamedLoraTrainer:
                  full_ft_layers: tuple[int, ...] = (),
                  full_ft_modules: tuple[str, ...] = ("q_proj", "k_proj", "v_proj", "o_proj"),
                  group=None, weight_shard: bool = False, vram_slots: int = 2,
-                 weights: str | None = None):
+                 weights: str | None = None, attn_impl: str = "sdpa"):
         self.shape = shape
         self.device = torch.device(device)
         self.batch, self.seq = batch, seq
@@ -166,6 +166,7 @@ class StreamedLoraTrainer:
                 apply_lora(blk, lora_rank, lora_alpha, targets)
             blk.gradient_checkpointing = gradient_checkpointing
             blk.self_attn.attn_chunk = attn_chunk
+            blk.self_attn.attn_impl = attn_impl
         # LoRA parameters per layer, reference init (A kaiming-uniform, B zeros)
         self.lora: list[dict[str, tuple[nn.Parameter, nn.Parameter]]] = []
         for _ in range(self.L):
