@@ -36,28 +36,33 @@ def _ev_ptr(ev: torch.cuda.Event | None):
 
 
 class ActivationCheckpointStore:
-    """``num`` pinned host slots of ``shape`` (bf16 by default).
+    """``num`` checkpoint slots of ``shape`` (bf16 by default): slots
+    [0, device_slots) stay in device memory, the others go to pinned host slots.
 
-    ``mode`` 0 saves through the copy engine, 1 through the SM store kernel
-    (``lema_ckpt_save``); mode 2 keeps the boundary tensors in device memory
-    instead (the reference's ``boundary_activations`` list,
+    ``mode`` 0 saves the host slots through the copy engine, 1 through the SM
+    store kernel (``lema_ckpt_save``); mode 2 keeps every boundary tensor in
+    device memory (the reference's ``boundary_activations`` list,
     src/lema/_trainer.py:109-111): no host slots, no copies."""
 
     DEVICE = 2
 
     def __init__(self, num: int, shape: tuple[int, ...], device: torch.device,
                  dtype: torch.dtype = torch.bfloat16, mode: int = 0,
-                 h2d_stream: torch.cuda.Stream | None = None):
+                 h2d_stream: torch.cuda.Stream | None = None, device_slots: int = 0):
         if mode not in (0, 1, self.DEVICE):
             raise ValueError(f"checkpoint mode must be 0, 1 or 2, not {mode}")
         self.device = torch.device(device)
         self.shape = tuple(shape)
         self.dtype = dtype
+        self.device_slots = num if mode == self.DEVICE else max(0, min(int(device_slots), num))
+        if self.device_slots == num:
+            mode = self.DEVICE
         self.mode = mode
+        self.host_slots = num - self.device_slots
         self._kept: dict[int, torch.Tensor] = {}
         if mode == self.DEVICE:
             self.host = None
-            self.nbytes = 0  # bytes moved per slot and direction
+            self.nbytes = 0  # bytes moved per host slot and direction
             self._dev_buf: dict[int, torch.Tensor] = {}
             return
         self.host = torch.empty((num, *shape), dtype=dtype).pin_memory()
@@ -74,7 +79,7 @@ class ActivationCheckpointStore:
             raise ValueError(f"checkpoint slot holds {self.shape} {self.dtype}, got "
                              f"{tuple(t.shape)} {t.dtype}")
         t = t.detach()
-        if self.mode == self.DEVICE:
+        if i < self.device_slots:
             self._kept[i] = t
             return
         if not t.is_contiguous():
@@ -88,7 +93,7 @@ class ActivationCheckpointStore:
     def restore_async(self, i: int) -> torch.Tensor:
         """Starts the H2D copy of slot i into a device buffer and returns the buffer;
         call ``wait(i)`` on the consuming stream before reading it."""
-        if self.mode == self.DEVICE:
+        if i < self.device_slots:
             self._dev_buf[i] = self._kept.pop(i)
             return self._dev_buf[i]
         buf = torch.empty(self.shape, dtype=self.dtype, device=self.device)
@@ -102,11 +107,16 @@ class ActivationCheckpointStore:
         return buf
 
     def wait(self, i: int, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-        if self.mode == self.DEVICE:
+        if i < self.device_slots:
             return self._dev_buf.pop(i)
         s = stream or torch.cuda.current_stream(self.device)
         s.wait_event(self.restored[i])
         return self._dev_buf.pop(i)
+
+    @property
+    def moved_bytes(self) -> int:
+        """Bytes copied per step and direction (the host slots)."""
+        return self.nbytes * self.host_slots
 
     def restore(self, i: int) -> torch.Tensor:
         self.restore_async(i)

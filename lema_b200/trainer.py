@@ -7,8 +7,11 @@
   from pinned RAM into one of two VRAM slots by the native manager's copy
   stream while block i-1 computes; the block's W8A8 projections are bound to
   views of the slot (no parameter copy, unlike src/lema/adapters/_llama.py:
-  95-100); the block's input is saved to a pinned host slot on a D2H stream
-  (the reference keeps it in VRAM, :109-111, which ``ckpt_mode=2`` selects);
+  95-100); the block's input is kept in VRAM as the reference keeps it
+  (:109-111) while the layers' inputs fit an HBM budget (by default a quarter
+  of the memory free when the trainer is built); past the budget the
+  remaining layers' inputs go to pinned host slots on a D2H stream
+  (``ckpt_mode`` 0 / 1 offload every layer, 2 keeps every layer in VRAM);
 * head + loss (reference :151-162): final RMSNorm, bf16 lm_head, shifted
   cross entropy, backward to the last hidden state;
 * backward in reverse (reference :125-173): the saved input is restored on the
@@ -88,7 +91,8 @@ class LoraGradReducer:
 class StreamedLoraTrainer:
     def __init__(self, shape: LlamaShape, device, batch: int, seq: int, lora_rank: int = 16,
                  lora_alpha: float = 32.0, targets: tuple[str, ...] = ("q_proj", "v_proj"),
-                 lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0, ckpt_mode: int = 0,
+                 lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0,
+                 ckpt_mode: int | None = None, ckpt_hbm_budget: int | None = None,
                  resident_layers: int = 0, grad_accum: int = 1,
                  gradient_checkpointing: bool = False, attn_chunk: int = 0,
                  full_ft_layers: tuple[int, ...] = (),
@@ -188,8 +192,17 @@ class StreamedLoraTrainer:
             self.full_ft = SelectiveFullFT(self.ws, sorted({b for b, _ in true_weights}),
                                            full_ft_modules, true_weights, dev, lr, weight_decay)
             del true_weights
+        per_layer = batch * seq * shape.hidden * 2  # one bf16 boundary activation
+        if ckpt_mode is None:  # keep what fits the HBM budget, offload the rest
+            budget = (ckpt_hbm_budget if ckpt_hbm_budget is not None
+                      else torch.cuda.mem_get_info(dev)[0] // 4)
+            mode = 0
+        else:
+            budget = ckpt_hbm_budget or 0
+            mode = ckpt_mode
         self.ckpt = ActivationCheckpointStore(self.L, (batch, seq, shape.hidden), dev,
-                                              mode=ckpt_mode, h2d_stream=self.ws.h2d_stream)
+                                              mode=mode, h2d_stream=self.ws.h2d_stream,
+                                              device_slots=int(budget // per_layer))
         self.cos, self.sin = rope_cos_sin(shape, seq, dev, torch.bfloat16)
         self.reducer = LoraGradReducer(group)
         # device-side failures (a bounded wait in a kernel that ran out) are

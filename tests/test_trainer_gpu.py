@@ -112,21 +112,23 @@ def test_streamed_equals_hbm_resident(cuda_device):
 
 def test_trainer_kernel_mode_checkpoint(cuda_device):
     """Boundary activations saved by the SM store kernel (mode 1) instead of the
-    copy engine, or kept in device memory (mode 2, no offload), give the same
-    step."""
+    copy engine, kept in device memory (mode 2, no offload), or split by an HBM
+    budget (two layers kept, the rest offloaded) give the same step."""
     ids = _ids(13, 2, 64, SMALL.vocab, cuda_device)
-    out = []
-    for mode in (0, 1, 2):
+    per_layer = 2 * 64 * SMALL.hidden * 2
+    runs = []
+    for mode, budget in ((0, None), (1, None), (2, None), (None, 2 * per_layer)):
         tr = StreamedLoraTrainer(SMALL, cuda_device, batch=2, seq=64, lr=1e-3, seed=2,
-                                 ckpt_mode=mode)
+                                 ckpt_mode=mode, ckpt_hbm_budget=budget)
+        if budget is not None:
+            assert (tr.ckpt.device_slots, tr.ckpt.host_slots) == (2, tr.L - 2)
         with sdpa_kernel(SDPBackend.MATH):
-            out.append(float(tr.train_step(ids)))
-        out.append([p.detach().clone() for p in tr.params])
+            runs.append((float(tr.train_step(ids)), [p.detach().clone() for p in tr.params]))
         tr.close()
-    assert out[0] == out[2] == out[4]
-    for a, b, c in zip(out[1], out[3], out[5]):
-        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
-        assert torch.equal(a.view(torch.int16), c.view(torch.int16))
+    for loss, params in runs[1:]:
+        assert loss == runs[0][0]
+        for a, b in zip(runs[0][1], params):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
 def test_attention_checkpointing_gives_the_same_step(cuda_device):
