@@ -1,10 +1,11 @@
 """Micro-benchmarks of single kernels on one GPU (CUDA events, median of the
 repetitions), printing one JSON line per case.
 
-    python -m lema_b200.kernel_bench attention [small]
+    python -m lema_b200.kernel_bench attention [small | long]
         the tcgen05 causal attention (ops.attention_fwd / attention_bwd) beside
-        torch SDPA at the training shapes; ``small`` runs B 2, S 512, H 8 once
-        per direction set (the shape the attention ncu captures use)
+        torch SDPA at the training shapes; ``small`` runs B 2, S 512, H 8 and
+        ``long`` B 1, S 4096, H 16, Hkv 4 only (the shapes the attention ncu
+        captures use: latency, and throughput)
     python -m lema_b200.kernel_bench producers
         K1 (quantize_rows), RMSNorm -> quantise and SwiGLU -> quantise at
         M = 4096 tokens, each beside a device copy moving the same bytes; the L2
@@ -42,10 +43,10 @@ def _time_us(fn, reps: int = 7, flush: torch.Tensor | None = None) -> float:
     return statistics.median(ts)
 
 
-def attention(small: bool) -> None:
+def attention(which: str) -> None:
     dev = torch.device("cuda:0")
-    shapes = ([(2, 512, 8, 8)] if small else
-              [(8, 512, 32, 32), (8, 512, 32, 8), (1, 2048, 32, 32), (2, 4096, 32, 8)])
+    shapes = {"small": [(2, 512, 8, 8)], "long": [(1, 4096, 16, 4)]}.get(
+        which, [(8, 512, 32, 32), (8, 512, 32, 8), (1, 2048, 32, 32), (2, 4096, 32, 8)])
     for B, S, H, Hkv in shapes:
         q = torch.randn(B * S, H * D, device=dev).to(torch.bfloat16)
         k = torch.randn(B * S, Hkv * D, device=dev).to(torch.bfloat16)
@@ -109,9 +110,10 @@ def producers() -> None:
 
 def main(argv: list[str]) -> None:
     if not argv or argv[0] not in ("attention", "producers"):
-        raise SystemExit("usage: python -m lema_b200.kernel_bench {attention [small] | producers}")
+        raise SystemExit("usage: python -m lema_b200.kernel_bench "
+                         "{attention [small | long] | producers}")
     if argv[0] == "attention":
-        attention(len(argv) > 1 and argv[1] == "small")
+        attention(argv[1] if len(argv) > 1 else "")
     else:
         producers()
     if _native.device_error() != 0:
