@@ -122,8 +122,45 @@ __device__ __forceinline__ float ex2(float x) {
 // Named barrier over the 128 threads of warps 2..5 (backward kernels).
 __device__ __forceinline__ void sync_rows() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Named barrier over the 256 row threads of the forward (warps 2..9).
-__device__ __forceinline__ void sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier over the 512 row threads of the forward (warps 2..17).
+__device__ __forceinline__ void sync_softmax() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+// Named barrier over the four row warps of TMEM lane quarter q (ids 2..5).
+__device__ __forceinline__ void quarter_sync(int q) {
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + q) : "memory");
+}
+
+// The four partials of this thread's row (one per warp of its lane quarter):
+// each thread stores its own into TMEM column col + sub of its lane, the
+// quarter's warps meet, and each reads the four back. Every row thread calls it
+// (the barrier needs all 128 of the quarter).
+__device__ __forceinline__ void quarter_exchange(uint32_t trow, uint32_t col, int sub, int quarter,
+                                                 float mine, uint32_t (&all)[4]) {
+  ptx::tmem_st_32x32b_x1(trow + col + static_cast<uint32_t>(sub), __float_as_uint(mine));
+  ptx::tmem_st_wait();
+  ptx::tc_fence_before();
+  quarter_sync(quarter);
+  ptx::tc_fence_after();
+  ptx::tmem_ld_32x32b_x4(trow + col, all);
+  ptx::tmem_ld_wait();
+}
+
+__device__ __forceinline__ float quarter_exchange_max(uint32_t trow, uint32_t col, int sub,
+                                                      int quarter, float mine) {
+  uint32_t a[4];
+  quarter_exchange(trow, col, sub, quarter, mine, a);
+  return fmaxf(fmaxf(__uint_as_float(a[0]), __uint_as_float(a[1])),
+               fmaxf(__uint_as_float(a[2]), __uint_as_float(a[3])));
+}
+
+// The row's sum, added in the same order by all four threads of the row.
+__device__ __forceinline__ float quarter_exchange_sum(uint32_t trow, uint32_t col, int sub,
+                                                      int quarter, float mine) {
+  uint32_t a[4];
+  quarter_exchange(trow, col, sub, quarter, mine, a);
+  return (__uint_as_float(a[0]) + __uint_as_float(a[1])) +
+         (__uint_as_float(a[2]) + __uint_as_float(a[3]));
+}
 
 // S or dP = A B^T over head_dim: A, B both [128 x 128] K-major tiles.
 __device__ __forceinline__ void mma_tile_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
@@ -159,9 +196,10 @@ __device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, lo
 }
 
 // ------------------------------------------------------------------ forward
-constexpr int kFwdThreads = 320;  // producer, MMA issuer, 8 row warps
+constexpr int kFwdThreads = 576;  // producer, MMA issuer, 16 row warps
 constexpr int kFwdBars = 18;
-constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 2 * kTile * 4 + 1024;
+constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 1024;
+constexpr uint32_t kXchCol = 384;  // TMEM columns [384, 396): row-partial exchange
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
@@ -187,7 +225,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kFwdBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* xch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row-half exchange
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -206,8 +243,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     ptx::prefetch_tmap(&mo);
     for (int i = 0; i < kFwdBars; ++i) ptx::mbar_init(&bars[i], 1);
     for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(&s_free[s], 256);  // every row thread arrives
-      ptx::mbar_init(&p_full[s], 256);
+      ptx::mbar_init(&s_free[s], 512);  // every row thread arrives
+      ptx::mbar_init(&p_full[s], 512);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -298,73 +335,66 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax rows (warps 2..9): two threads per query row ----------------
-    // Warps w and w + 4 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..); warps
-    // 2..5 take score / O columns [0, 64) of their rows, warps 6..9 [64, 128).
-    // The halves of a row exchange their partial maxima (and, at the end, their
-    // sums) through shared memory. A thread whose wait fails keeps passing the
-    // named barriers with its work skipped, so no row warp is left waiting.
+    // ---------------- softmax rows (warps 2..17): four threads per query row ----------------
+    // Warps w, w + 4, w + 8, w + 12 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..)
+    // and take score / O columns [32 sub, 32 sub + 32), sub = (w - 2) / 4. The four
+    // partial row maxima (and, at the end, the four partial sums) meet in spare TMEM
+    // columns: each thread stores its partial into its lane's column
+    // kXchCol + 4 (j % 2) + sub, the quarter's four warps pass their own named
+    // barrier, and one load returns all four. A thread whose wait fails keeps
+    // passing the barriers with its work skipped, so no row warp is left waiting.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int sub = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
-    const int c0 = half * 64;
+    const int c0 = sub * 32;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint64_t c2 = f2_splat(p.scale_log2);
-    float m_run = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    float m_run = -INFINITY, l = 0.f;  // l: this thread's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
-      uint32_t v[2][32];
+      uint32_t v[32];
       float pmax = -INFINITY;
       if (ok && wait_bar_warp(&s_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
         ptx::tc_fence_after();
-        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0, v[0]);
-        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0 + 32, v[1]);
+        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0, v);
         ptx::tmem_ld_wait();
         ptx::tc_fence_before();
         ptx::mbar_arrive(&s_free[s]);
         if (j == qt) {  // diagonal tile: keys after the query are masked
 #pragma unroll
-          for (int k = 0; k < 2; ++k)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c0 + k * 32 + i > row) v[k][i] = 0xff800000u;  // -inf
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i > row) v[i] = 0xff800000u;  // -inf
         }
         float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          m0 = fmaxf(m0, __uint_as_float(v[0][i]));
-          m1 = fmaxf(m1, __uint_as_float(v[1][i]));
+        for (int i = 0; i < 16; ++i) {
+          m0 = fmaxf(m0, __uint_as_float(v[2 * i]));
+          m1 = fmaxf(m1, __uint_as_float(v[2 * i + 1]));
         }
         pmax = fmaxf(m0, m1);
       } else {
         ok = false;
       }
-      xch[half * kTile + row] = pmax;
-      sync_softmax();
-      const float smax = fmaxf(pmax, xch[(half ^ 1) * kTile + row]);
-      sync_softmax();  // the partner has read it before the next tile writes
+      const float smax = quarter_exchange_max(trow, kXchCol + 4 * s, sub, quarter, pmax);
       if (!ok) continue;
       const float tmax = smax * p.scale_log2;  // scale > 0: max commutes with it
       const bool need = tmax > m_run + kRescaleLog2;
       const float m_new = need ? tmax : m_run;
       const float alpha = need ? ex2(m_run - m_new) : 1.f;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O *= alpha on this thread's half row, once P_{j-1} V_{j-1} has landed
+        // O *= alpha on this thread's 32 columns, once P_{j-1} V_{j-1} has landed
         if (!wait_bar_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.budget, abort_flag)) {
           ok = false;
           continue;
         }
         ptx::tc_fence_after();
+        uint32_t o[32];
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c0, o);
+        ptx::tmem_ld_wait();
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          uint32_t o[32];
-          ptx::tmem_ld_32x32b_x32(trow + 256 + c0 + k * 32, o);
-          ptx::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          ptx::tmem_st_32x32b_x32(trow + 256 + c0 + k * 32, o);
-        }
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        ptx::tmem_st_32x32b_x32(trow + 256 + c0, o);
         ptx::tmem_st_wait();
       }
       l *= alpha;
@@ -372,19 +402,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // P = 2^(s c - m): the scaling and the sum two columns per instruction
       const uint64_t negm2 = f2_splat(-m_run);
       uint64_t acc = f2_splat(0.f);
-      uint32_t pk[32];
+      uint32_t pk[16];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float ta, tb;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(v[k][2 * i]), __uint_as_float(v[k][2 * i + 1])),
-                           c2, negm2),
-                    ta, tb);
-          const float ea = ex2(ta), eb = ex2(tb);
-          acc = f2_add(acc, f2_pack(ea, eb));
-          pk[k * 16 + i] = pack_bf16x2(ea, eb);
-        }
+      for (int i = 0; i < 16; ++i) {
+        float ta, tb;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2,
+                         negm2),
+                  ta, tb);
+        const float ea = ex2(ta), eb = ex2(tb);
+        acc = f2_add(acc, f2_pack(ea, eb));
+        pk[i] = pack_bf16x2(ea, eb);
       }
       float s_lo, s_hi;
       f2_unpack(acc, s_lo, s_hi);
@@ -396,7 +423,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const uint32_t pbase = ptx::smem_u32(sp + s * kTileBytes);
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
+      for (int cc = 0; cc < 4; ++cc)
         st_shared_v4(pbase + swz_chunk(row, c0 + cc * 8), pk[cc * 4], pk[cc * 4 + 1],
                      pk[cc * 4 + 2], pk[cc * 4 + 3]);
       ptx::fence_proxy_async_smem();
@@ -407,32 +434,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (ok && !wait_bar_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.budget,
                              abort_flag))
       ok = false;
-    xch[half * kTile + row] = l;
-    sync_softmax();
-    const float l_row = l + xch[(half ^ 1) * kTile + row];
+    const float l_row = quarter_exchange_sum(trow, kXchCol + 8, sub, quarter, l);
     if (!ok) {
       record_err(p.err, kDevErrAttnTimeout, abort_flag);
     } else {
       ptx::tc_fence_after();
       const float inv_l = 1.f / l_row;
       const uint32_t obase = ptx::smem_u32(sq);
+      uint32_t o[32];
+      ptx::tmem_ld_32x32b_x32(trow + 256 + c0, o);
+      ptx::tmem_ld_wait();
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        uint32_t o[32];
-        ptx::tmem_ld_32x32b_x32(trow + 256 + c0 + k * 32, o);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t* e = &o[i * 8];
-          st_shared_v4(obase + swz_chunk(row, c0 + k * 32 + i * 8),
-                       pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
-                       pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
-                       pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
-                       pack_bf16x2(__uint_as_float(e[6]) * inv_l, __uint_as_float(e[7]) * inv_l));
-        }
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t* e = &o[i * 8];
+        st_shared_v4(obase + swz_chunk(row, c0 + i * 8),
+                     pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
+                     pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
+                     pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
+                     pack_bf16x2(__uint_as_float(e[6]) * inv_l, __uint_as_float(e[7]) * inv_l));
       }
       const int q = q0 + row;
-      if (half == 0 && q < p.S)
+      if (sub == 0 && q < p.S)
         p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l_row);
     }
     ptx::fence_proxy_async_smem();
