@@ -292,14 +292,18 @@ LEMA_API int lema_attn_fwd(const void* q, int64_t ldq, const void* k, int64_t ld
 
 /* Gradients of lema_attn_fwd: dq [B*S, H*128], dk / dv [B*S, Hkv*128] (bf16,
  * written whole; dk / dv of a kv head sum over its query heads) from q, k, v,
- * the forward's o and lse, and dout. delta [B, H, S] fp32 is caller-provided
- * scratch (receives rowsum(dout * o)). Three kernels on `stream`. */
+ * the forward's o and lse, and dout. Caller-provided scratch: delta [B, H, S]
+ * fp32 (receives rowsum(dout * o)) and, optionally, dkv_ws of 2*B*S*H*128 fp32
+ * (16-byte aligned): with GQA and fewer (b, kv head, key tile) units than SMs,
+ * each query head's dK / dV share goes there and a fourth kernel sums
+ * them in head order; NULL keeps one CTA per kv head. Three or four kernels on
+ * `stream`. */
 LEMA_API int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
                            const void* v, int64_t ldv, const void* o, int64_t ldo,
                            const void* dout, int64_t lddo, const float* lse, float* delta,
-                           void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
-                           int64_t lddv, int64_t B, int64_t S, int64_t H, int64_t Hkv,
-                           int64_t head_dim, float scale, void* stream);
+                           float* dkv_ws, void* dq, int64_t lddq, void* dk, int64_t lddk,
+                           void* dv, int64_t lddv, int64_t B, int64_t S, int64_t H,
+                           int64_t Hkv, int64_t head_dim, float scale, void* stream);
 
 /* Wait budget (clock cycles) of the attention kernels' bounded waits; 0
  * restores the default. A wait that runs out records device error 0x105. */

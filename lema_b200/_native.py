@@ -63,8 +63,8 @@ _SIGNATURES: dict[str, list] = {
     "lema_swiglu_bwd": [vp, i64, vp, i64, i64, i64, vp, i64, vp],
     "lema_attn_fwd": [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, i64,
                       C.c_float, vp],
-    "lema_attn_bwd": [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64,
-                      vp, i64, i64, i64, i64, i64, i64, C.c_float, vp],
+    "lema_attn_bwd": [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, vp, i64, vp,
+                      i64, vp, i64, i64, i64, i64, i64, i64, C.c_float, vp],
     "lema_attn_set_wait_budget": [i64],
     "lema_ckpt_save": [vp, vp, sz, i32, vp, vp, vp],
     "lema_ckpt_restore": [vp, vp, sz, vp, vp, vp],

@@ -24,11 +24,15 @@
 // through a TMA store and record the row's log-sum-exp.
 //
 // Backward (two kernels, no atomics, deterministic):
-//   attn_bwd_dkdv_kernel: one CTA per (b, kv head, 128-key tile); for every
-//     query head of the group and every causal query tile it forms S^T = K Q^T
-//     and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse), dS^T = P^T (dP^T -
-//     delta), and accumulates dV += P^T dO and dK += dS^T Q (Q, dO read MN-major
-//     from the tiles the first two MMAs used K-major).
+//   attn_bwd_dkdv_kernel: one CTA per (b, kv head, 128-key tile), heaviest
+//     first; for every query head of the group and every causal query tile it
+//     forms S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse),
+//     dS^T = P^T (dP^T - delta), and accumulates dV += P^T dO and dK += dS^T Q
+//     (Q, dO read MN-major from the tiles the first two MMAs used K-major). When
+//     those CTAs would not fill the GPU (GQA, few sequences or heads), one CTA per
+//     query head instead writes its head's fp32 dK / dV share and
+//     attn_dkv_reduce_kernel sums a group's shares in head order into the bf16
+//     dK / dV of its kv head.
 //   attn_bwd_dq_kernel: one CTA per (b, h, 128-query tile); for every causal key
 //     tile it forms S = Q K^T and dP = dO V^T, dS = P (dP - delta), and
 //     accumulates dQ += dS K (K read MN-major).
@@ -68,6 +72,9 @@ struct AttnParams {
   float scale_log2;  // scale * log2(e)
   float* lse;        // [B, H, S]
   const float* delta;  // [B, H, S] (backward)
+  float* dkv_ws;       // split GQA backward: fp32 dK / dV shares per query head, or null
+  int64_t ws_half;     // floats in each half of dkv_ws (B * S * H * 128)
+  int heads_per_cta;   // dK/dV kernel: the whole group (bf16 out) or 1 (shares into dkv_ws)
   int32_t* err;
   long long budget;
 };
@@ -537,7 +544,7 @@ constexpr int kBwdThreads = 192;
 constexpr int kDkdvBars = 6;
 constexpr int kDkdvSmem = 6 * kTileBytes + 1024 + kDkdvBars * 8 + 16 + 1024;
 
-// dK, dV of one (b, kv head, 128-key tile).
+// dK, dV of one (b, kv head, 128-key tile), or one query head's share of them.
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap mk,
@@ -569,13 +576,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int bkv = p.B * p.Hkv;
-  const int kt = static_cast<int>(blockIdx.x) / bkv;  // key tile 0 (the heaviest) first
-  const int b = (static_cast<int>(blockIdx.x) % bkv) / p.Hkv;
-  const int kvh = static_cast<int>(blockIdx.x) % p.Hkv;
-  const int rep = p.H / p.Hkv;
+  const int groups = p.H / p.heads_per_cta;  // head groups per sequence
+  const int bg_count = p.B * groups;
+  const int kt = static_cast<int>(blockIdx.x) / bg_count;  // key tile 0 (the heaviest) first
+  const int b = (static_cast<int>(blockIdx.x) % bg_count) / groups;
+  const int h0 = (static_cast<int>(blockIdx.x) % groups) * p.heads_per_cta;
+  const int kvh = h0 / (p.H / p.Hkv);
   const int per_head = p.q_tiles - kt;  // causal query tiles kt .. q_tiles - 1
-  const int n_items = rep * per_head;
+  const int n_items = p.heads_per_cta * per_head;
 
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&mq);
@@ -609,7 +617,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ptx::tma_load_3d(sv, &mv, kv_full, kvh * kHd, kt * kTile, b);
       ptx::tma_load_3d(sv + kBox, &mv, kv_full, kvh * kHd + 64, kt * kTile, b);
       for (int it = 0; it < n_items; ++it) {
-        const int h = kvh * rep + it / per_head;
+        const int h = h0 + it / per_head;
         const int q0 = (kt + it % per_head) * kTile;
         if (it > 0 && !wait_bar(qd_empty, (it - 1) & 1, p.budget, abort_flag)) {
           ok = false;
@@ -665,7 +673,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t pt_base = ptx::smem_u32(spt), dst_base = ptx::smem_u32(sdst);
     bool ok = true;
     for (int it = 0; it < n_items; ++it) {
-      const int h = kvh * rep + it / per_head;
+      const int h = h0 + it / per_head;
       const int qi = kt + it % per_head;
       sync_rows();  // every row is done with the previous item's (lse, delta)
       stage_rows(p, b, h, qi * kTile, tid, lse_s, delta_s);
@@ -698,10 +706,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(pd_full);
     }
-    // ---------------- epilogue: dV, scale * dK -> bf16 -> TMA store ----------------
+    // ---------------- epilogue: dV, scale * dK -> bf16 -> TMA store, or (GQA) this
+    // head's fp32 share into the workspace ----------------
     if (ok && !wait_bar_warp(qd_empty, (n_items - 1) & 1, p.budget, abort_flag)) ok = false;
     if (!ok) {
       record_err(p.err, kDevErrAttnTimeout, abort_flag);
+    } else if (p.dkv_ws != nullptr) {
+      ptx::tc_fence_after();
+      const int key = kt * kTile + row;
+      float* wk = p.dkv_ws + (static_cast<int64_t>(b) * p.S + key) * (p.H * kHd) + h0 * kHd;
+      float* wv = wk + p.ws_half;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t a[32], g[32];
+        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
+        ptx::tmem_ld_32x32b_x32(trow + 384 + c4 * 32, g);
+        ptx::tmem_ld_wait();
+        if (key < p.S) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            reinterpret_cast<float4*>(wv + c4 * 32)[i] =
+                make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                            __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3]));
+            reinterpret_cast<float4*>(wk + c4 * 32)[i] = make_float4(
+                __uint_as_float(g[4 * i]) * p.scale, __uint_as_float(g[4 * i + 1]) * p.scale,
+                __uint_as_float(g[4 * i + 2]) * p.scale, __uint_as_float(g[4 * i + 3]) * p.scale);
+          }
+        }
+      }
     } else {
       ptx::tc_fence_after();
 #pragma unroll 1
@@ -722,7 +754,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     ptx::fence_proxy_async_smem();
     sync_rows();
-    if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
+    if (threadIdx.x == 64 && p.dkv_ws == nullptr && !is_aborted(abort_flag)) {
       ptx::tma_store_3d(&mdv, spt, kvh * kHd, kt * kTile, b);
       ptx::tma_store_3d(&mdv, spt + kBox, kvh * kHd + 64, kt * kTile, b);
       ptx::tma_store_3d(&mdk, sdst, kvh * kHd, kt * kTile, b);
@@ -737,6 +769,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// dk / dv [b, s, kvh, :] (bf16) = the sum over the group's query heads, in head
+// order, of their fp32 shares in the workspace ([2][B * S][H * 128]: dK, dV).
+// One thread per 4 columns of one (token, kv head, dK or dV).
+__global__ void __launch_bounds__(256) attn_dkv_reduce_kernel(
+    const float* __restrict__ ws, int64_t ws_half, int64_t tokens, int H, int Hkv,
+    __nv_bfloat16* __restrict__ dk, int64_t lddk, __nv_bfloat16* __restrict__ dv, int64_t lddv) {
+  const int rep = H / Hkv;
+  const int64_t units = tokens * Hkv * 2 * (kHd / 4);
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(u % (kHd / 4)) * 4;
+    const int which = static_cast<int>((u / (kHd / 4)) % 2);
+    const int64_t rest = u / (kHd / 4) / 2;
+    const int kvh = static_cast<int>(rest % Hkv);
+    const int64_t tok = rest / Hkv;
+    const float* src = ws + which * ws_half + tok * (static_cast<int64_t>(H) * kHd) +
+                       static_cast<int64_t>(kvh) * rep * kHd + c;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (int r = 1; r < rep; ++r) {
+      const float4 x = *reinterpret_cast<const float4*>(src + r * kHd);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    __nv_bfloat16* dst = (which == 0 ? dk + tok * lddk : dv + tok * lddv) + kvh * kHd + c;
+    const uint2 pk = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+    *reinterpret_cast<uint2*>(dst) = pk;
   }
 }
 
@@ -1070,9 +1133,9 @@ extern "C" int lema_attn_set_wait_budget(int64_t cycles) {
 extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk,
                              const void* v, int64_t ldv, const void* o, int64_t ldo,
                              const void* dout, int64_t lddo, const float* lse, float* delta,
-                             void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
-                             int64_t lddv, int64_t B, int64_t S, int64_t H, int64_t Hkv,
-                             int64_t head_dim, float scale, void* stream) {
+                             float* dkv_ws, void* dq, int64_t lddq, void* dk, int64_t lddk,
+                             void* dv, int64_t lddv, int64_t B, int64_t S, int64_t H,
+                             int64_t Hkv, int64_t head_dim, float scale, void* stream) {
   clear_error();
   int rc = check_attn(B, S, H, Hkv, head_dim);
   if (rc) return rc;
@@ -1090,6 +1153,17 @@ extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t 
   if (p.err == nullptr) return set_error(LEMA_ERR_CUDA, "cannot resolve device error word");
   p.lse = const_cast<float*>(lse);
   p.delta = delta;
+  // dK/dV CTAs per kv head (the group's heads in one CTA, bf16 out) unless they
+  // would leave SMs idle and a workspace for per-query-head shares was given
+  p.heads_per_cta = static_cast<int>(H / Hkv);
+  if (H != Hkv && dkv_ws != nullptr &&
+      B * Hkv * p.q_tiles < static_cast<int64_t>(device_sm_count())) {
+    if (!aligned16(dkv_ws))
+      return set_error(LEMA_ERR_INVALID_ARGUMENT, "dkv_ws must be 16-byte aligned");
+    p.dkv_ws = dkv_ws;
+    p.ws_half = B * S * H * kHd;
+    p.heads_per_cta = 1;
+  }
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   if ((rc = make_seq_map(&mq, q, B, S, H * kHd, ldq)) ||
       (rc = make_seq_map(&mk, k, B, S, Hkv * kHd, ldk)) ||
@@ -1103,7 +1177,7 @@ extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t 
   if ((rc = set_smem(attn_bwd_dkdv_kernel, kDkdvSmem, done_kv)) ||
       (rc = set_smem(attn_bwd_dq_kernel, kDqSmem, done_q)))
     return rc;
-  const int64_t q_ctas = B * H * p.q_tiles, kv_ctas = B * Hkv * p.q_tiles;
+  const int64_t q_ctas = B * H * p.q_tiles, kv_ctas = B * (H / p.heads_per_cta) * p.q_tiles;
   if (q_ctas > 0x7fffffff) return set_error(LEMA_ERR_INVALID_ARGUMENT, "too many tiles");
   auto s = static_cast<cudaStream_t>(stream);
   const int64_t warps = B * S * H;
@@ -1116,6 +1190,15 @@ extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t 
   attn_bwd_dkdv_kernel<<<static_cast<unsigned>(kv_ctas), kBwdThreads, kDkdvSmem, s>>>(
       mq, mk, mv, mdo, mdk, mdv, p);
   LEMA_CUDA_TRY(cudaGetLastError());
+  if (p.dkv_ws != nullptr) {
+    const int64_t units = B * S * Hkv * 2 * (kHd / 4);
+    const int blocks = static_cast<int>(
+        std::min<int64_t>((units + 255) / 256, static_cast<int64_t>(device_sm_count()) * 8));
+    attn_dkv_reduce_kernel<<<blocks, 256, 0, s>>>(
+        p.dkv_ws, p.ws_half, B * S, static_cast<int>(H), static_cast<int>(Hkv),
+        static_cast<__nv_bfloat16*>(dk), lddk, static_cast<__nv_bfloat16*>(dv), lddv);
+    LEMA_CUDA_TRY(cudaGetLastError());
+  }
   attn_bwd_dq_kernel<<<static_cast<unsigned>(q_ctas), kBwdThreads, kDqSmem, s>>>(mq, mk, mv, mdo,
                                                                                 mdq, p);
   LEMA_CUDA_TRY(cudaGetLastError());

@@ -785,8 +785,10 @@ def attention_fwd(q2d: torch.Tensor, k2d: torch.Tensor, v2d: torch.Tensor, B: in
 
 
 def attention_bwd(q2d, k2d, v2d, o2d, lse, dout2d, B: int, S: int, H: int, Hkv: int,
-                  scale: float):
-    """(dq [B*S, H*128], dk, dv [B*S, Hkv*128]) of attention_fwd."""
+                  scale: float, split_heads: bool = True):
+    """(dq [B*S, H*128], dk, dv [B*S, Hkv*128]) of attention_fwd. With GQA the
+    library may split dK / dV per query head through a workspace (when the kv
+    heads alone would leave SMs idle); ``split_heads=False`` withholds it."""
     dev = _require_cuda(q2d, k2d, v2d, o2d, lse, dout2d)
     q2d, k2d, v2d, o2d = (_rows_view(t) for t in (q2d, k2d, v2d, o2d))
     dout2d = _rows_view(dout2d.to(torch.bfloat16))
@@ -794,10 +796,15 @@ def attention_bwd(q2d, k2d, v2d, o2d, lse, dout2d, B: int, S: int, H: int, Hkv: 
     dk = torch.empty(B * S, Hkv * 128, dtype=torch.bfloat16, device=dev)
     dv = torch.empty(B * S, Hkv * 128, dtype=torch.bfloat16, device=dev)
     delta = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+    ws = (torch.empty(2 * B * S * H * 128, dtype=torch.float32, device=dev)
+          if H != Hkv and split_heads else None)
     N.call("lema_attn_bwd", _ptr(q2d), _ld(q2d), _ptr(k2d), _ld(k2d), _ptr(v2d), _ld(v2d),
            _ptr(o2d), _ld(o2d), _ptr(dout2d), _ld(dout2d), _ptr(lse.contiguous()), _ptr(delta),
-           _ptr(dq), H * 128, _ptr(dk), Hkv * 128, _ptr(dv), Hkv * 128, B, S, H, Hkv, 128,
-           float(scale), _stream(dev))
+           _ptr(ws), _ptr(dq), H * 128, _ptr(dk), Hkv * 128, _ptr(dv), Hkv * 128, B, S, H, Hkv,
+           128, float(scale), _stream(dev))
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    if ws is not None and B * Hkv * -(-S // 128) < n_sm:
+        N.kernel_launches += 1  # the library split dK/dV per query head: the reduce kernel
     return dq, dk, dv
 
 

@@ -125,3 +125,28 @@ def test_trainer_step_with_tcgen05_attention_matches_sdpa(cuda_device, moe):
     for a, b in zip(g_tc, g_ref):
         rel = ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
         assert rel <= 3e-2, rel
+
+
+@pytest.mark.parametrize("B,S,H,Hkv", [(2, 256, 4, 2), (1, 200, 8, 2)])
+def test_backward_gqa_without_head_split(cuda_device, B, S, H, Hkv):
+    """The GQA backward with one CTA per kv head (no workspace: the group's
+    query heads accumulate in TMEM) against the split one and the fp32 autograd
+    reference, at the same bar."""
+    q, k, v = _inputs(B, S, H, Hkv, 5 * S + H, cuda_device)
+    g = torch.Generator(device="cpu").manual_seed(S + 1)
+    do = torch.randn(B * S, H * D, generator=g).to(torch.bfloat16).to(cuda_device)
+    o, lse = ops.attention_fwd(q, k, v, B, S, H, Hkv, D ** -0.5)
+    grouped = ops.attention_bwd(q, k, v, o, lse, do, B, S, H, Hkv, D ** -0.5, split_heads=False)
+    split = ops.attention_bwd(q, k, v, o, lse, do, B, S, H, Hkv, D ** -0.5)
+    torch.cuda.synchronize()
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    o_ref, _ = _ref_fp32(qf, kf, vf, B, S, H, Hkv)
+    o_ref.transpose(1, 2).reshape(B * S, H * D).backward(do.float())
+    for name, a, b_, ref in zip(("dq", "dk", "dv"), grouped, split, (qf.grad, kf.grad, vf.grad)):
+        floor = 2 ** -8 * ref.abs().max().item()
+        scale = ref.abs().max().item()
+        for got in (a, b_):
+            assert torch.isfinite(got).all(), name
+            assert (got.float() - ref).abs().max().item() <= 2e-2 * scale + floor, name
+        # the two orders of summing the group's heads agree to bf16 rounding
+        assert (a.float() - b_.float()).abs().max().item() <= 2 ** -7 * scale, name
