@@ -541,10 +541,16 @@ __device__ __forceinline__ void store_row32(uint32_t tile, int r, int col, const
 }
 
 constexpr int kBwdThreads = 192;
-constexpr int kDkdvBars = 6;
-constexpr int kDkdvSmem = 6 * kTileBytes + 1024 + kDkdvBars * 8 + 16 + 1024;
+constexpr int kDkdvBars = 11;
+constexpr int kDkdvSmem = 7 * kTileBytes + 1024 + kDkdvBars * 8 + 16 + 1024;
 
 // dK, dV of one (b, kv head, 128-key tile), or one query head's share of them.
+// The Q / dO tiles of the items are double-buffered, so the next item's loads
+// overlap this one; P^T and dS^T share one tile: P^T is written, dV += P^T dO
+// reads it, then dS^T (kept in registers meanwhile) replaces it for
+// dK += dS^T Q. MMA issue order per item i: dV(i - 1), S^T(i) and dP^T(i),
+// dK(i - 1). A row thread whose wait fails keeps passing the named barriers
+// with its work skipped.
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap mk,
@@ -558,19 +564,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sk = smem;
   uint8_t* sv = smem + kTileBytes;
-  uint8_t* sq = smem + 2 * kTileBytes;
-  uint8_t* sdo = smem + 3 * kTileBytes;
-  uint8_t* spt = smem + 4 * kTileBytes;   // P^T (bf16); dV staging at the end
-  uint8_t* sdst = smem + 5 * kTileBytes;  // dS^T (bf16); dK staging at the end
-  float* lse_s = reinterpret_cast<float*>(smem + 6 * kTileBytes);
+  uint8_t* sq = smem + 2 * kTileBytes;   // 2 slots (item % 2); dV, dK staging at the end
+  uint8_t* sdo = smem + 4 * kTileBytes;  // 2 slots
+  uint8_t* spd = smem + 6 * kTileBytes;  // P^T, then dS^T (bf16)
+  float* lse_s = reinterpret_cast<float*>(smem + 7 * kTileBytes);
   float* delta_s = lse_s + kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes + 1024);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes + 1024);
   uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 2;  // the item's four MMAs are complete
-  uint64_t* st_full = bars + 3;   // S^T and dP^T are in TMEM
-  uint64_t* pd_full = bars + 4;   // P^T and dS^T are in shared memory (128 arrivals)
-  uint64_t* drain = bars + 5;
+  uint64_t* qd_full = bars + 1;   // 2 slots
+  uint64_t* qd_empty = bars + 3;  // 2 slots: the item's dV and dK MMAs are complete
+  uint64_t* st_full = bars + 5;   // S^T and dP^T are in TMEM
+  uint64_t* st_free = bars + 6;   // the rows have read them (128 arrivals)
+  uint64_t* p_ready = bars + 7;   // P^T is in shared memory (128 arrivals)
+  uint64_t* dv_done = bars + 8;   // dV += P^T dO is complete: the tile is free
+  uint64_t* ds_ready = bars + 9;  // dS^T is in shared memory (128 arrivals)
+  uint64_t* drain = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDkdvBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -591,7 +599,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     ptx::prefetch_tmap(&mv);
     ptx::prefetch_tmap(&mdo);
     for (int i = 0; i < kDkdvBars; ++i) ptx::mbar_init(&bars[i], 1);
-    ptx::mbar_init(pd_full, 128);
+    ptx::mbar_init(st_free, 128);
+    ptx::mbar_init(p_ready, 128);
+    ptx::mbar_init(ds_ready, 128);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
@@ -617,46 +627,70 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ptx::tma_load_3d(sv, &mv, kv_full, kvh * kHd, kt * kTile, b);
       ptx::tma_load_3d(sv + kBox, &mv, kv_full, kvh * kHd + 64, kt * kTile, b);
       for (int it = 0; it < n_items; ++it) {
+        const int slot = it & 1;
         const int h = h0 + it / per_head;
         const int q0 = (kt + it % per_head) * kTile;
-        if (it > 0 && !wait_bar(qd_empty, (it - 1) & 1, p.budget, abort_flag)) {
+        if (it >= 2 && !wait_bar(&qd_empty[slot], ((it - 2) >> 1) & 1, p.budget, abort_flag)) {
           ok = false;
           break;
         }
-        ptx::mbar_arrive_expect_tx(qd_full, 2 * kTileBytes);
-        ptx::tma_load_3d(sq, &mq, qd_full, h * kHd, q0, b);
-        ptx::tma_load_3d(sq + kBox, &mq, qd_full, h * kHd + 64, q0, b);
-        ptx::tma_load_3d(sdo, &mdo, qd_full, h * kHd, q0, b);
-        ptx::tma_load_3d(sdo + kBox, &mdo, qd_full, h * kHd + 64, q0, b);
+        uint8_t* q_dst = sq + slot * kTileBytes;
+        uint8_t* do_dst = sdo + slot * kTileBytes;
+        ptx::mbar_arrive_expect_tx(&qd_full[slot], 2 * kTileBytes);
+        ptx::tma_load_3d(q_dst, &mq, &qd_full[slot], h * kHd, q0, b);
+        ptx::tma_load_3d(q_dst + kBox, &mq, &qd_full[slot], h * kHd + 64, q0, b);
+        ptx::tma_load_3d(do_dst, &mdo, &qd_full[slot], h * kHd, q0, b);
+        ptx::tma_load_3d(do_dst + kBox, &mdo, &qd_full[slot], h * kHd + 64, q0, b);
         ++issued;
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      // every issued load lands before this CTA's shared memory is released
       (void)ptx::mbar_wait(kv_full, 0, p.budget);
-      if (issued > 0) (void)ptx::mbar_wait(qd_full, (issued - 1) & 1, p.budget);
+      for (int i = issued - 1; i >= 0 && i >= issued - 2; --i)
+        (void)ptx::mbar_wait(&qd_full[i & 1], (i >> 1) & 1, p.budget);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       bool ok = wait_bar(kv_full, 0, p.budget, abort_flag);
       bool issued = false;
-      for (int it = 0; ok && it < n_items; ++it) {
-        if (!wait_bar(qd_full, it & 1, p.budget, abort_flag)) {
-          ok = false;
-          break;
+      for (int it = 0; ok && it <= n_items; ++it) {
+        if (it >= 1) {  // dV += P^T dO of item it - 1
+          const int j = it - 1;
+          if (!wait_bar(p_ready, j & 1, p.budget, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kmn(tmem + 256, ptx::smem_u32(spd), ptx::smem_u32(sdo + (j & 1) * kTileBytes),
+                       j > 0);
+          ptx::mma_commit(dv_done);
         }
-        ptx::tc_fence_after();
-        mma_tile_kk(tmem, ptx::smem_u32(sk), ptx::smem_u32(sq), false);         // S^T = K Q^T
-        mma_tile_kk(tmem + 128, ptx::smem_u32(sv), ptx::smem_u32(sdo), false);  // dP^T = V dO^T
-        issued = true;
-        ptx::mma_commit(st_full);
-        if (!wait_bar(pd_full, it & 1, p.budget, abort_flag)) {
-          ok = false;
-          break;
+        if (it < n_items) {  // S^T = K Q^T, dP^T = V dO^T of item it
+          const int slot = it & 1;
+          if (!wait_bar(&qd_full[slot], (it >> 1) & 1, p.budget, abort_flag) ||
+              (it >= 1 && !wait_bar(st_free, (it - 1) & 1, p.budget, abort_flag))) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kk(tmem, ptx::smem_u32(sk), ptx::smem_u32(sq + slot * kTileBytes), false);
+          mma_tile_kk(tmem + 128, ptx::smem_u32(sv), ptx::smem_u32(sdo + slot * kTileBytes),
+                      false);
+          issued = true;
+          ptx::mma_commit(st_full);
         }
-        ptx::tc_fence_after();
-        mma_tile_kmn(tmem + 256, ptx::smem_u32(spt), ptx::smem_u32(sdo), it > 0);   // dV += P^T dO
-        mma_tile_kmn(tmem + 384, ptx::smem_u32(sdst), ptx::smem_u32(sq), it > 0);   // dK += dS^T Q
-        ptx::mma_commit(qd_empty);
+        if (it >= 1) {  // dK += dS^T Q of item it - 1
+          const int j = it - 1;
+          if (!wait_bar(ds_ready, j & 1, p.budget, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          mma_tile_kmn(tmem + 384, ptx::smem_u32(spd), ptx::smem_u32(sq + (j & 1) * kTileBytes),
+                       j > 0);
+          ptx::mma_commit(&qd_empty[j & 1]);
+        }
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
       if (issued) {
@@ -670,7 +704,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = quarter * 32 + lane;
     const int tid = threadIdx.x - 64;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t pt_base = ptx::smem_u32(spt), dst_base = ptx::smem_u32(sdst);
+    const uint32_t pd_base = ptx::smem_u32(spd);
     bool ok = true;
     for (int it = 0; it < n_items; ++it) {
       const int h = h0 + it / per_head;
@@ -678,37 +712,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       sync_rows();  // every row is done with the previous item's (lse, delta)
       stage_rows(p, b, h, qi * kTile, tid, lse_s, delta_s);
       sync_rows();
-      if (!wait_bar_warp(st_full, it & 1, p.budget, abort_flag)) {
-        ok = false;
-        break;
+      if (!ok) continue;
+      if (!wait_bar_warp(st_full, it & 1, p.budget, abort_flag) ||
+          (it >= 1 &&
+           !wait_bar_warp(&qd_empty[(it - 1) & 1], ((it - 1) >> 1) & 1, p.budget, abort_flag))) {
+        ok = false;  // the shared P / dS tile is free once dK of item it - 1 is done
+        continue;
       }
       ptx::tc_fence_after();
       const bool diag = qi == kt;
-#pragma unroll 1
+      uint32_t dsk[64];  // this row's dS^T, bf16 pairs, until dV has read P^T
+#pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t sv32[32], dp32[32];
         ptx::tmem_ld_32x32b_x32(trow + c4 * 32, sv32);
         ptx::tmem_ld_32x32b_x32(trow + 128 + c4 * 32, dp32);
         ptx::tmem_ld_wait();
-        float pf[32], ds[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = c4 * 32 + i;  // query column
-          float pv = ex2(__uint_as_float(sv32[i]) * p.scale_log2 - lse_s[c]);
-          if (diag && c < row) pv = 0.f;  // key after query
-          pf[i] = pv;
-          ds[i] = pv * (__uint_as_float(dp32[i]) - delta_s[c]);
+        for (int i = 0; i < 16; ++i) {
+          float pr[2], dr[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = c4 * 32 + 2 * i + e;  // query column
+            float pv = ex2(__uint_as_float(sv32[2 * i + e]) * p.scale_log2 - lse_s[c]);
+            if (diag && c < row) pv = 0.f;  // key after query
+            pr[e] = pv;
+            dr[e] = pv * (__uint_as_float(dp32[2 * i + e]) - delta_s[c]);
+          }
+          pk[i] = pack_bf16x2(pr[0], pr[1]);
+          dsk[c4 * 16 + i] = pack_bf16x2(dr[0], dr[1]);
         }
-        store_row32(pt_base, row, c4 * 32, pf, 1.f);
-        store_row32(dst_base, row, c4 * 32, ds, 1.f);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          st_shared_v4(pd_base + swz_chunk(row, c4 * 32 + cc * 8), pk[cc * 4], pk[cc * 4 + 1],
+                       pk[cc * 4 + 2], pk[cc * 4 + 3]);
       }
-      ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(pd_full);
+      ptx::mbar_arrive(st_free);
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(p_ready);
+      if (!wait_bar_warp(dv_done, it & 1, p.budget, abort_flag)) {
+        ok = false;
+        continue;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc)
+        st_shared_v4(pd_base + swz_chunk(row, cc * 8), dsk[cc * 4], dsk[cc * 4 + 1],
+                     dsk[cc * 4 + 2], dsk[cc * 4 + 3]);
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(ds_ready);
     }
-    // ---------------- epilogue: dV, scale * dK -> bf16 -> TMA store, or (GQA) this
-    // head's fp32 share into the workspace ----------------
-    if (ok && !wait_bar_warp(qd_empty, (n_items - 1) & 1, p.budget, abort_flag)) ok = false;
+    // ---------------- epilogue: dV, scale * dK -> bf16 -> TMA store, or (split
+    // heads) this head's fp32 share into the workspace ----------------
+    if (ok && !wait_bar_warp(&qd_empty[(n_items - 1) & 1], ((n_items - 1) >> 1) & 1, p.budget,
+                             abort_flag))
+      ok = false;
+    const uint32_t dv_stage = ptx::smem_u32(sq), dk_stage = ptx::smem_u32(sq + kTileBytes);
     if (!ok) {
       record_err(p.err, kDevErrAttnTimeout, abort_flag);
     } else if (p.dkv_ws != nullptr) {
@@ -748,17 +808,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           af[i] = __uint_as_float(a[i]);
           gf[i] = __uint_as_float(g[i]);
         }
-        store_row32(pt_base, row, c4 * 32, af, 1.f);
-        store_row32(dst_base, row, c4 * 32, gf, p.scale);
+        store_row32(dv_stage, row, c4 * 32, af, 1.f);
+        store_row32(dk_stage, row, c4 * 32, gf, p.scale);
       }
     }
     ptx::fence_proxy_async_smem();
     sync_rows();
     if (threadIdx.x == 64 && p.dkv_ws == nullptr && !is_aborted(abort_flag)) {
-      ptx::tma_store_3d(&mdv, spt, kvh * kHd, kt * kTile, b);
-      ptx::tma_store_3d(&mdv, spt + kBox, kvh * kHd + 64, kt * kTile, b);
-      ptx::tma_store_3d(&mdk, sdst, kvh * kHd, kt * kTile, b);
-      ptx::tma_store_3d(&mdk, sdst + kBox, kvh * kHd + 64, kt * kTile, b);
+      ptx::tma_store_3d(&mdv, sq, kvh * kHd, kt * kTile, b);
+      ptx::tma_store_3d(&mdv, sq + kBox, kvh * kHd + 64, kt * kTile, b);
+      ptx::tma_store_3d(&mdk, sq + kTileBytes, kvh * kHd, kt * kTile, b);
+      ptx::tma_store_3d(&mdk, sq + kTileBytes + kBox, kvh * kHd + 64, kt * kTile, b);
       ptx::bulk_commit_group();
       ptx::bulk_wait_group_all();
     }
