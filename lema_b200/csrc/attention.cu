@@ -126,8 +126,11 @@ __device__ __forceinline__ float ex2(float x) {
   return r;
 }
 
-// Named barrier over the 128 threads of warps 2..5 (backward kernels).
-__device__ __forceinline__ void sync_rows() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier 1 over the N row threads of a kernel (warps 2 ..).
+template <int N>
+__device__ __forceinline__ void sync_softmax_n() {
+  asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
+}
 
 // Named barrier over the 512 row threads of the forward (warps 2..17).
 __device__ __forceinline__ void sync_softmax() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
@@ -540,18 +543,21 @@ __device__ __forceinline__ void store_row32(uint32_t tile, int r, int col, const
                  pack_bf16x2(x[i * 8 + 6] * mul, x[i * 8 + 7] * mul));
 }
 
-constexpr int kBwdThreads = 192;
+constexpr int kDqThreads = 576;  // producer, MMA issuer, 16 row warps
+constexpr int kDkdvThreads = 320;  // producer, MMA issuer, 8 row warps
 constexpr int kDkdvBars = 11;
 constexpr int kDkdvSmem = 7 * kTileBytes + 1024 + kDkdvBars * 8 + 16 + 1024;
 
 // dK, dV of one (b, kv head, 128-key tile), or one query head's share of them.
+// Eight row warps: warps w and w + 4 share TMEM lane quarter w % 4 and take
+// query columns [64 half, 64 half + 64) of their key rows.
 // The Q / dO tiles of the items are double-buffered, so the next item's loads
 // overlap this one; P^T and dS^T share one tile: P^T is written, dV += P^T dO
 // reads it, then dS^T (kept in registers meanwhile) replaces it for
 // dK += dS^T Q. MMA issue order per item i: dV(i - 1), S^T(i) and dP^T(i),
 // dK(i - 1). A row thread whose wait fails keeps passing the named barriers
 // with its work skipped.
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kDkdvThreads, 1)
     attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap mk,
                          const __grid_constant__ CUtensorMap mv,
@@ -574,10 +580,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* qd_full = bars + 1;   // 2 slots
   uint64_t* qd_empty = bars + 3;  // 2 slots: the item's dV and dK MMAs are complete
   uint64_t* st_full = bars + 5;   // S^T and dP^T are in TMEM
-  uint64_t* st_free = bars + 6;   // the rows have read them (128 arrivals)
-  uint64_t* p_ready = bars + 7;   // P^T is in shared memory (128 arrivals)
+  uint64_t* st_free = bars + 6;   // the rows have read them (256 arrivals)
+  uint64_t* p_ready = bars + 7;   // P^T is in shared memory (256 arrivals)
   uint64_t* dv_done = bars + 8;   // dV += P^T dO is complete: the tile is free
-  uint64_t* ds_ready = bars + 9;  // dS^T is in shared memory (128 arrivals)
+  uint64_t* ds_ready = bars + 9;  // dS^T is in shared memory (256 arrivals)
   uint64_t* drain = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDkdvBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
@@ -599,9 +605,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     ptx::prefetch_tmap(&mv);
     ptx::prefetch_tmap(&mdo);
     for (int i = 0; i < kDkdvBars; ++i) ptx::mbar_init(&bars[i], 1);
-    ptx::mbar_init(st_free, 128);
-    ptx::mbar_init(p_ready, 128);
-    ptx::mbar_init(ds_ready, 128);
+    ptx::mbar_init(st_free, 256);
+    ptx::mbar_init(p_ready, 256);
+    ptx::mbar_init(ds_ready, 256);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
@@ -699,8 +705,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
-    // ---------------- elementwise rows (warps 2..5): one key per thread ----------------
+    // ---------------- elementwise rows (warps 2..9): two threads per key row ----------------
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int tid = threadIdx.x - 64;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -709,9 +716,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int it = 0; it < n_items; ++it) {
       const int h = h0 + it / per_head;
       const int qi = kt + it % per_head;
-      sync_rows();  // every row is done with the previous item's (lse, delta)
-      stage_rows(p, b, h, qi * kTile, tid, lse_s, delta_s);
-      sync_rows();
+      sync_softmax_n<256>();  // every row is done with the previous item's (lse, delta)
+      if (tid < kTile) stage_rows(p, b, h, qi * kTile, tid, lse_s, delta_s);
+      sync_softmax_n<256>();
       if (!ok) continue;
       if (!wait_bar_warp(st_full, it & 1, p.budget, abort_flag) ||
           (it >= 1 &&
@@ -721,9 +728,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       ptx::tc_fence_after();
       const bool diag = qi == kt;
-      uint32_t dsk[64];  // this row's dS^T, bf16 pairs, until dV has read P^T
+      uint32_t dsk[32];  // this half row's dS^T, bf16 pairs, until dV has read P^T
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int cq = 0; cq < 2; ++cq) {
+        const int c4 = 2 * half + cq;
         uint32_t sv32[32], dp32[32];
         ptx::tmem_ld_32x32b_x32(trow + c4 * 32, sv32);
         ptx::tmem_ld_32x32b_x32(trow + 128 + c4 * 32, dp32);
@@ -741,7 +749,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             dr[e] = pv * (__uint_as_float(dp32[2 * i + e]) - delta_s[c]);
           }
           pk[i] = pack_bf16x2(pr[0], pr[1]);
-          dsk[c4 * 16 + i] = pack_bf16x2(dr[0], dr[1]);
+          dsk[cq * 16 + i] = pack_bf16x2(dr[0], dr[1]);
         }
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc)
@@ -757,8 +765,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         continue;
       }
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc)
-        st_shared_v4(pd_base + swz_chunk(row, cc * 8), dsk[cc * 4], dsk[cc * 4 + 1],
+      for (int cc = 0; cc < 8; ++cc)
+        st_shared_v4(pd_base + swz_chunk(row, half * 64 + cc * 8), dsk[cc * 4], dsk[cc * 4 + 1],
                      dsk[cc * 4 + 2], dsk[cc * 4 + 3]);
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive(ds_ready);
@@ -777,7 +785,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       float* wk = p.dkv_ws + (static_cast<int64_t>(b) * p.S + key) * (p.H * kHd) + h0 * kHd;
       float* wv = wk + p.ws_half;
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = 2 * half; c4 < 2 * half + 2; ++c4) {
         uint32_t a[32], g[32];
         ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
         ptx::tmem_ld_32x32b_x32(trow + 384 + c4 * 32, g);
@@ -797,7 +805,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     } else {
       ptx::tc_fence_after();
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = 2 * half; c4 < 2 * half + 2; ++c4) {
         uint32_t a[32], g[32];
         ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
         ptx::tmem_ld_32x32b_x32(trow + 384 + c4 * 32, g);
@@ -813,7 +821,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     ptx::fence_proxy_async_smem();
-    sync_rows();
+    sync_softmax_n<256>();
     if (threadIdx.x == 64 && p.dkv_ws == nullptr && !is_aborted(abort_flag)) {
       ptx::tma_store_3d(&mdv, sq, kvh * kHd, kt * kTile, b);
       ptx::tma_store_3d(&mdv, sq + kBox, kvh * kHd + 64, kt * kTile, b);
@@ -867,7 +875,7 @@ constexpr int kDqBars = 11;
 constexpr int kDqSmem = 7 * kTileBytes + kDqBars * 8 + 16 + 1024;
 
 // dQ of one (b, h, 128-query tile).
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kDqThreads, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap mq,
                        const __grid_constant__ CUtensorMap mk,
                        const __grid_constant__ CUtensorMap mv,
@@ -887,8 +895,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* kv_full = bars + 1;   // 2
   uint64_t* kv_empty = bars + 3;  // 2
   uint64_t* sd_full = bars + 5;   // S and dP are in TMEM
-  uint64_t* sd_free = bars + 6;   // the rows have read them (128 arrivals)
-  uint64_t* ds_full = bars + 7;   // dS is in shared memory (128 arrivals)
+  uint64_t* sd_free = bars + 6;   // the rows have read them (512 arrivals)
+  uint64_t* ds_full = bars + 7;   // dS is in shared memory (512 arrivals)
   uint64_t* dq_done = bars + 8;   // dQ += dS K complete
   uint64_t* drain = bars + 9;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDqBars);
@@ -910,8 +918,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     ptx::prefetch_tmap(&mv);
     ptx::prefetch_tmap(&mdo);
     for (int i = 0; i < kDqBars; ++i) ptx::mbar_init(&bars[i], 1);
-    ptx::mbar_init(sd_free, 128);
-    ptx::mbar_init(ds_full, 128);
+    ptx::mbar_init(sd_free, 512);
+    ptx::mbar_init(ds_full, 512);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
@@ -992,9 +1000,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
-    // ---------------- elementwise rows (warps 2..5): one query per thread ----------------
+    // ---------------- elementwise rows (warps 2..17): four threads per query row ----------------
+    // Warps w, w + 4, w + 8, w + 12 share TMEM lane quarter w % 4 and take key
+    // columns [32 sub, 32 sub + 32). Each reads its S and dP columns and frees
+    // them at once (the next key tile's MMAs then overlap this one's dS).
     const int quarter = warp & 3;
+    const int sub = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    const int c0 = sub * 32;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t ds_base = ptx::smem_u32(sds);
     const int q = q0 + row;
@@ -1003,30 +1016,39 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float delta_r = q < p.S ? p.delta[ri] : 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!wait_bar_warp(sd_full, j & 1, p.budget, abort_flag) ||
-          (j >= 1 && !wait_bar_warp(dq_done, (j - 1) & 1, p.budget, abort_flag))) {
+      if (!wait_bar_warp(sd_full, j & 1, p.budget, abort_flag)) {
         ok = false;
         break;
       }
       ptx::tc_fence_after();
-      const bool diag = j == qi;
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t sv32[32], dp32[32];
-        ptx::tmem_ld_32x32b_x32(trow + c4 * 32, sv32);
-        ptx::tmem_ld_32x32b_x32(trow + 128 + c4 * 32, dp32);
-        ptx::tmem_ld_wait();
-        float ds[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float pv = ex2(__uint_as_float(sv32[i]) * p.scale_log2 - lse_r);
-          if (diag && c4 * 32 + i > row) pv = 0.f;  // key after query
-          ds[i] = pv * (__uint_as_float(dp32[i]) - delta_r);
-        }
-        store_row32(ds_base, row, c4 * 32, ds, 1.f);
-      }
+      uint32_t sv32[32], dp32[32];
+      ptx::tmem_ld_32x32b_x32(trow + c0, sv32);
+      ptx::tmem_ld_32x32b_x32(trow + 128 + c0, dp32);
+      ptx::tmem_ld_wait();
       ptx::tc_fence_before();
       ptx::mbar_arrive(sd_free);
+      const bool diag = j == qi;
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float d2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float pv = ex2(__uint_as_float(sv32[2 * i + e]) * p.scale_log2 - lse_r);
+          if (diag && c0 + 2 * i + e > row) pv = 0.f;  // key after query
+          d2[e] = pv * (__uint_as_float(dp32[2 * i + e]) - delta_r);
+        }
+        pk[i] = pack_bf16x2(d2[0], d2[1]);
+      }
+      // dS_j goes into the one dS tile once dQ += dS_{j-1} K_{j-1} has read it
+      if (j >= 1 && !wait_bar_warp(dq_done, (j - 1) & 1, p.budget, abort_flag)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        st_shared_v4(ds_base + swz_chunk(row, c0 + cc * 8), pk[cc * 4], pk[cc * 4 + 1],
+                     pk[cc * 4 + 2], pk[cc * 4 + 3]);
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive(ds_full);
     }
@@ -1036,20 +1058,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       record_err(p.err, kDevErrAttnTimeout, abort_flag);
     } else {
       ptx::tc_fence_after();
-      const uint32_t qbase = ptx::smem_u32(sq);
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t a[32];
-        ptx::tmem_ld_32x32b_x32(trow + 256 + c4 * 32, a);
-        ptx::tmem_ld_wait();
-        float af[32];
+      uint32_t a[32];
+      ptx::tmem_ld_32x32b_x32(trow + 256 + c0, a);
+      ptx::tmem_ld_wait();
+      float af[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) af[i] = __uint_as_float(a[i]);
-        store_row32(qbase, row, c4 * 32, af, p.scale);
-      }
+      for (int i = 0; i < 32; ++i) af[i] = __uint_as_float(a[i]);
+      store_row32(ptx::smem_u32(sq), row, c0, af, p.scale);
     }
     ptx::fence_proxy_async_smem();
-    sync_rows();
+    sync_softmax_n<512>();
     if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
       ptx::tma_store_3d(&mdq, sq, h * kHd, q0, b);
       ptx::tma_store_3d(&mdq, sq + kBox, h * kHd + 64, q0, b);
@@ -1247,7 +1265,7 @@ extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t 
       static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo,
       delta, static_cast<int>(B), static_cast<int>(S), static_cast<int>(H));
   LEMA_CUDA_TRY(cudaGetLastError());
-  attn_bwd_dkdv_kernel<<<static_cast<unsigned>(kv_ctas), kBwdThreads, kDkdvSmem, s>>>(
+  attn_bwd_dkdv_kernel<<<static_cast<unsigned>(kv_ctas), kDkdvThreads, kDkdvSmem, s>>>(
       mq, mk, mv, mdo, mdk, mdv, p);
   LEMA_CUDA_TRY(cudaGetLastError());
   if (p.dkv_ws != nullptr) {
@@ -1259,7 +1277,7 @@ extern "C" int lema_attn_bwd(const void* q, int64_t ldq, const void* k, int64_t 
         static_cast<__nv_bfloat16*>(dk), lddk, static_cast<__nv_bfloat16*>(dv), lddv);
     LEMA_CUDA_TRY(cudaGetLastError());
   }
-  attn_bwd_dq_kernel<<<static_cast<unsigned>(q_ctas), kBwdThreads, kDqSmem, s>>>(mq, mk, mv, mdo,
+  attn_bwd_dq_kernel<<<static_cast<unsigned>(q_ctas), kDqThreads, kDqSmem, s>>>(mq, mk, mv, mdo,
                                                                                 mdq, p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
