@@ -574,12 +574,13 @@ def run_train(args, world, rank, local) -> dict | None:
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
                                  weight_shard=shard, vram_slots=args.vram_slots,
-                                 ckpt_mode=CKPT_MODES[args.ckpt], attn_impl=args.attn)
+                                 ckpt_mode=CKPT_MODES[args.ckpt],
+                                 ckpt_hbm_budget=ckpt_budget_bytes(args), attn_impl=args.attn)
         workload = (f"mixtral_streamed_lora: {shape.layers} x [hidden 4096, 32 q / 8 kv heads "
                     "x 128, 8 experts x SwiGLU 14336, top-2 softmax routing], vocab 32000, LoRA "
                     "r16 a32 on q/v, W8A8 attention projections and grouped W8A8 experts "
                     f"streamed from pinned RAM ({tr.ws.seg_bytes / 1e9:.2f} GB per layer), "
-                    "activation checkpoints in HBM within a budget (offloaded past it)")
+                    "activation checkpoints offloaded to pinned host")
     elif long_ft:
         # bs 1 x seq 2048, 512-token chunked attention, activations offloaded, selective
         # full fine-tuning of q/k/v/o in the last 4 layers (fp32 AdamW states in host RAM)
@@ -588,22 +589,23 @@ def run_train(args, world, rank, local) -> dict | None:
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, targets=(), seed=0,
                                  resident_layers=args.resident_layers, attn_chunk=512,
                                  full_ft_layers=last4, ckpt_mode=CKPT_MODES[args.ckpt],
+                                 ckpt_hbm_budget=ckpt_budget_bytes(args),
                                  attn_impl=args.attn)
         workload = (f"llama7b_selective_ft_2048: {shape.layers} x [hidden 4096, 32x128 heads, "
                     "MLP 11008], vocab 32000, bs 1 x seq 2048, 512-token chunked causal "
                     "attention, W8A8 projections streamed from pinned RAM, activation "
-                    f"checkpoints in HBM within a budget, full fine-tuning of q/k/v/o in layers {list(last4)} "
+                    f"checkpoints offloaded to pinned host, full fine-tuning of q/k/v/o in layers {list(last4)} "
                     "(fp32 AdamW states in pinned host RAM, re-quantised each step)")
     else:
         batch, seq = 8, 512
         tr = StreamedLoraTrainer(shape, dev, batch=batch, seq=seq, lora_rank=16,
                                  lora_alpha=32.0, seed=0, resident_layers=args.resident_layers,
                                  weight_shard=shard, vram_slots=args.vram_slots,
-                                 ckpt_mode=CKPT_MODES[args.ckpt], attn_impl=args.attn)
+                                 ckpt_mode=CKPT_MODES[args.ckpt],
+                                 ckpt_hbm_budget=ckpt_budget_bytes(args), attn_impl=args.attn)
         workload = (f"llama7b_streamed_lora: {shape.layers} x [hidden 4096, 32x128 heads, MLP "
                     "11008], vocab 32000, LoRA r16 a32 on q/v, W8A8 projections streamed "
-                    "from pinned RAM, activation checkpoints in HBM within a budget "
-                    "(offloaded past it)")
+                    "from pinned RAM, activation checkpoints offloaded to pinned host")
     tokens_per_step = batch * seq
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     n_batches = 4
@@ -740,7 +742,8 @@ def run_train(args, world, rank, local) -> dict | None:
                    "vram_slots": args.vram_slots,
                    "dgrad": args.dgrad,
                    "attention": args.attn,
-                   "checkpoints": args.ckpt,
+                   "checkpoints": args.ckpt + ("" if args.ckpt_budget_gb is None
+                                               else f" {args.ckpt_budget_gb} GB"),
                    "weight_stream": ("sharded: 1/N of each segment per rank over PCIe, NCCL "
                                      "all-gather over NVLink" if shard else
                                      "own: every rank streams its own full segments"),
@@ -998,6 +1001,11 @@ def run_reference(args) -> dict | None:
 CKPT_MODES = {"budget": None, "host": 0, "host-kernel": 1, "device": 2}
 
 
+def ckpt_budget_bytes(args) -> int | None:
+    """HBM bytes for boundary activations under --ckpt budget (None: the trainer's default)."""
+    return None if args.ckpt_budget_gb is None else int(args.ckpt_budget_gb * 1e9)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1021,11 +1029,14 @@ def main():
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
                     help="block attention: torch SDPA (default) or this library's tcgen05 "
                          "kernels (opt-in, head_dim 128)")
-    ap.add_argument("--ckpt", choices=list(CKPT_MODES), default="budget",
-                    help="boundary activations: budget (default: kept in HBM while they fit a "
-                         "quarter of the free memory, the rest offloaded by the copy engine), "
-                         "host (all offloaded by the copy engine), host-kernel (all offloaded "
-                         "by the SM store kernel) or device (all kept in HBM)")
+    ap.add_argument("--ckpt", choices=list(CKPT_MODES), default="host",
+                    help="boundary activations: host (default: all offloaded to pinned host "
+                         "by the copy engine), host-kernel (all offloaded by the SM store "
+                         "kernel), budget (kept in HBM while they fit a quarter of the free "
+                         "memory, the rest offloaded) or device (all kept in HBM)")
+    ap.add_argument("--ckpt-budget-gb", type=float, default=None,
+                    help="with --ckpt budget: HBM bytes (GB) for boundary activations "
+                         "(default a quarter of the free memory); layers past it are offloaded")
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="keep this many blocks' int8 segments resident in HBM")
     ap.add_argument("--cpu-seq", type=int, default=128)

@@ -7,11 +7,12 @@
   from pinned RAM into one of two VRAM slots by the native manager's copy
   stream while block i-1 computes; the block's W8A8 projections are bound to
   views of the slot (no parameter copy, unlike src/lema/adapters/_llama.py:
-  95-100); the block's input is kept in VRAM as the reference keeps it
-  (:109-111) while the layers' inputs fit an HBM budget (by default a quarter
-  of the memory free when the trainer is built); past the budget the
-  remaining layers' inputs go to pinned host slots on a D2H stream
-  (``ckpt_mode`` 0 / 1 offload every layer, 2 keeps every layer in VRAM);
+  95-100); the block's input is saved to a pinned host slot on a D2H stream
+  (``ckpt_mode`` 0, the default; 1 saves through the SM store kernel). The
+  reference keeps it in VRAM (:109-111): ``ckpt_mode=2`` does that for every
+  layer, and ``ckpt_mode=None`` for as many layers as fit ``ckpt_hbm_budget``
+  bytes (by default a quarter of the memory free when the trainer is built),
+  offloading only the rest;
 * head + loss (reference :151-162): final RMSNorm, bf16 lm_head, shifted
   cross entropy, backward to the last hidden state;
 * backward in reverse (reference :125-173): the saved input is restored on the
@@ -92,7 +93,7 @@ class StreamedLoraTrainer:
     def __init__(self, shape: LlamaShape, device, batch: int, seq: int, lora_rank: int = 16,
                  lora_alpha: float = 32.0, targets: tuple[str, ...] = ("q_proj", "v_proj"),
                  lr: float = 1e-4, weight_decay: float = 0.01, seed: int = 0,
-                 ckpt_mode: int | None = None, ckpt_hbm_budget: int | None = None,
+                 ckpt_mode: int | None = 0, ckpt_hbm_budget: int | None = None,
                  resident_layers: int = 0, grad_accum: int = 1,
                  gradient_checkpointing: bool = False, attn_chunk: int = 0,
                  full_ft_layers: tuple[int, ...] = (),
@@ -322,6 +323,8 @@ class StreamedLoraTrainer:
                 self.ckpt.save(i, h)
                 h = blk(h, self.cos, self.sin)
                 self._release(i)
+        # the last block's input comes back while the head and the loss run
+        self.ckpt.restore_async(L - 1)
         # head + loss
         h = h.detach().requires_grad_(True)
         logits = self.head(h)
@@ -334,7 +337,6 @@ class StreamedLoraTrainer:
         grad = h.grad
         del logits, h
         # backward in reverse: restore, re-forward with grad, backward
-        self.ckpt.restore_async(L - 1)
         for k in range(1, ahead):
             if L - 1 - k >= 0:
                 self._ensure(L - 1 - k)
