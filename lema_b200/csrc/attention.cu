@@ -13,9 +13,9 @@
 // scaled scores; delta [B, H, S] fp32 holds rowsum(dO * O) for the backward.
 //
 // Forward (attn_fwd_kernel): one CTA per (b, h, 128-query tile), heaviest tiles
-// first. Warp 0 loads Q once and K / V tiles into two-slot rings (TMA, 128-byte
-// swizzle); warp 1 issues S = Q K^T (M = N = 128, K = 128) into one of two TMEM
-// score buffers and O += P V into a TMEM accumulator, with V read MN-major
+// first. Warp 0 loads Q once, K tiles into one slot and V tiles into a
+// three-slot ring (two producer threads; TMA, 128-byte swizzle); warp 1 issues
+// S = Q K^T (M = N = 128, K = 128) into one of two TMEM score buffers and O += P V into a TMEM accumulator, with V read MN-major
 // straight from its token-major tile; warps 2..5 own one query row per thread:
 // they read the row's scores from TMEM, mask the diagonal tile, keep a running
 // row max and sum (online softmax; O is rescaled in TMEM only when a row max
@@ -218,16 +218,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // K needs one slot (S_j is issued as soon as its K lands, and frees it at
+  // once); V needs three: V_j is free only when P_j V_j is done, which waits for
+  // the softmax of tile j, so its ring carries two tiles of slack.
   uint8_t* sq = smem;                     // Q tile; O staging at the end
-  uint8_t* sk = smem + kTileBytes;        // K ring, 2 slots
-  uint8_t* sv = smem + 3 * kTileBytes;    // V ring, 2 slots
+  uint8_t* sk = smem + kTileBytes;        // K, 1 slot
+  uint8_t* sv = smem + 2 * kTileBytes;    // V ring, 3 slots
   uint8_t* sp = smem + 5 * kTileBytes;    // P (bf16), 2 slots
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 3;
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 7;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;   // 3 slots
+  uint64_t* v_empty = bars + 6;  // 3 slots
   uint64_t* s_full = bars + 9;
   uint64_t* s_free = bars + 11;
   uint64_t* p_full = bars + 13;
@@ -271,39 +274,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   ptx::griddep_wait();
 
   if (warp == 0) {
+    // ---------------- TMA producers: lane 0 Q and K, lane 1 V ----------------
+    // Two threads, so that a V slot still held by a P V never delays the next K.
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      int k_issued = 0, v_issued = 0;
+      int k_issued = 0;
       bool ok = true;
       ptx::mbar_arrive_expect_tx(q_full, kTileBytes);
       ptx::tma_load_3d(sq, &mq, q_full, h * kHd, q0, b);
       ptx::tma_load_3d(sq + kBox, &mq, q_full, h * kHd + 64, q0, b);
       for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !wait_bar(&k_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
+        if (j >= 1 && !wait_bar(k_empty, (j - 1) & 1, p.budget, abort_flag)) {
           ok = false;
           break;
         }
-        ptx::mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-        ptx::tma_load_3d(sk + s * kTileBytes, &mk, &k_full[s], kvh * kHd, j * kTile, b);
-        ptx::tma_load_3d(sk + s * kTileBytes + kBox, &mk, &k_full[s], kvh * kHd + 64, j * kTile, b);
+        ptx::mbar_arrive_expect_tx(k_full, kTileBytes);
+        ptx::tma_load_3d(sk, &mk, k_full, kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sk + kBox, &mk, k_full, kvh * kHd + 64, j * kTile, b);
         ++k_issued;
-        if (j >= 2 && !wait_bar(&v_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
-          ok = false;
-          break;
-        }
-        ptx::mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-        ptx::tma_load_3d(sv + s * kTileBytes, &mv, &v_full[s], kvh * kHd, j * kTile, b);
-        ptx::tma_load_3d(sv + s * kTileBytes + kBox, &mv, &v_full[s], kvh * kHd + 64, j * kTile, b);
-        ++v_issued;
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
       // every issued load lands before this CTA's shared memory is released
       (void)ptx::mbar_wait(q_full, 0, p.budget);
-      for (int i = k_issued - 1; i >= 0 && i >= k_issued - 2; --i)
-        (void)ptx::mbar_wait(&k_full[i & 1], (i >> 1) & 1, p.budget);
-      for (int i = v_issued - 1; i >= 0 && i >= v_issued - 2; --i)
-        (void)ptx::mbar_wait(&v_full[i & 1], (i >> 1) & 1, p.budget);
+      if (k_issued > 0) (void)ptx::mbar_wait(k_full, (k_issued - 1) & 1, p.budget);
+    } else if (lane == 1) {
+      int v_issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int v = j % 3;
+        if (j >= 3 && !wait_bar(&v_empty[v], (j / 3 - 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(&v_full[v], kTileBytes);
+        ptx::tma_load_3d(sv + v * kTileBytes, &mv, &v_full[v], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sv + v * kTileBytes + kBox, &mv, &v_full[v], kvh * kHd + 64, j * kTile,
+                         b);
+        ++v_issued;
+      }
+      if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      for (int i = v_issued - 1; i >= 0 && i >= v_issued - 3; --i)
+        (void)ptx::mbar_wait(&v_full[i % 3], (i / 3) & 1, p.budget);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -313,29 +323,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (j < n_kv) {  // S_j = Q K_j^T
           const int s = j & 1;
-          if (!wait_bar(&k_full[s], (j >> 1) & 1, p.budget, abort_flag) ||
+          if (!wait_bar(k_full, j & 1, p.budget, abort_flag) ||
               (j >= 2 && !wait_bar(&s_free[s], ((j - 2) >> 1) & 1, p.budget, abort_flag))) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          mma_tile_kk(tmem + s * 128, ptx::smem_u32(sq), ptx::smem_u32(sk + s * kTileBytes), false);
+          mma_tile_kk(tmem + s * 128, ptx::smem_u32(sq), ptx::smem_u32(sk), false);
           issued = true;
           ptx::mma_commit(&s_full[s]);
-          ptx::mma_commit(&k_empty[s]);
+          ptx::mma_commit(k_empty);
         }
         if (j >= 1) {  // O += P_{j-1} V_{j-1}
-          const int jj = j - 1, s = jj & 1;
+          const int jj = j - 1, s = jj & 1, v = jj % 3;
           if (!wait_bar(&p_full[s], (jj >> 1) & 1, p.budget, abort_flag) ||
-              !wait_bar(&v_full[s], (jj >> 1) & 1, p.budget, abort_flag)) {
+              !wait_bar(&v_full[v], (jj / 3) & 1, p.budget, abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
           mma_tile_kmn(tmem + 256, ptx::smem_u32(sp + s * kTileBytes),
-                       ptx::smem_u32(sv + s * kTileBytes), jj > 0);
+                       ptx::smem_u32(sv + v * kTileBytes), jj > 0);
           ptx::mma_commit(&pv_done[s]);
-          ptx::mma_commit(&v_empty[s]);
+          ptx::mma_commit(&v_empty[v]);
         }
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
