@@ -15,27 +15,32 @@
 // Forward (attn_fwd_kernel): one CTA per (b, h, 128-query tile), heaviest tiles
 // first. Warp 0 loads Q once, K tiles into one slot and V tiles into a
 // three-slot ring (two producer threads; TMA, 128-byte swizzle); warp 1 issues
-// S = Q K^T (M = N = 128, K = 128) into one of two TMEM score buffers and O += P V into a TMEM accumulator, with V read MN-major
-// straight from its token-major tile; warps 2..5 own one query row per thread:
-// they read the row's scores from TMEM, mask the diagonal tile, keep a running
-// row max and sum (online softmax; O is rescaled in TMEM only when a row max
-// grows by more than 2^8, so P stays below 256), write P as bf16 into a
-// swizzled shared tile for the P V MMA, and finally normalise O, write it
-// through a TMA store and record the row's log-sum-exp.
+// S = Q K^T (M = N = 128, K = 128) into one of two TMEM score buffers and
+// O += P V into a TMEM accumulator, with V read MN-major straight from its
+// token-major tile; 16 row warps, four per TMEM lane quarter, each take 32 of a
+// query row's score columns: they mask the diagonal tile, keep the row's running
+// max and sum (online softmax, the four partial maxima exchanged through spare
+// TMEM columns; O is rescaled in TMEM only when a row max grows by more than
+// 2^8, so P stays below 256), write P as bf16 into a swizzled shared tile for
+// the P V MMA, and finally normalise O, write it through a TMA store and record
+// the row's log-sum-exp.
 //
-// Backward (two kernels, no atomics, deterministic):
+// Backward (three or four kernels, no atomics, deterministic): attn_delta_kernel
+// (rowsum(dO * O)), then
 //   attn_bwd_dkdv_kernel: one CTA per (b, kv head, 128-key tile), heaviest
-//     first; for every query head of the group and every causal query tile it
-//     forms S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse),
-//     dS^T = P^T (dP^T - delta), and accumulates dV += P^T dO and dK += dS^T Q
-//     (Q, dO read MN-major from the tiles the first two MMAs used K-major). When
+//     first; for every query head of the group and every causal query tile (Q / dO
+//     double-buffered) it forms S^T = K Q^T and dP^T = V dO^T in TMEM, P^T =
+//     exp2(S^T c - lse), dS^T = P^T (dP^T - delta), and accumulates dV += P^T dO
+//     and dK += dS^T Q (Q, dO read MN-major from the tiles the first two MMAs used
+//     K-major; P^T and dS^T share one shared tile in turn). When
 //     those CTAs would not fill the GPU (GQA, few sequences or heads), one CTA per
 //     query head instead writes its head's fp32 dK / dV share and
 //     attn_dkv_reduce_kernel sums a group's shares in head order into the bf16
 //     dK / dV of its kv head.
 //   attn_bwd_dq_kernel: one CTA per (b, h, 128-query tile); for every causal key
-//     tile it forms S = Q K^T and dP = dO V^T, dS = P (dP - delta), and
-//     accumulates dQ += dS K (K read MN-major).
+//     tile (K / V double-buffered) it forms S = Q K^T and dP = dO V^T, dS = P (dP
+//     - delta), and accumulates dQ += dS K (K read MN-major); its 16 row warps
+//     free the score TMEM as soon as they have read it.
 // dK, dQ carry the softmax scale; dK / dV of a kv head sum over its query heads.
 //
 // Every wait is bounded (clock64 budget) and also ends when another role of the
