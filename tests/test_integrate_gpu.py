@@ -2,7 +2,8 @@
 (lema_b200.integrate), against the same reference code on the CPU with the
 oracle's W8A8 linears.
 
-1. Llama: the reference's ``LemaModel(backend="cpp")`` on a 3-block model
+1. Llama and Mistral (GQA, 2 kv heads, sliding window longer than the
+   sequence): the reference's ``LemaModel(backend="cpp")`` on a 3-block model
    (LoRA r4 on q/v, bf16, eager attention) runs two ``LemaTrainer.train_step``s
    with AdamW on the GPU: weights stream through this library's manager, the
    seven projections of every block are W8A8 (quantised from the streamed
@@ -10,7 +11,8 @@ oracle's W8A8 linears.
    The same reference model on the CPU (``backend="python"``) with every
    projection computing the oracle's W8A8 linear runs the same two steps from
    the same LoRA parameters. The losses agree within two bf16 ulps (measured
-   on B200: identical, 6.5625 and 6.46875).
+   on B200: Llama 6.5625 / 6.46875 against 6.5625 / 6.4375 on the CPU, Mistral
+   6.53125 / 6.46875 against 6.5 / 6.4375: at most one ulp apart).
 2. GPT-2: the reference's GPT-2 adapter cannot run a training step under the
    transformers version installed here (its ``forward_layer`` takes ``[0]`` of
    the block's output, which transformers 5 returns as a tensor, not a
@@ -70,7 +72,13 @@ def _save(d: Path, sd: dict, cfg: dict) -> str:
 H, HEADS, INTER, LAYERS, VOCAB, SEQ, BATCH = 256, 4, 512, 3, 512, 64, 2
 
 
-def _llama_checkpoint(d: Path) -> str:
+KV_HEADS = {"llama": HEADS, "mistral": 2}
+
+
+def _decoder_checkpoint(d: Path, kind: str) -> str:
+    """A random HF Llama- or Mistral-layout checkpoint (the two adapters share
+    the parameter names; Mistral here with GQA and a sliding window)."""
+    kv = KV_HEADS[kind] * (H // HEADS)
     g = torch.Generator().manual_seed(71)
     sd = {"model.embed_tokens.weight": 0.5 * torch.randn(VOCAB, H, generator=g),
           "model.norm.weight": 1.0 + 0.1 * torch.randn(H, generator=g),
@@ -79,17 +87,20 @@ def _llama_checkpoint(d: Path) -> str:
         p = f"model.layers.{i}"
         sd[f"{p}.input_layernorm.weight"] = 1.0 + 0.1 * torch.randn(H, generator=g)
         sd[f"{p}.post_attention_layernorm.weight"] = 1.0 + 0.1 * torch.randn(H, generator=g)
-        for n, (o, k) in {"self_attn.q_proj": (H, H), "self_attn.k_proj": (H, H),
-                          "self_attn.v_proj": (H, H), "self_attn.o_proj": (H, H),
+        for n, (o, k) in {"self_attn.q_proj": (H, H), "self_attn.k_proj": (kv, H),
+                          "self_attn.v_proj": (kv, H), "self_attn.o_proj": (H, H),
                           "mlp.gate_proj": (INTER, H), "mlp.up_proj": (INTER, H),
                           "mlp.down_proj": (H, INTER)}.items():
             sd[f"{p}.{n}.weight"] = 0.06 * torch.randn(o, k, generator=g)
-    cfg = {"model_type": "llama", "architectures": ["LlamaForCausalLM"], "hidden_size": H,
-           "num_attention_heads": HEADS, "num_key_value_heads": HEADS,
+    cfg = {"model_type": kind,
+           "architectures": ["LlamaForCausalLM" if kind == "llama" else "MistralForCausalLM"],
+           "hidden_size": H, "num_attention_heads": HEADS, "num_key_value_heads": KV_HEADS[kind],
            "intermediate_size": INTER, "num_hidden_layers": LAYERS, "vocab_size": VOCAB,
            "rms_norm_eps": 1e-5, "rope_theta": 10000.0, "max_position_embeddings": 512,
            "tie_word_embeddings": False, "hidden_act": "silu", "torch_dtype": "bfloat16",
            "dtype": "bfloat16"}
+    if kind == "mistral":
+        cfg["sliding_window"] = 4096
     return _save(d, sd, cfg)
 
 
@@ -124,20 +135,22 @@ def _route_through_oracle(adapter, blocks):
     adapter.construct_layer_module = construct_layer_module
 
 
-def test_reference_llama_model_trains_through_backend_cpp(lema_ref, cuda_device, tmp_path):
+@pytest.mark.parametrize("kind", ["llama", "mistral"])
+def test_reference_decoder_model_trains_through_backend_cpp(lema_ref, cuda_device, tmp_path,
+                                                            kind):
     from lema_b200 import _native as N
     from lema_b200._csrc._lema_cpp import LemaMemoryManager
     from lema_b200.modules import W8A8Linear
     lema = lema_ref
-    path = _llama_checkpoint(tmp_path / "llama")
+    path = _decoder_checkpoint(tmp_path / kind, kind)
     ids = torch.randint(0, VOCAB, (BATCH, SEQ), generator=torch.Generator().manual_seed(5))
     targets = ("q_proj", "v_proj")
 
-    cpu = lema.LemaModel(_config(lema, path, "llama", "cpu", "python", targets))
+    cpu = lema.LemaModel(_config(lema, path, kind, "cpu", "python", targets))
     blocks = {m["id"] for m in cpu.adapter.get_layer_metadata() if m["type"] == "block"}
     _route_through_oracle(cpu.adapter, blocks)
     cpu.initialize_lora()
-    gpu = lema.LemaModel(_config(lema, path, "llama", "cuda", "cpp", targets))
+    gpu = lema.LemaModel(_config(lema, path, kind, "cuda", "cpp", targets))
     gpu.initialize_lora()
     assert sorted(gpu.lora_manager.params) == sorted(cpu.lora_manager.params)
     with torch.no_grad():
@@ -162,7 +175,7 @@ def test_reference_llama_model_trains_through_backend_cpp(lema_ref, cuda_device,
                     for sub in m.modules() if isinstance(sub, W8A8Linear)]
             assert pool, "no W8A8 projection in the adapter's module pool"
         trainer.close()
-    print(f"[integrate] losses cpu {losses['cpu']} gpu {losses['gpu']}")
+    print(f"[integrate] {kind} losses cpu {losses['cpu']} gpu {losses['gpu']}")
     assert N.kernel_launches > launches0
     for a, b in zip(losses["gpu"], losses["cpu"]):
         assert abs(a - b) <= 2 * bf16_ulp(b), (losses["gpu"], losses["cpu"])
