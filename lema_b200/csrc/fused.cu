@@ -300,8 +300,17 @@ __device__ __forceinline__ uint32_t silu_bf16x2(uint32_t gw) {
 
 constexpr int kSwThreads = 256;  // wide rows (I = 11008 / 14336): 256 threads per row
 
+// Resident 256-thread blocks per SM asked of the register allocator. VPT 6 (I = 11008)
+// fits in 48 registers, 5 blocks instead of the 4 that its unconstrained 55 allow; VPT 8
+// (I = 14336) keeps its 64 registers (4 blocks: its 16 uint4 of row data would spill
+// below that) but is scheduled differently under the hint. Measured at M = 4096 with
+// the L2 flushed: 55.3 -> 51 us at I = 11008, 68.5 -> 60 us at I = 14336. Omitting the
+// hint is not the same as 1: a 1 lets ptxas grow VPT 8 to 148 registers (1 block per
+// SM, 1.75x slower).
+constexpr int sw_min_blocks(int vpt) { return vpt <= 2 ? 8 : vpt <= 6 ? 5 : 4; }
+
 template <int VPT>
-__global__ void __launch_bounds__(kSwThreads) swiglu_quant_kernel(
+__global__ void __launch_bounds__(kSwThreads, sw_min_blocks(VPT)) swiglu_quant_kernel(
     const __nv_bfloat16* __restrict__ gu, int64_t ldgu, int inter, int8_t* __restrict__ q,
     int64_t ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ m_out, int64_t ldm) {
   __shared__ float red[kSwThreads / 32];
