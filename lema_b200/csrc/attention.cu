@@ -12,18 +12,19 @@
 // lse [B, H, S] fp32 holds each query row's log2-domain log-sum-exp of the
 // scaled scores; delta [B, H, S] fp32 holds rowsum(dO * O) for the backward.
 //
-// Forward (attn_fwd_kernel): one CTA per (b, h, 128-query tile), heaviest tiles
-// first. Warp 0 loads Q once, K tiles into one slot and V tiles into a
-// three-slot ring (two producer threads; TMA, 128-byte swizzle); warp 1 issues
-// S = Q K^T (M = N = 128, K = 128) into one of two TMEM score buffers and
-// O += P V into a TMEM accumulator, with V read MN-major straight from its
-// token-major tile; 16 row warps, four per TMEM lane quarter, each take 32 of a
-// query row's score columns: they mask the diagonal tile, keep the row's running
-// max and sum (online softmax, the four partial maxima exchanged through spare
-// TMEM columns; O is rescaled in TMEM only when a row max grows by more than
-// 2^8, so P stays below 256), write P as bf16 into a swizzled shared tile for
-// the P V MMA, and finally normalise O, write it through a TMA store and record
-// the row's log-sum-exp.
+// Forward (attn_fwd_kernel): one CTA per (b, h, pair of 128-query tiles A and B),
+// heaviest pairs first; the pair shares every K / V tile it loads. Warp 0 loads
+// Q of both tiles once and K / V tiles into two-slot rings (two producer
+// threads; TMA, 128-byte swizzle); warp 1 issues S = Q K^T (M = N = 128, K = 128)
+// into each tile's TMEM score block and O += P V into each tile's TMEM
+// accumulator, P read from TMEM as the A operand and V read MN-major straight
+// from its token-major tile, in the order P_A V, S_A(next), P_B V, S_B(next), so
+// that one tile's softmax runs while the tensor core works on the other's. Four
+// softmax warps per tile, one thread per query row: each masks the diagonal tile,
+// keeps its row's running max and sum (online softmax; O is rescaled in TMEM only
+// when the max grows by more than 2^8, so P stays below 256), writes P as bf16
+// over its own scores in TMEM, and finally normalises O into a TMA store and
+// records the row's log-sum-exp.
 //
 // Backward (three or four kernels, no atomics, deterministic): attn_delta_kernel
 // (rowsum(dO * O)), then
@@ -137,46 +138,6 @@ __device__ __forceinline__ void sync_softmax_n() {
   asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
 }
 
-// Named barrier over the 512 row threads of the forward (warps 2..17).
-__device__ __forceinline__ void sync_softmax() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
-
-// Named barrier over the four row warps of TMEM lane quarter q (ids 2..5).
-__device__ __forceinline__ void quarter_sync(int q) {
-  asm volatile("bar.sync %0, 128;" ::"r"(2 + q) : "memory");
-}
-
-// The four partials of this thread's row (one per warp of its lane quarter):
-// each thread stores its own into TMEM column col + sub of its lane, the
-// quarter's warps meet, and each reads the four back. Every row thread calls it
-// (the barrier needs all 128 of the quarter).
-__device__ __forceinline__ void quarter_exchange(uint32_t trow, uint32_t col, int sub, int quarter,
-                                                 float mine, uint32_t (&all)[4]) {
-  ptx::tmem_st_32x32b_x1(trow + col + static_cast<uint32_t>(sub), __float_as_uint(mine));
-  ptx::tmem_st_wait();
-  ptx::tc_fence_before();
-  quarter_sync(quarter);
-  ptx::tc_fence_after();
-  ptx::tmem_ld_32x32b_x4(trow + col, all);
-  ptx::tmem_ld_wait();
-}
-
-__device__ __forceinline__ float quarter_exchange_max(uint32_t trow, uint32_t col, int sub,
-                                                      int quarter, float mine) {
-  uint32_t a[4];
-  quarter_exchange(trow, col, sub, quarter, mine, a);
-  return fmaxf(fmaxf(__uint_as_float(a[0]), __uint_as_float(a[1])),
-               fmaxf(__uint_as_float(a[2]), __uint_as_float(a[3])));
-}
-
-// The row's sum, added in the same order by all four threads of the row.
-__device__ __forceinline__ float quarter_exchange_sum(uint32_t trow, uint32_t col, int sub,
-                                                      int quarter, float mine) {
-  uint32_t a[4];
-  quarter_exchange(trow, col, sub, quarter, mine, a);
-  return (__uint_as_float(a[0]) + __uint_as_float(a[1])) +
-         (__uint_as_float(a[2]) + __uint_as_float(a[3]));
-}
-
 // S or dP = A B^T over head_dim: A, B both [128 x 128] K-major tiles.
 __device__ __forceinline__ void mma_tile_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
                                             bool accumulate_first) {
@@ -211,10 +172,21 @@ __device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, lo
 }
 
 // ------------------------------------------------------------------ forward
-constexpr int kFwdThreads = 576;  // producer, MMA issuer, 16 row warps
-constexpr int kFwdBars = 18;
-constexpr int kFwdSmem = 7 * kTileBytes + kFwdBars * 8 + 16 + 1024;
-constexpr uint32_t kXchCol = 384;  // TMEM columns [384, 396): row-partial exchange
+constexpr int kFwdThreads = 320;  // producer warp, MMA warp, 2 x 4 softmax warps
+constexpr int kFwdBars = 16;
+constexpr int kFwdSmem = 6 * kTileBytes + kFwdBars * 8 + 16 + 1024;
+
+// O += P V over 128 keys: P [128 rows x 128 keys] bf16 in TMEM (64 columns from
+// p_tmem, two keys per column), V a token-major [128 keys x 128 dims] tile read
+// MN-major (N = dims).
+__device__ __forceinline__ void mma_tile_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr,
+                                            bool accumulate_first) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    ptx::mma_bf16_tmem_a(d_tmem, p_tmem + static_cast<uint32_t>(k * 8),
+                         ptx::desc_mnmajor_sw128(v_addr + k * 2048, kBox, 1024), kIdescKMn,
+                         (accumulate_first || k > 0) ? 1u : 0u);
+}
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
@@ -223,36 +195,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  // K needs one slot (S_j is issued as soon as its K lands, and frees it at
-  // once); V needs three: V_j is free only when P_j V_j is done, which waits for
-  // the softmax of tile j, so its ring carries two tiles of slack.
-  uint8_t* sq = smem;                     // Q tile; O staging at the end
-  uint8_t* sk = smem + kTileBytes;        // K, 1 slot
-  uint8_t* sv = smem + 2 * kTileBytes;    // V ring, 3 slots
-  uint8_t* sp = smem + 5 * kTileBytes;    // P (bf16), 2 slots
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
+  uint8_t* sq = smem;                   // Q of tiles A and B; O staging at the end
+  uint8_t* sk = smem + 2 * kTileBytes;  // K ring, 2 slots
+  uint8_t* sv = smem + 4 * kTileBytes;  // V ring, 2 slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;   // 3 slots
-  uint64_t* v_empty = bars + 6;  // 3 slots
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_free = bars + 11;
-  uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 15;
-  uint64_t* drain = bars + 17;
+  uint64_t* k_full = bars + 1;   // 2 slots
+  uint64_t* k_empty = bars + 3;  // 2 slots
+  uint64_t* v_full = bars + 5;   // 2 slots
+  uint64_t* v_empty = bars + 7;  // 2 slots
+  uint64_t* s_full = bars + 9;   // per query tile
+  uint64_t* p_full = bars + 11;  // per query tile
+  uint64_t* o_done = bars + 13;  // per query tile
+  uint64_t* drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kFwdBars);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int bh_count = p.B * p.H;
-  const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
+  const int pairs = (p.q_tiles + 1) / 2;
+  const int pair = pairs - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
   const int bh = static_cast<int>(blockIdx.x) % bh_count;
   const int b = bh / p.H, h = bh % p.H;
   const int kvh = h / (p.H / p.Hkv);
-  const int n_kv = qt + 1;
-  const int q0 = qt * kTile;
+  const int qa = 2 * pair;                // query tile A; B is qa + 1
+  const bool has_b = qa + 1 < p.q_tiles;  // an odd tile count leaves the last pair without B
+  const int n_a = qa + 1;                 // key tiles of A (causal)
+  const int n_kv = has_b ? qa + 2 : n_a;  // key tiles of the pair
 
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&mq);
@@ -260,16 +230,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     ptx::prefetch_tmap(&mv);
     ptx::prefetch_tmap(&mo);
     for (int i = 0; i < kFwdBars; ++i) ptx::mbar_init(&bars[i], 1);
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(&s_free[s], 512);  // every row thread arrives
-      ptx::mbar_init(&p_full[s], 512);
-    }
+    ptx::mbar_init(&p_full[0], 128);  // every row thread of the tile arrives
+    ptx::mbar_init(&p_full[1], 128);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, 512);  // S0 [0,128), S1 [128,256), O [256,384)
+    ptx::tmem_alloc(tmem_slot, 512);  // S/P of A [0,128), of B [128,256); O of A, B [256,512)
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
@@ -280,78 +248,123 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producers: lane 0 Q and K, lane 1 V ----------------
-    // Two threads, so that a V slot still held by a P V never delays the next K.
     if (lane == 0) {
       int k_issued = 0;
       bool ok = true;
-      ptx::mbar_arrive_expect_tx(q_full, kTileBytes);
-      ptx::tma_load_3d(sq, &mq, q_full, h * kHd, q0, b);
-      ptx::tma_load_3d(sq + kBox, &mq, q_full, h * kHd + 64, q0, b);
+      ptx::mbar_arrive_expect_tx(q_full, (has_b ? 2 : 1) * kTileBytes);
+      ptx::tma_load_3d(sq, &mq, q_full, h * kHd, qa * kTile, b);
+      ptx::tma_load_3d(sq + kBox, &mq, q_full, h * kHd + 64, qa * kTile, b);
+      if (has_b) {
+        ptx::tma_load_3d(sq + kTileBytes, &mq, q_full, h * kHd, (qa + 1) * kTile, b);
+        ptx::tma_load_3d(sq + kTileBytes + kBox, &mq, q_full, h * kHd + 64, (qa + 1) * kTile, b);
+      }
       for (int j = 0; j < n_kv; ++j) {
-        if (j >= 1 && !wait_bar(k_empty, (j - 1) & 1, p.budget, abort_flag)) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_bar(&k_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
           ok = false;
           break;
         }
-        ptx::mbar_arrive_expect_tx(k_full, kTileBytes);
-        ptx::tma_load_3d(sk, &mk, k_full, kvh * kHd, j * kTile, b);
-        ptx::tma_load_3d(sk + kBox, &mk, k_full, kvh * kHd + 64, j * kTile, b);
+        ptx::mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        ptx::tma_load_3d(sk + s * kTileBytes, &mk, &k_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sk + s * kTileBytes + kBox, &mk, &k_full[s], kvh * kHd + 64, j * kTile,
+                         b);
         ++k_issued;
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
       // every issued load lands before this CTA's shared memory is released
       (void)ptx::mbar_wait(q_full, 0, p.budget);
-      if (k_issued > 0) (void)ptx::mbar_wait(k_full, (k_issued - 1) & 1, p.budget);
+      for (int i = k_issued - 1; i >= 0 && i >= k_issued - 2; --i)
+        (void)ptx::mbar_wait(&k_full[i & 1], (i >> 1) & 1, p.budget);
     } else if (lane == 1) {
       int v_issued = 0;
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        const int v = j % 3;
-        if (j >= 3 && !wait_bar(&v_empty[v], (j / 3 - 1) & 1, p.budget, abort_flag)) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_bar(&v_empty[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
           ok = false;
           break;
         }
-        ptx::mbar_arrive_expect_tx(&v_full[v], kTileBytes);
-        ptx::tma_load_3d(sv + v * kTileBytes, &mv, &v_full[v], kvh * kHd, j * kTile, b);
-        ptx::tma_load_3d(sv + v * kTileBytes + kBox, &mv, &v_full[v], kvh * kHd + 64, j * kTile,
+        ptx::mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        ptx::tma_load_3d(sv + s * kTileBytes, &mv, &v_full[s], kvh * kHd, j * kTile, b);
+        ptx::tma_load_3d(sv + s * kTileBytes + kBox, &mv, &v_full[s], kvh * kHd + 64, j * kTile,
                          b);
         ++v_issued;
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
-      for (int i = v_issued - 1; i >= 0 && i >= v_issued - 3; --i)
-        (void)ptx::mbar_wait(&v_full[i % 3], (i / 3) & 1, p.budget);
+      for (int i = v_issued - 1; i >= 0 && i >= v_issued - 2; --i)
+        (void)ptx::mbar_wait(&v_full[i & 1], (i >> 1) & 1, p.budget);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      bool ok = wait_bar(q_full, 0, p.budget, abort_flag);
+      // Order: S_A(0), S_B(0), then for every key tile j: O_A += P_A(j) V_j, S_A(j+1),
+      // O_B += P_B(j) V_j, S_B(j+1). S_X(j+1) overwrites P_X(j) in TMEM after the
+      // P V MMA that reads it (MMAs of one thread run in issue order), and one
+      // tile's softmax runs while the tensor core works on the other tile.
+      bool ok = wait_bar(q_full, 0, p.budget, abort_flag) &&
+                wait_bar(&k_full[0], 0, p.budget, abort_flag);
       bool issued = false;
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {  // S_j = Q K_j^T
-          const int s = j & 1;
-          if (!wait_bar(k_full, j & 1, p.budget, abort_flag) ||
-              (j >= 2 && !wait_bar(&s_free[s], ((j - 2) >> 1) & 1, p.budget, abort_flag))) {
+      if (ok) {
+        ptx::tc_fence_after();
+        mma_tile_kk(tmem, ptx::smem_u32(sq), ptx::smem_u32(sk), false);
+        ptx::mma_commit(&s_full[0]);
+        if (has_b) {
+          mma_tile_kk(tmem + 128, ptx::smem_u32(sq + kTileBytes), ptx::smem_u32(sk), false);
+          ptx::mma_commit(&s_full[1]);
+        }
+        ptx::mma_commit(&k_empty[0]);
+        issued = true;
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1, nx = j + 1, ns = nx & 1;
+        const uint32_t v_addr = ptx::smem_u32(sv + s * kTileBytes);
+        const uint32_t k_addr = ptx::smem_u32(sk + ns * kTileBytes);
+        bool k_ready = false;
+        if (!wait_bar(&v_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (j < n_a) {
+          if (!wait_bar(&p_full[0], j & 1, p.budget, abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          mma_tile_kk(tmem + s * 128, ptx::smem_u32(sq), ptx::smem_u32(sk), false);
-          issued = true;
-          ptx::mma_commit(&s_full[s]);
-          ptx::mma_commit(k_empty);
+          mma_tile_pv(tmem + 256, tmem, v_addr, j > 0);
+          if (nx < n_a) {
+            if (!wait_bar(&k_full[ns], (nx >> 1) & 1, p.budget, abort_flag)) {
+              ok = false;
+              break;
+            }
+            k_ready = true;
+            ptx::tc_fence_after();
+            mma_tile_kk(tmem, ptx::smem_u32(sq), k_addr, false);
+            ptx::mma_commit(&s_full[0]);
+          } else {
+            ptx::mma_commit(&o_done[0]);
+          }
         }
-        if (j >= 1) {  // O += P_{j-1} V_{j-1}
-          const int jj = j - 1, s = jj & 1, v = jj % 3;
-          if (!wait_bar(&p_full[s], (jj >> 1) & 1, p.budget, abort_flag) ||
-              !wait_bar(&v_full[v], (jj / 3) & 1, p.budget, abort_flag)) {
+        if (has_b) {
+          if (!wait_bar(&p_full[1], j & 1, p.budget, abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          mma_tile_kmn(tmem + 256, ptx::smem_u32(sp + s * kTileBytes),
-                       ptx::smem_u32(sv + v * kTileBytes), jj > 0);
-          ptx::mma_commit(&pv_done[s]);
-          ptx::mma_commit(&v_empty[v]);
+          mma_tile_pv(tmem + 384, tmem + 128, v_addr, j > 0);
+          if (nx < n_kv) {
+            if (!k_ready && !wait_bar(&k_full[ns], (nx >> 1) & 1, p.budget, abort_flag)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            mma_tile_kk(tmem + 128, ptx::smem_u32(sq + kTileBytes), k_addr, false);
+            ptx::mma_commit(&s_full[1]);
+          } else {
+            ptx::mma_commit(&o_done[1]);
+          }
         }
+        ptx::mma_commit(&v_empty[s]);
+        if (nx < n_kv) ptx::mma_commit(&k_empty[ns]);
       }
       if (!ok) record_err(p.err, kDevErrAttnTimeout, abort_flag);
       if (issued) {  // all MMAs complete before TMEM is released
@@ -360,135 +373,127 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax rows (warps 2..17): four threads per query row ----------------
-    // Warps w, w + 4, w + 8, w + 12 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..)
-    // and take score / O columns [32 sub, 32 sub + 32), sub = (w - 2) / 4. The four
-    // partial row maxima (and, at the end, the four partial sums) meet in spare TMEM
-    // columns: each thread stores its partial into its lane's column
-    // kXchCol + 4 (j % 2) + sub, the quarter's four warps pass their own named
-    // barrier, and one load returns all four. A thread whose wait fails keeps
-    // passing the barriers with its work skipped, so no row warp is left waiting.
+    // ---------------- softmax: warps 2..5 tile A, 6..9 tile B, one thread per query row ----------------
+    // A thread holds its row's 128 scores, so the row max and sum never leave it.
+    // O is rescaled in TMEM only when the row max grows by more than 2^8 (P stays
+    // below 256); P (bf16) is written over the row's scores, where the P V MMA reads
+    // it. The thread's O row is quiescent then: S_X(j) completing implies that
+    // every earlier MMA of the issuer, P_X(j-1) V included, has completed.
+    const int tile = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int sub = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
-    const int c0 = sub * 32;
+    const int qx = qa + tile;
+    const int n_x = tile == 0 ? n_a : n_kv;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint64_t c2 = f2_splat(p.scale_log2);
-    float m_run = -INFINITY, l = 0.f;  // l: this thread's share of the row sum
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int s = j & 1;
-      uint32_t v[32];
-      float pmax = -INFINITY;
-      if (ok && wait_bar_warp(&s_full[s], (j >> 1) & 1, p.budget, abort_flag)) {
-        ptx::tc_fence_after();
-        ptx::tmem_ld_32x32b_x32(trow + s * 128 + c0, v);
-        ptx::tmem_ld_wait();
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(&s_free[s]);
-        if (j == qt) {  // diagonal tile: keys after the query are masked
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i > row) v[i] = 0xff800000u;  // -inf
-        }
-        float m0 = -INFINITY, m1 = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          m0 = fmaxf(m0, __uint_as_float(v[2 * i]));
-          m1 = fmaxf(m1, __uint_as_float(v[2 * i + 1]));
-        }
-        pmax = fmaxf(m0, m1);
-      } else {
-        ok = false;
-      }
-      const float smax = quarter_exchange_max(trow, kXchCol + 4 * s, sub, quarter, pmax);
-      if (!ok) continue;
-      const float tmax = smax * p.scale_log2;  // scale > 0: max commutes with it
-      const bool need = tmax > m_run + kRescaleLog2;
-      const float m_new = need ? tmax : m_run;
-      const float alpha = need ? ex2(m_run - m_new) : 1.f;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O *= alpha on this thread's 32 columns, once P_{j-1} V_{j-1} has landed
-        if (!wait_bar_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.budget, abort_flag)) {
+    const uint32_t s_col = static_cast<uint32_t>(tile * 128);
+    const uint32_t o_col = 256 + s_col;
+    if (tile == 0 || has_b) {
+      const uint64_t c2 = f2_splat(p.scale_log2);
+      float m_run = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_x; ++j) {
+        if (!wait_bar_warp(&s_full[tile], j & 1, p.budget, abort_flag)) {
           ok = false;
-          continue;
+          break;
         }
         ptx::tc_fence_after();
-        uint32_t o[32];
-        ptx::tmem_ld_32x32b_x32(trow + 256 + c0, o);
+        uint32_t v[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          ptx::tmem_ld_32x32b_x32(trow + s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
         ptx::tmem_ld_wait();
+        if (j == qx) {  // diagonal tile: keys after the query are masked
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-        ptx::tmem_st_32x32b_x32(trow + 256 + c0, o);
+          for (int i = 0; i < 128; ++i)
+            if (i > row) v[i] = 0xff800000u;  // -inf
+        }
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+        const float smax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        const float tmax = smax * p.scale_log2;  // scale > 0: max commutes with it
+        const bool need = tmax > m_run + kRescaleLog2;
+        const float m_new = need ? tmax : m_run;
+        const float alpha = need ? ex2(m_run - m_new) : 1.f;
+        l *= alpha;
+        m_run = m_new;
+        // P = 2^(s c - m), written over the scores in two halves of 64 keys: the
+        // scaling and the sum two columns per instruction
+        const uint64_t negm2 = f2_splat(-m_run);
+        uint64_t acc0 = f2_splat(0.f), acc1 = f2_splat(0.f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = half * 64 + 2 * i;
+            float ta, tb;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), c2, negm2),
+                      ta, tb);
+            const float ea = ex2(ta), eb = ex2(tb);
+            if (i & 1)
+              acc1 = f2_add(acc1, f2_pack(ea, eb));
+            else
+              acc0 = f2_add(acc0, f2_pack(ea, eb));
+            pk[i] = pack_bf16x2(ea, eb);
+          }
+          ptx::tmem_st_32x32b_x32(trow + s_col + half * 32, pk);
+        }
+        float s0, s1, s2, s3;
+        f2_unpack(acc0, s0, s1);
+        f2_unpack(acc1, s2, s3);
+        l += (s0 + s1) + (s2 + s3);
+        // O *= alpha on this thread's row, after the scores are no longer held
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld_32x32b_x32(trow + o_col + c * 32, o);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            ptx::tmem_st_32x32b_x32(trow + o_col + c * 32, o);
+          }
+        }
         ptx::tmem_st_wait();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&p_full[tile]);
       }
-      l *= alpha;
-      m_run = m_new;
-      // P = 2^(s c - m): the scaling and the sum two columns per instruction
-      const uint64_t negm2 = f2_splat(-m_run);
-      uint64_t acc = f2_splat(0.f);
-      uint32_t pk[16];
+      // ---------------- epilogue: O / l -> bf16 -> TMA store; lse ----------------
+      if (ok && !wait_bar_warp(&o_done[tile], 0, p.budget, abort_flag)) ok = false;
+      if (!ok) {
+        record_err(p.err, kDevErrAttnTimeout, abort_flag);
+      } else {
+        ptx::tc_fence_after();
+        const float inv_l = 1.f / l;
+        // Q_X is free: its last S MMA completed before the last P V of the tile
+        const uint32_t obase = ptx::smem_u32(sq + tile * kTileBytes);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          ptx::tmem_ld_32x32b_x32(trow + o_col + c * 32, o);
+          ptx::tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float ta, tb;
-        f2_unpack(f2_fma(f2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2,
-                         negm2),
-                  ta, tb);
-        const float ea = ex2(ta), eb = ex2(tb);
-        acc = f2_add(acc, f2_pack(ea, eb));
-        pk[i] = pack_bf16x2(ea, eb);
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t* e = &o[i * 8];
+            st_shared_v4(obase + swz_chunk(row, c * 32 + i * 8),
+                         pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
+                         pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
+                         pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
+                         pack_bf16x2(__uint_as_float(e[6]) * inv_l, __uint_as_float(e[7]) * inv_l));
+          }
+        }
+        const int q = qx * kTile + row;
+        if (q < p.S) p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l);
       }
-      float s_lo, s_hi;
-      f2_unpack(acc, s_lo, s_hi);
-      l += s_lo + s_hi;
-      // P_j goes to slot s once P_{j-2} V_{j-2} has read it
-      if (j >= 2 && !wait_bar_warp(&pv_done[s], ((j - 2) >> 1) & 1, p.budget, abort_flag)) {
-        ok = false;
-        continue;
-      }
-      const uint32_t pbase = ptx::smem_u32(sp + s * kTileBytes);
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        st_shared_v4(pbase + swz_chunk(row, c0 + cc * 8), pk[cc * 4], pk[cc * 4 + 1],
-                     pk[cc * 4 + 2], pk[cc * 4 + 3]);
       ptx::fence_proxy_async_smem();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&p_full[s]);
-    }
-    // ---------------- epilogue: O / l -> bf16 -> TMA store; lse ----------------
-    if (ok && !wait_bar_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.budget,
-                             abort_flag))
-      ok = false;
-    const float l_row = quarter_exchange_sum(trow, kXchCol + 8, sub, quarter, l);
-    if (!ok) {
-      record_err(p.err, kDevErrAttnTimeout, abort_flag);
-    } else {
-      ptx::tc_fence_after();
-      const float inv_l = 1.f / l_row;
-      const uint32_t obase = ptx::smem_u32(sq);
-      uint32_t o[32];
-      ptx::tmem_ld_32x32b_x32(trow + 256 + c0, o);
-      ptx::tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t* e = &o[i * 8];
-        st_shared_v4(obase + swz_chunk(row, c0 + i * 8),
-                     pack_bf16x2(__uint_as_float(e[0]) * inv_l, __uint_as_float(e[1]) * inv_l),
-                     pack_bf16x2(__uint_as_float(e[2]) * inv_l, __uint_as_float(e[3]) * inv_l),
-                     pack_bf16x2(__uint_as_float(e[4]) * inv_l, __uint_as_float(e[5]) * inv_l),
-                     pack_bf16x2(__uint_as_float(e[6]) * inv_l, __uint_as_float(e[7]) * inv_l));
+      asm volatile("bar.sync %0, 128;" ::"r"(1 + tile) : "memory");  // the tile's 4 warps
+      if (quarter == 2 && lane == 0 && !is_aborted(abort_flag)) {  // first warp of the tile
+        ptx::tma_store_3d(&mo, sq + tile * kTileBytes, h * kHd, qx * kTile, b);
+        ptx::tma_store_3d(&mo, sq + tile * kTileBytes + kBox, h * kHd + 64, qx * kTile, b);
+        ptx::bulk_commit_group();
+        ptx::bulk_wait_group_all();
       }
-      const int q = q0 + row;
-      if (sub == 0 && q < p.S)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.S + q] = m_run + log2f(l_row);
-    }
-    ptx::fence_proxy_async_smem();
-    sync_softmax();
-    if (threadIdx.x == 64 && !is_aborted(abort_flag)) {
-      ptx::tma_store_3d(&mo, sq, h * kHd, q0, b);
-      ptx::tma_store_3d(&mo, sq + kBox, h * kHd + 64, q0, b);
-      ptx::bulk_commit_group();
-      ptx::bulk_wait_group_all();
     }
   }
 
@@ -1208,7 +1213,7 @@ extern "C" int lema_attn_fwd(const void* q, int64_t ldq, const void* k, int64_t 
     return rc;
   static bool done[64] = {};
   if ((rc = set_smem(attn_fwd_kernel, kFwdSmem, done))) return rc;
-  const int64_t ctas = B * H * p.q_tiles;
+  const int64_t ctas = B * H * ((p.q_tiles + 1) / 2);
   if (ctas > 0x7fffffff) return set_error(LEMA_ERR_INVALID_ARGUMENT, "too many tiles");
   attn_fwd_kernel<<<static_cast<unsigned>(ctas), kFwdThreads, kFwdSmem,
                     static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
