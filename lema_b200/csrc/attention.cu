@@ -173,6 +173,7 @@ __device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, lo
 
 // ------------------------------------------------------------------ forward
 constexpr int kFwdThreads = 320;  // producer warp, MMA warp, 2 x 4 softmax warps
+constexpr bool kPolyExp = true;
 constexpr int kFwdBars = 16;
 constexpr int kFwdSmem = 6 * kTileBytes + kFwdBars * 8 + 16 + 1024;
 
@@ -417,27 +418,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float alpha = need ? ex2(m_run - m_new) : 1.f;
         l *= alpha;
         m_run = m_new;
-        // P = 2^(s c - m), written over the scores in two halves of 64 keys: the
+        // P = 2^(s c - m), written over the scores in quarters of 32 keys: the
         // scaling and the sum two columns per instruction
         const uint64_t negm2 = f2_splat(-m_run);
         uint64_t acc0 = f2_splat(0.f), acc1 = f2_splat(0.f);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+        for (int qtr = 0; qtr < 4; ++qtr) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = half * 64 + 2 * i;
-            float ta, tb;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), c2, negm2),
-                      ta, tb);
-            const float ea = ex2(ta), eb = ex2(tb);
+          for (int i = 0; i < 16; ++i) {
+            const int c = qtr * 32 + 2 * i;
+            const uint64_t x2 =
+                f2_fma(f2_pack(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), c2, negm2);
+            float ea, eb;
+            f2_unpack(x2, ea, eb);
+            ea = ex2(ea);
+            eb = ex2(eb);
             if (i & 1)
               acc1 = f2_add(acc1, f2_pack(ea, eb));
             else
               acc0 = f2_add(acc0, f2_pack(ea, eb));
             pk[i] = pack_bf16x2(ea, eb);
           }
-          ptx::tmem_st_32x32b_x32(trow + s_col + half * 32, pk);
+          ptx::tmem_st_32x32b_x16(trow + s_col + qtr * 16, pk);
         }
         float s0, s1, s2, s3;
         f2_unpack(acc0, s0, s1);
