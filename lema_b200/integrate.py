@@ -44,13 +44,17 @@ from .modules import W8A8Linear
 
 # Projections of each reference adapter's decoder layers that become W8A8
 # (src/lema/adapters/_llama.py:41-57, _mistral.py, _mixtral.py attention,
-# _gpt2.py:33-49). Mixtral's experts are fused 3-D parameters, not linears.
+# _gpt2.py:33-49, _lfm2.py:48-75: LFM2's attention q/k/v/out_proj, its short
+# convolution's in_proj/out_proj and the dense layers' w1/w2/w3). Mixtral's and
+# LFM2's experts are fused 3-D parameters and LFM2's depthwise convolution a
+# Conv1d, not linears: they stay in the model dtype.
 PROJECTIONS = {
     "LlamaAdapter": ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"),
     "MistralAdapter": ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj",
                        "down_proj"),
     "MixtralAdapter": ("q_proj", "k_proj", "v_proj", "o_proj"),
     "GPT2Adapter": ("c_attn", "c_proj", "c_fc"),
+    "Lfm2Adapter": ("q_proj", "k_proj", "v_proj", "out_proj", "in_proj", "w1", "w2", "w3"),
 }
 
 _saved: dict[str, object] = {}

@@ -1,7 +1,8 @@
 """CPU tests of lema_b200.integrate: the reference's backend="cpp" import
 resolves to this library's manager, enable()/disable() wrap and restore the
-reference's LemaModel, and a mapping entry of a W8A8 projection quantises the
-flat-buffer view it is given (transposed for GPT-2's Conv1D)."""
+reference's LemaModel, a mapping entry of a W8A8 projection quantises the
+flat-buffer view it is given (transposed for GPT-2's Conv1D), and the
+projections listed for LFM2 are linears the reference adapter streams."""
 import sys
 from pathlib import Path
 
@@ -75,3 +76,32 @@ def test_offload_eligibility_rules():
     x = torch.randn(2, 8)
     assert not off._eligible(x)  # CPU tensors stay where they are
     assert not off._eligible(torch.zeros(2, 3, dtype=torch.int64))
+
+
+def test_lfm2_projections_are_streamed_linears(lema_ref):
+    """Every name listed for the reference's LFM2 adapter is an nn.Linear of its
+    convolution and attention blocks, and its weight is one of the parameters
+    the adapter streams for that layer (src/lema/adapters/_lfm2.py:48-75), so
+    the mapping has an entry to quantise."""
+    pytest.importorskip("transformers.models.lfm2_moe")
+    from transformers import Lfm2MoeConfig
+
+    from lema.adapters import get_adapter
+    cfg = Lfm2MoeConfig(vocab_size=64, hidden_size=32, intermediate_size=64,
+                        moe_intermediate_size=32, num_hidden_layers=2, num_attention_heads=4,
+                        num_key_value_heads=2, num_experts=4, num_experts_per_tok=2,
+                        layer_types=["conv", "full_attention"], num_dense_layers=2,
+                        max_position_embeddings=16)
+    adapter = get_adapter("lfm2_moe", cfg.to_dict())
+    names = integrate.PROJECTIONS[type(adapter).__name__]
+    seen = set()
+    for layer_id in (1, 2):
+        module = adapter.construct_layer_module(layer_id)
+        streamed = set(adapter.get_param_names_for_layer(layer_id))
+        prefix = f"model.layers.{layer_id - 1}."
+        for full, child in module.named_modules():
+            if full.rsplit(".", 1)[-1] in names:
+                assert isinstance(child, torch.nn.Linear), (full, type(child))
+                assert prefix + full + ".weight" in streamed, full
+                seen.add(full.rsplit(".", 1)[-1])
+    assert seen == set(names)

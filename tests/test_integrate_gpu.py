@@ -13,6 +13,16 @@ oracle's W8A8 linears.
    the same LoRA parameters. The losses agree within two bf16 ulps (measured
    on B200: Llama 6.5625 / 6.46875 against 6.5625 / 6.4375 on the CPU, Mistral
    6.53125 / 6.46875 against 6.5 / 6.4375: at most one ulp apart).
+   LFM2 (the reference's ``lfm2_moe`` adapter, dense feed-forward layers) runs
+   the same comparison twice: with attention blocks only (LoRA on q/v; W8A8
+   q/k/v/out_proj and w1/w2/w3) and with short-convolution blocks only (LoRA
+   on in_proj; W8A8 in_proj/out_proj and w1/w2/w3); measured on B200,
+   6.625 / 6.53125 against 6.65625 / 6.53125 (attention) and 6.78125 / 6.5625
+   against 6.78125 / 6.53125 (convolution). A model that mixes the two
+   block types does not train under the reference itself: its adapter's
+   module pool hands any pooled decoder layer to the next layer
+   (src/lema/adapters/_lfm2.py:88-101), so an attention layer can receive a
+   convolution layer's module and weight mapping (NaN losses on the CPU).
 2. GPT-2: the reference's GPT-2 adapter cannot run a training step under the
    transformers version installed here (its ``forward_layer`` takes ``[0]`` of
    the block's output, which transformers 5 returns as a tensor, not a
@@ -104,6 +114,41 @@ def _decoder_checkpoint(d: Path, kind: str) -> str:
     return _save(d, sd, cfg)
 
 
+def _lfm2_checkpoint(d: Path, layer_type: str) -> str:
+    """A random HF LFM2-MoE checkpoint whose blocks are all of one type
+    ("full_attention" or "conv") with dense feed-forward layers."""
+    from transformers import Lfm2MoeConfig
+    from transformers.models.lfm2_moe.modeling_lfm2_moe import Lfm2MoeForCausalLM
+    cfg = Lfm2MoeConfig(vocab_size=VOCAB, hidden_size=H, intermediate_size=INTER,
+                        moe_intermediate_size=128, num_hidden_layers=LAYERS,
+                        num_attention_heads=HEADS, num_key_value_heads=2, num_experts=4,
+                        num_experts_per_tok=2, layer_types=[layer_type] * LAYERS,
+                        num_dense_layers=LAYERS, max_position_embeddings=512,
+                        tie_word_embeddings=False)
+    g = torch.Generator().manual_seed(71)
+    sd = {}
+    for k, v in Lfm2MoeForCausalLM(cfg).state_dict().items():
+        if k.endswith("norm.weight"):
+            sd[k] = 1.0 + 0.1 * torch.randn(v.shape, generator=g)
+        elif k.endswith("conv.conv.weight"):
+            sd[k] = 0.3 * torch.randn(v.shape, generator=g)
+        elif "embed_tokens" in k:
+            sd[k] = 0.5 * torch.randn(v.shape, generator=g)
+        else:
+            sd[k] = 0.06 * torch.randn(v.shape, generator=g)
+    return _save(d, sd, {**cfg.to_dict(), "torch_dtype": "bfloat16", "dtype": "bfloat16"})
+
+
+# kind -> (model_type, checkpoint builder, LoRA targets)
+DECODERS = {
+    "llama": ("llama", lambda d: _decoder_checkpoint(d, "llama"), ("q_proj", "v_proj")),
+    "mistral": ("mistral", lambda d: _decoder_checkpoint(d, "mistral"), ("q_proj", "v_proj")),
+    "lfm2_attention": ("lfm2_moe", lambda d: _lfm2_checkpoint(d, "full_attention"),
+                       ("q_proj", "v_proj")),
+    "lfm2_conv": ("lfm2_moe", lambda d: _lfm2_checkpoint(d, "conv"), ("in_proj",)),
+}
+
+
 def _config(lema, path, model_type, device, backend, targets):
     return lema.LemaConfig(model_name_or_path=path, model_type=model_type,
                            gbi_path=os.path.join(path, "model.safetensors"), device=device,
@@ -118,7 +163,8 @@ def _route_through_oracle(adapter, blocks):
     computes the oracle's W8A8 linear of the weight it holds at call time."""
     from oracle.torch_ref import OracleW8A8Linear
     construct = adapter.construct_layer_module
-    names = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+    names = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj",
+             "out_proj", "in_proj", "w1", "w2", "w3")
 
     def construct_layer_module(layer_id, *a, **k):
         module = construct(layer_id, *a, **k)
@@ -135,22 +181,24 @@ def _route_through_oracle(adapter, blocks):
     adapter.construct_layer_module = construct_layer_module
 
 
-@pytest.mark.parametrize("kind", ["llama", "mistral"])
+@pytest.mark.parametrize("kind", list(DECODERS))
 def test_reference_decoder_model_trains_through_backend_cpp(lema_ref, cuda_device, tmp_path,
                                                             kind):
     from lema_b200 import _native as N
     from lema_b200._csrc._lema_cpp import LemaMemoryManager
     from lema_b200.modules import W8A8Linear
     lema = lema_ref
-    path = _decoder_checkpoint(tmp_path / kind, kind)
+    model_type, build, targets = DECODERS[kind]
+    if model_type == "lfm2_moe":
+        pytest.importorskip("transformers.models.lfm2_moe")
+    path = build(tmp_path / kind)
     ids = torch.randint(0, VOCAB, (BATCH, SEQ), generator=torch.Generator().manual_seed(5))
-    targets = ("q_proj", "v_proj")
 
-    cpu = lema.LemaModel(_config(lema, path, kind, "cpu", "python", targets))
+    cpu = lema.LemaModel(_config(lema, path, model_type, "cpu", "python", targets))
     blocks = {m["id"] for m in cpu.adapter.get_layer_metadata() if m["type"] == "block"}
     _route_through_oracle(cpu.adapter, blocks)
     cpu.initialize_lora()
-    gpu = lema.LemaModel(_config(lema, path, kind, "cuda", "cpp", targets))
+    gpu = lema.LemaModel(_config(lema, path, model_type, "cuda", "cpp", targets))
     gpu.initialize_lora()
     assert sorted(gpu.lora_manager.params) == sorted(cpu.lora_manager.params)
     with torch.no_grad():
