@@ -23,6 +23,10 @@ oracle's W8A8 linears.
    module pool hands any pooled decoder layer to the next layer
    (src/lema/adapters/_lfm2.py:88-101), so an attention layer can receive a
    convolution layer's module and weight mapping (NaN losses on the CPU).
+   Mixtral (4 experts, top-2, GQA): the attention's q/k/v/o are W8A8, the
+   fused experts stay bf16 on both sides; measured 6.59375 / 6.5 against
+   6.59375 / 6.46875. (The CPU side's own losses move by one ulp between runs:
+   its bf16 reductions are multithreaded.)
 2. GPT-2: the reference's GPT-2 adapter cannot run a training step under the
    transformers version installed here (its ``forward_layer`` takes ``[0]`` of
    the block's output, which transformers 5 returns as a tensor, not a
@@ -139,6 +143,27 @@ def _lfm2_checkpoint(d: Path, layer_type: str) -> str:
     return _save(d, sd, {**cfg.to_dict(), "torch_dtype": "bfloat16", "dtype": "bfloat16"})
 
 
+def _mixtral_checkpoint(d: Path) -> str:
+    """A random HF Mixtral checkpoint (4 experts, top-2; GQA with 2 kv heads)."""
+    from transformers import MixtralConfig
+    from transformers.models.mixtral.modeling_mixtral import MixtralForCausalLM
+    cfg = MixtralConfig(vocab_size=VOCAB, hidden_size=H, intermediate_size=INTER,
+                        num_hidden_layers=LAYERS, num_attention_heads=HEADS,
+                        num_key_value_heads=2, num_local_experts=4, num_experts_per_tok=2,
+                        max_position_embeddings=512, tie_word_embeddings=False,
+                        sliding_window=None)
+    g = torch.Generator().manual_seed(71)
+    sd = {}
+    for k, v in MixtralForCausalLM(cfg).state_dict().items():
+        if k.endswith("norm.weight"):
+            sd[k] = 1.0 + 0.1 * torch.randn(v.shape, generator=g)
+        elif "embed_tokens" in k:
+            sd[k] = 0.5 * torch.randn(v.shape, generator=g)
+        else:
+            sd[k] = 0.06 * torch.randn(v.shape, generator=g)
+    return _save(d, sd, {**cfg.to_dict(), "torch_dtype": "bfloat16", "dtype": "bfloat16"})
+
+
 # kind -> (model_type, checkpoint builder, LoRA targets)
 DECODERS = {
     "llama": ("llama", lambda d: _decoder_checkpoint(d, "llama"), ("q_proj", "v_proj")),
@@ -146,6 +171,7 @@ DECODERS = {
     "lfm2_attention": ("lfm2_moe", lambda d: _lfm2_checkpoint(d, "full_attention"),
                        ("q_proj", "v_proj")),
     "lfm2_conv": ("lfm2_moe", lambda d: _lfm2_checkpoint(d, "conv"), ("in_proj",)),
+    "mixtral": ("mixtral", _mixtral_checkpoint, ("q_proj", "v_proj")),
 }
 
 
