@@ -17,7 +17,10 @@ streams layer weights through ``_lema_cpp.LemaMemoryManager``
    buffer per output channel (K1, on the device) into the module's own int8
    weight and scales, where the reference copies bf16 values into an
    ``nn.Linear`` (src/lema/adapters/_llama.py:95-100). GPT-2's ``Conv1D``
-   weights, stored [in, out], are transposed at that point;
+   weights, stored [in, out], are transposed at that point. Fused MoE experts
+   (Mixtral, LFM2: 3-D ``gate_up_proj`` / ``down_proj``) become
+   ``W8A8Experts``, two grouped W8A8 GEMMs over the routed tokens, whose two
+   mapping entries re-quantise each streamed copy the same way;
 3. ``LemaTrainer.train_step`` keeps every streamed layer's input for the
    backward's recompute (src/lema/_trainer.py:109-111, 146-149). Those
    boundary activations now leave HBM: once a layer's no-grad forward is done,
@@ -38,16 +41,19 @@ import sys
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _native as N
 from .modules import W8A8Linear
+from .moe import W8A8Experts
 
 # Projections of each reference adapter's decoder layers that become W8A8
 # (src/lema/adapters/_llama.py:41-57, _mistral.py, _mixtral.py attention,
 # _gpt2.py:33-49, _lfm2.py:48-75: LFM2's attention q/k/v/out_proj, its short
 # convolution's in_proj/out_proj and the dense layers' w1/w2/w3). Mixtral's and
-# LFM2's experts are fused 3-D parameters and LFM2's depthwise convolution a
-# Conv1d, not linears: they stay in the model dtype.
+# LFM2's experts are fused 3-D parameters: a decoder layer's ``experts`` module
+# becomes W8A8Experts (grouped W8A8 GEMMs) instead. LFM2's depthwise
+# convolution is a Conv1d and stays in the model dtype.
 PROJECTIONS = {
     "LlamaAdapter": ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"),
     "MistralAdapter": ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj",
@@ -111,6 +117,21 @@ def disable() -> None:
 # W8A8 projections bound to the streamed flat buffer
 # ---------------------------------------------------------------------------
 
+class _ExpertsPart:
+    """One fused expert parameter (``gate_up_proj`` or ``down_proj``) of a
+    W8A8Experts module, as the target of a mapping entry."""
+
+    def __init__(self, experts, part: str):
+        self.experts = experts
+        self.part = part
+
+    def requantize_(self, w: torch.Tensor) -> None:
+        if self.part == "gate_up_proj":
+            self.experts.requantize_gate_up_(w)
+        else:
+            self.experts.requantize_down_(w)
+
+
 class _QuantizingSlot:
     """Takes a projection weight's place in the adapter's mapping
     (``(param, offset, numel, shape)`` entries): the adapter's
@@ -144,11 +165,46 @@ def _full_ft_names(full_ft) -> set[str]:
     return names
 
 
+def _is_fused_experts(m: nn.Module) -> bool:
+    """HF's fused-experts modules (MixtralExperts, Lfm2MoeExperts): 3-D
+    gate_up_proj [E, 2I, H] and down_proj [E, H, I], SiLU gating."""
+    gu, dn = getattr(m, "gate_up_proj", None), getattr(m, "down_proj", None)
+    act = getattr(m, "act_fn", None)
+    silu = act is F.silu or type(act).__name__ in ("SiLU", "SiLUActivation")
+    return (isinstance(gu, nn.Parameter) and isinstance(dn, nn.Parameter) and gu.dim() == 3
+            and dn.dim() == 3 and silu)
+
+
+def _convert_experts(mapping, index, parent: nn.Module, cname: str, child: nn.Module,
+                     full: str, keep: set[str]) -> None:
+    """Replaces fused bf16 experts by grouped W8A8 experts (lema_grouped_w8a8_gemm)
+    quantised from the weights just streamed; the two mapping entries then
+    re-quantise each new streamed copy."""
+    if f"{full}.gate_up_proj" in keep or f"{full}.down_proj" in keep:
+        return
+    entries = []
+    for part in ("gate_up_proj", "down_proj"):
+        i = index.get(id(getattr(child, part)))
+        if i is None:
+            raise N.LemaError(N.LEMA_ERR_UNSUPPORTED,
+                              f"{full}.{part} is not in the adapter's weight mapping", "integrate")
+        entries.append((part, i))
+    experts = W8A8Experts.from_fused(child.gate_up_proj.detach(), child.down_proj.detach())
+    for part, i in entries:
+        _, off, numel, shape = mapping[i]
+        mapping[i] = (_QuantizingSlot(_ExpertsPart(experts, part), False), off, numel, shape)
+    setattr(parent, cname, experts)
+
+
 def _convert(adapter, module: nn.Module, names: tuple[str, ...], keep: set[str]) -> None:
     mapping = adapter.param_mappings[id(module)]
     index = {id(param): i for i, (param, _, _, _) in enumerate(mapping)}
     for prefix, parent in list(module.named_modules()):
         for cname, child in list(parent.named_children()):
+            if cname == "experts" and _is_fused_experts(child):
+                _convert_experts(mapping, index, parent, cname, child,
+                                 f"{prefix}.{cname}" if prefix else cname, keep)
+                continue
             if cname not in names:
                 continue
             wrapped = hasattr(child, "base_layer")

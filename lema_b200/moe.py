@@ -94,6 +94,8 @@ def route_sort(top_i: torch.Tensor, E: int):
     order = torch.argsort(flat, stable=True)
     counts = torch.bincount(flat, minlength=E)
     offsets = [0] + torch.cumsum(counts, 0).tolist()
+    if len(offsets) != E + 1:
+        raise ValueError(f"routing index out of range for {E} experts")
     return order, order // k, order % k, offsets
 
 
@@ -148,11 +150,15 @@ class _GroupedExpertsFn(torch.autograd.Function):
 
 class W8A8Experts(nn.Module):
     """Frozen experts: int8 gate_up [E, 2I, H] and down [E, H, I] with per-output-channel
-    fp32 scales; forward through the grouped W8A8 GEMMs."""
+    fp32 scales; forward through the grouped W8A8 GEMMs. ``forward(x2d, top_i, top_w)``
+    takes the arguments of HF's fused-experts modules (MixtralExperts, Lfm2MoeExperts:
+    hidden states [T, H], top-k indices and weights [T, k]) and combines like them."""
 
-    def __init__(self, shape: MixtralShape, device=None):
+    def __init__(self, shape: MixtralShape | None = None, device=None,
+                 dims: tuple[int, int, int] | None = None):
         super().__init__()
-        E, I, H = shape.experts, shape.intermediate, shape.hidden
+        E, I, H = dims if dims is not None else (shape.experts, shape.intermediate,
+                                                  shape.hidden)
         self.register_buffer("wq_gate_up", torch.zeros(E, 2 * I, H, dtype=torch.int8, device=device))
         self.register_buffer("sw_gate_up", torch.ones(E, 2 * I, dtype=torch.float32, device=device))
         self.register_buffer("wq_down", torch.zeros(E, H, I, dtype=torch.int8, device=device))
@@ -160,14 +166,31 @@ class W8A8Experts(nn.Module):
 
     @torch.no_grad()
     def load_float(self, gate_up: torch.Tensor, down: torch.Tensor) -> None:
+        self.requantize_gate_up_(gate_up)
+        self.requantize_down_(down)
+
+    @classmethod
+    def from_fused(cls, gate_up: torch.Tensor, down: torch.Tensor) -> "W8A8Experts":
+        """Quantises HF fused expert weights (gate_up [E, 2I, H], down [E, H, I],
+        on the device) per output channel."""
         E, I2, H = gate_up.shape
+        m = cls(device=gate_up.device, dims=(E, I2 // 2, H))
+        m.load_float(gate_up, down)
+        return m
+
+    @torch.no_grad()
+    def requantize_gate_up_(self, gate_up: torch.Tensor) -> None:
+        E, I2, H = self.wq_gate_up.shape
         q, s = ops.quantize_weight(gate_up.reshape(E * I2, H).to(self.wq_gate_up.device))
         self.wq_gate_up.copy_(q.reshape(E, I2, H))
         self.sw_gate_up.copy_(s.reshape(E, I2))
-        E, H2, I = down.shape
-        q, s = ops.quantize_weight(down.reshape(E * H2, I).to(self.wq_down.device))
-        self.wq_down.copy_(q.reshape(E, H2, I))
-        self.sw_down.copy_(s.reshape(E, H2))
+
+    @torch.no_grad()
+    def requantize_down_(self, down: torch.Tensor) -> None:
+        E, H, I = self.wq_down.shape
+        q, s = ops.quantize_weight(down.reshape(E * H, I).to(self.wq_down.device))
+        self.wq_down.copy_(q.reshape(E, H, I))
+        self.sw_down.copy_(s.reshape(E, H))
 
     def forward(self, x2d, top_i, top_w):
         return _GroupedExpertsFn.apply(x2d, top_w, top_i, self.wq_gate_up, self.sw_gate_up,
