@@ -105,3 +105,40 @@ def test_lfm2_projections_are_streamed_linears(lema_ref):
                 assert prefix + full + ".weight" in streamed, full
                 seen.add(full.rsplit(".", 1)[-1])
     assert seen == set(names)
+
+
+def test_fused_experts_are_recognised_and_their_parts_dispatched():
+    """HF's fused-experts modules (Mixtral, LFM2-MoE) are the ones the W8A8
+    conversion takes; a dense MLP is not; each streamed 3-D parameter's mapping
+    entry re-quantises its own half of the W8A8 experts."""
+    from transformers import MixtralConfig
+    from transformers.models.mixtral.modeling_mixtral import MixtralExperts, MixtralMLP
+    cfg = MixtralConfig(hidden_size=32, intermediate_size=64, num_local_experts=4,
+                        num_experts_per_tok=2, num_attention_heads=4, num_key_value_heads=2)
+    assert integrate._is_fused_experts(MixtralExperts(cfg))
+    assert not integrate._is_fused_experts(MixtralMLP(cfg))
+    try:
+        from transformers import Lfm2MoeConfig
+        from transformers.models.lfm2_moe.modeling_lfm2_moe import Lfm2MoeExperts
+        lcfg = Lfm2MoeConfig(hidden_size=32, moe_intermediate_size=16, num_experts=4)
+        assert integrate._is_fused_experts(Lfm2MoeExperts(lcfg))
+    except ImportError:
+        pass
+
+    class _Experts:
+        def __init__(self):
+            self.got = []
+
+        def requantize_gate_up_(self, w):
+            self.got.append(("gate_up", tuple(w.shape)))
+
+        def requantize_down_(self, w):
+            self.got.append(("down", tuple(w.shape)))
+
+    ex = _Experts()
+    flat = torch.zeros(4 * 8 * 4 + 4 * 4 * 4)
+    gu = integrate._QuantizingSlot(integrate._ExpertsPart(ex, "gate_up_proj"), False)
+    dn = integrate._QuantizingSlot(integrate._ExpertsPart(ex, "down_proj"), False)
+    gu.data.copy_(flat[:128].view(4, 8, 4))
+    dn.data.copy_(flat[128:].view(4, 4, 4))
+    assert ex.got == [("gate_up", (4, 8, 4)), ("down", (4, 4, 4))]
