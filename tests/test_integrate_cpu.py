@@ -111,12 +111,14 @@ def test_fused_experts_are_recognised_and_their_parts_dispatched():
     """HF's fused-experts modules (Mixtral, LFM2-MoE) are the ones the W8A8
     conversion takes; a dense MLP is not; each streamed 3-D parameter's mapping
     entry re-quantises its own half of the W8A8 experts."""
-    from transformers import MixtralConfig
-    from transformers.models.mixtral.modeling_mixtral import MixtralExperts, MixtralMLP
+    from transformers import LlamaConfig, MixtralConfig
+    from transformers.models.llama.modeling_llama import LlamaMLP
+    from transformers.models.mixtral.modeling_mixtral import MixtralExperts
     cfg = MixtralConfig(hidden_size=32, intermediate_size=64, num_local_experts=4,
                         num_experts_per_tok=2, num_attention_heads=4, num_key_value_heads=2)
     assert integrate._is_fused_experts(MixtralExperts(cfg))
-    assert not integrate._is_fused_experts(MixtralMLP(cfg))
+    assert not integrate._is_fused_experts(
+        LlamaMLP(LlamaConfig(hidden_size=32, intermediate_size=64)))
     try:
         from transformers import Lfm2MoeConfig
         from transformers.models.lfm2_moe.modeling_lfm2_moe import Lfm2MoeExperts
