@@ -42,8 +42,9 @@ def _ref_fp32(q, k, v, B, S, H, Hkv):
     return o, lse2
 
 
+# (1, 640, 2, 1): five query tiles, so the forward's last pair of tiles has no second tile
 SHAPES = [(1, 128, 1, 1), (2, 256, 4, 2), (1, 200, 2, 2), (2, 512, 8, 2), (1, 2048, 4, 1),
-          (3, 77, 2, 1)]
+          (3, 77, 2, 1), (1, 640, 2, 1)]
 
 
 @pytest.mark.parametrize("B,S,H,Hkv", SHAPES)
@@ -65,7 +66,7 @@ def test_forward_matches_fp32_within_sdpa_error(cuda_device, B, S, H, Hkv):
 
 
 BWD_SHAPES = [(1, 128, 1, 1), (2, 256, 4, 2), (1, 200, 2, 2), (2, 512, 8, 2), (1, 2048, 4, 1),
-              (3, 77, 2, 1)]
+              (3, 77, 2, 1), (1, 640, 2, 1)]
 
 
 @pytest.mark.parametrize("B,S,H,Hkv", BWD_SHAPES)
