@@ -101,3 +101,18 @@ def test_grouped_path_equals_per_expert_loop_full_shape(cuda_device):
             o = ops.w8a8_linear(mid, ex.wq_down[e], ex.sw_down[e])
             ref.index_add_(0, tok, (o * top_w[tok, pos, None]).to(torch.bfloat16))
     assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_route_sort_groups_by_expert_and_rejects_out_of_range_indices():
+    """route_sort orders the (token, slot) assignments by expert (stable), gives
+    each sorted assignment's token and slot and the host offsets of the expert
+    groups, and refuses an index >= E (the grouped GEMM's offsets would not
+    cover those rows)."""
+    from lema_b200.moe import route_sort
+    top_i = torch.tensor([[2, 0], [1, 2], [0, 1]])
+    order, tok, slot, offsets = route_sort(top_i, 3)
+    assert offsets == [0, 2, 4, 6]
+    assert top_i.reshape(-1)[order].tolist() == [0, 0, 1, 1, 2, 2]
+    assert tok.tolist() == [0, 2, 1, 2, 0, 1] and slot.tolist() == [1, 0, 0, 1, 0, 1]
+    with pytest.raises(ValueError):
+        route_sort(torch.tensor([[0, 3]]), 3)
