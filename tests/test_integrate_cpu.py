@@ -144,3 +144,13 @@ def test_fused_experts_are_recognised_and_their_parts_dispatched():
     gu.data.copy_(flat[:128].view(4, 8, 4))
     dn.data.copy_(flat[128:].view(4, 4, 4))
     assert ex.got == [("gate_up", (4, 8, 4)), ("down", (4, 4, 4))]
+
+
+def test_every_reference_adapter_has_a_projection_list(lema_ref):
+    """Each adapter the reference registers (src/lema/adapters/__init__.py) has its
+    W8A8 projection list here, so ``backend="cpp"`` never meets an adapter it
+    cannot convert."""
+    from lema.adapters import _ADAPTER_REGISTRY
+    missing = [cls.__name__ for cls in _ADAPTER_REGISTRY.values()
+               if cls.__name__ not in integrate.PROJECTIONS]
+    assert not missing, missing
