@@ -13,7 +13,8 @@
 // scaled scores; delta [B, H, S] fp32 holds rowsum(dO * O) for the backward.
 //
 // Forward (attn_fwd_kernel): one CTA per (b, h, pair of 128-query tiles A and B),
-// heaviest pairs first; the pair shares every K / V tile it loads. Warp 0 loads
+// heaviest pairs first; the pair shares every K / V tile it loads (one tile per
+// CTA when the pairs would be fewer than the SMs). Warp 0 loads
 // Q of both tiles once and K / V tiles into two-slot rings (two producer
 // threads; TMA, 128-byte swizzle); warp 1 issues S = Q K^T (M = N = 128, K = 128)
 // into each tile's TMEM score block and O += P V into each tile's TMEM
@@ -81,6 +82,7 @@ struct AttnParams {
   float* dkv_ws;       // split GQA backward: fp32 dK / dV shares per query head, or null
   int64_t ws_half;     // floats in each half of dkv_ws (B * S * H * 128)
   int heads_per_cta;   // dK/dV kernel: the whole group (bf16 out) or 1 (shares into dkv_ws)
+  int fwd_tiles_per_cta;  // forward: 2 (pairs of query tiles) or 1 (grids below the SM count)
   int32_t* err;
   long long budget;
 };
@@ -215,13 +217,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int bh_count = p.B * p.H;
-  const int pairs = (p.q_tiles + 1) / 2;
-  const int pair = pairs - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
+  const int per = p.fwd_tiles_per_cta;  // 2, or 1 when pairs would leave SMs idle
+  const int groups = (p.q_tiles + per - 1) / per;
+  const int grp = groups - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
   const int bh = static_cast<int>(blockIdx.x) % bh_count;
   const int b = bh / p.H, h = bh % p.H;
   const int kvh = h / (p.H / p.Hkv);
-  const int qa = 2 * pair;                // query tile A; B is qa + 1
-  const bool has_b = qa + 1 < p.q_tiles;  // an odd tile count leaves the last pair without B
+  const int qa = per * grp;  // query tile A; B is qa + 1
+  // one tile per CTA, or an odd tile count's last pair: no tile B
+  const bool has_b = per == 2 && qa + 1 < p.q_tiles;
   const int n_a = qa + 1;                 // key tiles of A (causal)
   const int n_kv = has_b ? qa + 2 : n_a;  // key tiles of the pair
 
@@ -1172,6 +1176,7 @@ AttnParams make_params(int64_t B, int64_t S, int64_t H, int64_t Hkv, float scale
   p.q_tiles = static_cast<int>((S + kTile - 1) / kTile);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.fwd_tiles_per_cta = 2;
   p.err = gemm_error_word();
   p.budget = g_attn_budget.load();
   return p;
@@ -1216,7 +1221,12 @@ extern "C" int lema_attn_fwd(const void* q, int64_t ldq, const void* k, int64_t 
     return rc;
   static bool done[64] = {};
   if ((rc = set_smem(attn_fwd_kernel, kFwdSmem, done))) return rc;
-  const int64_t ctas = B * H * ((p.q_tiles + 1) / 2);
+  // pairs of query tiles share their K / V loads and overlap each other's softmax with
+  // the other's MMAs; below one CTA per SM, single tiles keep twice the SMs busy
+  if (B * H * ((p.q_tiles + 1) / 2) < static_cast<int64_t>(device_sm_count()))
+    p.fwd_tiles_per_cta = 1;
+  const int64_t ctas =
+      B * H * ((p.q_tiles + p.fwd_tiles_per_cta - 1) / p.fwd_tiles_per_cta);
   if (ctas > 0x7fffffff) return set_error(LEMA_ERR_INVALID_ARGUMENT, "too many tiles");
   attn_fwd_kernel<<<static_cast<unsigned>(ctas), kFwdThreads, kFwdSmem,
                     static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);

@@ -42,9 +42,12 @@ def _ref_fp32(q, k, v, B, S, H, Hkv):
     return o, lse2
 
 
-# (1, 640, 2, 1): five query tiles, so the forward's last pair of tiles has no second tile
+# The forward runs one query tile per CTA while B * H * (pairs of tiles) is below the SM
+# count (every shape up to (1, 640, 2, 1) here) and pairs of tiles above it:
+# (1, 2048, 20, 4) has 160 pairs, (1, 640, 64, 8) 192 pairs of five tiles, whose last
+# pair has no second tile.
 SHAPES = [(1, 128, 1, 1), (2, 256, 4, 2), (1, 200, 2, 2), (2, 512, 8, 2), (1, 2048, 4, 1),
-          (3, 77, 2, 1), (1, 640, 2, 1)]
+          (3, 77, 2, 1), (1, 640, 2, 1), (1, 2048, 20, 4), (1, 640, 64, 8)]
 
 
 @pytest.mark.parametrize("B,S,H,Hkv", SHAPES)
